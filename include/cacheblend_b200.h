@@ -1,0 +1,189 @@
+/*
+ * cacheblend_b200.h -- C ABI of the B200 (sm_100a) CacheBlend hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, int64
+ * sizes/strides (strides in BYTES unless stated otherwise) and a
+ * `cudaStream_t` passed as `void*`, and returns an int status:
+ *
+ *   CB_OK (0)              success (work is enqueued on `stream`)
+ *   CB_ERR_INVALID (-1)    invalid argument / shape / alignment
+ *   CB_ERR_UNSUPPORTED (-2) dtype or layout the kernels do not implement
+ *   CB_ERR_CUDA (-3)       a CUDA runtime/driver call failed
+ *
+ * `cb_last_error()` returns a thread-local message for the last failure on
+ * the calling thread.  The library allocates no device or host memory and
+ * keeps no global mutable state besides that per-thread string, so it is
+ * re-entrant and may be called from several host threads on several streams.
+ * Kernels run on the device that owns `stream`; for the legacy NULL stream,
+ * on the device that holds the call's output buffer.
+ *
+ * KV rows.  One token of one K (or V) plane is `num_heads` rows of
+ * `head_bytes` contiguous bytes; consecutive heads are `head_stride` bytes
+ * apart.  A paged plane addresses token slot s at
+ *     base + (s / block_size) * block_stride + (s % block_size) * slot_stride
+ * which covers vLLM's FlashAttention layout [2, blocks, block_size, H, D],
+ * FlashInfer's [blocks, 2, block_size, H, D], the HND stride orders and the
+ * separate (K, V) tuple layout.  A dense plane addresses token t at
+ *     base + plane * plane_stride + (t / chunk_tokens) * chunk_stride
+ *          + (t % chunk_tokens) * token_stride
+ * (chunk_tokens <= 0 disables chunking), which covers the contiguous
+ * [2, T, H, D] tensors of the reference and the chunk-major store staging.
+ */
+#ifndef CACHEBLEND_B200_H_
+#define CACHEBLEND_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CB_API __attribute__((visibility("default")))
+#else
+#define CB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CB_OK 0
+#define CB_ERR_INVALID (-1)
+#define CB_ERR_UNSUPPORTED (-2)
+#define CB_ERR_CUDA (-3)
+
+/* Element types of KV / query tensors. */
+#define CB_DTYPE_BF16 0
+#define CB_DTYPE_FP16 1
+#define CB_DTYPE_FP32 2
+
+/* ABI revision; bumped whenever a signature below changes. */
+CB_API int cb_abi_version(void);
+
+/* Thread-local description of the last failure ("" if none). */
+CB_API const char* cb_last_error(void);
+
+/*
+ * Paged gather: out[plane, t] = cache_plane[slots[t]] for plane in {K, V}.
+ * Replaces `gather_paged_kv(kv_layer, slot_mapping, block_size, out)`
+ * (cacheblend_vllm/kv_layout.py:90-122) and the Store-path gather into
+ * staging (cacheblend_vllm/connector.py:408-419).  Negative slots wrap once
+ * by num_blocks*block_size exactly like torch advanced indexing; any slot
+ * still out of range makes the kernel skip that row and is reported by the
+ * host wrapper's validation (kernels never touch memory out of range).
+ */
+CB_API int cb_paged_gather(const void* k_cache, const void* v_cache,
+                    int64_t block_stride, int64_t slot_stride, int64_t head_stride,
+                    int64_t num_blocks, int64_t block_size,
+                    int64_t num_heads, int64_t head_bytes,
+                    const int64_t* slots, int64_t num_tokens,
+                    void* out, int64_t out_plane_stride, int64_t out_token_stride,
+                    int64_t out_head_stride, int64_t out_chunk_tokens,
+                    int64_t out_chunk_stride, void* stream);
+
+/*
+ * Paged scatter: cache_plane[slots[t]] = src[plane, t].
+ * Replaces `scatter_paged_kv(contiguous, kv_layer, slot_mapping, block_size)`
+ * (cacheblend_vllm/kv_layout.py:125-161) and `PagedBlendLoader.commit`
+ * (cacheblend_vllm/ascend.py:385-407).  Duplicate slots: the last writer in
+ * token order is not guaranteed (as with torch index_put on CUDA).
+ */
+CB_API int cb_paged_scatter(const void* src, int64_t src_plane_stride, int64_t src_token_stride,
+                     int64_t src_head_stride, int64_t src_chunk_tokens,
+                     int64_t src_chunk_stride,
+                     void* k_cache, void* v_cache,
+                     int64_t block_stride, int64_t slot_stride, int64_t head_stride,
+                     int64_t num_blocks, int64_t block_size,
+                     int64_t num_heads, int64_t head_bytes,
+                     const int64_t* slots, int64_t num_tokens, void* stream);
+
+/*
+ * RoPE relocation of an already rotated key: out = R(new) R(old)^-1 key,
+ * evaluated op by op in the key dtype exactly like
+ * `relocate_key(rotary_emb, old_positions, new_positions, key)`
+ * (cacheblend_vllm/ascend.py:52-103, the cos_sin_cache branch).
+ * key/out: [num_tokens, num_heads, head_size] with row stride
+ * `token_stride` bytes and head stride `head_size` elements.  cos_sin:
+ * [max_position, rotary_dim] in the key dtype (cos half, then sin half).
+ * In-place (out == key) is allowed.
+ */
+CB_API int cb_relocate_key(const void* key, void* out, int64_t token_stride, int64_t out_token_stride,
+                    int64_t num_tokens, int64_t num_heads, int64_t head_size,
+                    int64_t rotary_dim, int is_neox, int dtype,
+                    const void* cos_sin, int64_t max_position,
+                    const int64_t* old_positions, const int64_t* new_positions,
+                    void* stream);
+
+/*
+ * One hit segment of a blend plan for one layer.  k_src / v_src are device
+ * addresses (device memory, or mapped pinned host memory for the zero-copy
+ * load) of the segment's first token; token t of the segment is at
+ * src + t * src_token_stride, heads `src_head_stride` apart.
+ */
+typedef struct cb_segment_t {
+  uint64_t k_src;
+  uint64_t v_src;
+  int64_t src_token_stride;
+  int64_t src_head_stride;
+  int32_t source_start; /* token position the chunk was cached at */
+  int32_t target_start; /* token position inside this request */
+  int32_t length;       /* tokens */
+  int32_t rotate;       /* nonzero: relocate K from source to target position */
+} cb_segment_t;
+
+/*
+ * Fused per-layer blend load into the staging buffer `out` ([2, alloc_end,
+ * H, D] dense plane description):
+ *   t <  apc_prefix            : gathered from the paged cache (slots[t])
+ *   token_segment[t] == -1     : zero (gap)
+ *   token_segment[t] == s >= 0 : segment s, K relocated when rotate != 0
+ * Replaces PagedBlendLoader.prefetch's body: the APC prefix gather, _zero_gaps,
+ * _load_segments_fused and _load_segments_individually
+ * (cacheblend_vllm/ascend.py:224-370).  token_segment is int32[alloc_end]
+ * (entries below apc_prefix are ignored); segments is cb_segment_t[num_segments]
+ * in device memory.  max_ctas > 0 caps the grid: a load that reads mapped
+ * host memory is PCIe-bound and needs only a few SMs' worth of loads in
+ * flight, leaving the rest of the GPU to the serving stream.
+ */
+CB_API int cb_blend_load_layer(void* out, int64_t out_plane_stride, int64_t out_token_stride,
+                        int64_t out_head_stride, int64_t alloc_end, int64_t apc_prefix,
+                        const void* k_cache, const void* v_cache,
+                        int64_t block_stride, int64_t slot_stride, int64_t head_stride,
+                        int64_t num_blocks, int64_t block_size, const int64_t* slots,
+                        int64_t num_heads, int64_t head_size, int dtype,
+                        const int32_t* token_segment, const cb_segment_t* segments,
+                        int64_t num_segments,
+                        const void* cos_sin, int64_t max_position, int64_t rotary_dim,
+                        int is_neox, int64_t max_ctas, void* stream);
+
+/*
+ * K-deviation score: scores[i] = sum_j (fresh[i, j] - cached[abs_i, j])^2 in
+ * fp32, abs_i = abs_index ? abs_index[i] : abs_offset + i; a row whose abs_i
+ * falls outside [0, cached_rows) scores NaN and is not read.  Replaces the
+ * inline expression of Qwen3BlendExecutor._compute_layer
+ * (cacheblend_vllm/ascend.py:535-538).  The reduction order is fixed (see
+ * the oracle): lane l of a warp accumulates 16-byte vectors l, l+32, ... with
+ * fmaf, then a xor-butterfly 16,8,4,2,1 combines the 32 partial sums.
+ * Strides are in bytes; width in elements.
+ */
+CB_API int cb_kv_deviation(const void* fresh, int64_t fresh_row_stride,
+                    const void* cached, int64_t cached_row_stride, int64_t cached_rows,
+                    const int64_t* abs_index, int64_t abs_offset,
+                    int64_t num_tokens, int64_t width, int dtype,
+                    float* scores, void* stream);
+
+/*
+ * Masked top-k selection (Qwen3BlendExecutor._select,
+ * cacheblend_vllm/ascend.py:757-796, after the TP all-reduce): writes the
+ * ascending indices of base_mask[i] != 0 united with the k largest scores
+ * among the remaining entries.  `k` must already follow the reference's
+ * budget formula (computed by the host: it depends only on mask counts).
+ * Exactly (#base + k) indices are written to out_index (never more than
+ * out_capacity).  Ties at the k-th value keep the lowest indices; NaN ranks
+ * above +inf (torch.topk order).  One CTA; no workspace.
+ */
+CB_API int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t n, int64_t k,
+                   int64_t* out_index, int64_t out_capacity, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CACHEBLEND_B200_H_ */

@@ -1,0 +1,194 @@
+"""Token scoring and recompute selection (K3; K4 host side).
+
+* ``kv_deviation`` -- ``cb_kv_deviation``: fp32 sum over the flattened local
+  heads of (k_fresh - k_cached)^2 per active token (ascend.py:535-538).
+* ``recompute_budget`` -- the top-k budget of ``_select`` (ascend.py:775-786):
+  ``k = int(cached * ratio)`` clamped to ``[1, available]`` when both counts
+  are non-zero, else 0; forced tokens do not consume budget.
+* ``select_tokens`` -- optional TP all-reduce of the scores (every rank then
+  runs the same deterministic kernel, so the reference's rank-0 broadcast is
+  unnecessary) and ``cb_select_topk``: ascending indices of base ∪ top-k.
+* ``sparse_q_masks`` -- query set, forced set and tail fallback of
+  ``_sparse_q_scores`` (ascend.py:652-673); these depend only on the plan's
+  gap mask, so they are computed on the host without a device round trip.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _native
+
+
+def _as_host_mask(mask: torch.Tensor | np.ndarray, name: str) -> np.ndarray:
+    if isinstance(mask, np.ndarray):
+        return mask.astype(np.bool_, copy=False)
+    if mask.dtype != torch.bool:
+        raise ValueError(f"{name} must be a boolean mask")
+    return mask.detach().to("cpu").numpy()
+
+
+def kv_deviation(
+    fresh_key: torch.Tensor,
+    cached_key: torch.Tensor,
+    absolute_indices: torch.Tensor | None = None,
+    absolute_offset: int = 0,
+    out: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> torch.Tensor:
+    """fp32 K-deviation score per row of ``fresh_key`` ([T, W] vs cached [N, W])."""
+    _native.require_cuda(fresh_key, cached_key)
+    fresh = fresh_key.reshape(fresh_key.shape[0], -1)
+    cached = cached_key.reshape(cached_key.shape[0], -1)
+    if fresh.shape[1] != cached.shape[1]:
+        raise ValueError("fresh and cached keys must have the same row width")
+    if fresh.dtype != cached.dtype:
+        raise ValueError("fresh and cached keys must have the same dtype")
+    if fresh.stride(1) != 1:
+        fresh = fresh.contiguous()
+    if cached.stride(1) != 1:
+        cached = cached.contiguous()
+    tokens = fresh.shape[0]
+    if out is None:
+        out = torch.empty(tokens, dtype=torch.float32, device=fresh.device)
+    index_ptr = 0
+    if absolute_indices is not None:
+        absolute_indices = absolute_indices.to(device=fresh.device, dtype=torch.long).contiguous()
+        if absolute_indices.numel() != tokens:
+            raise ValueError("one absolute index per fresh key row is required")
+        index_ptr = absolute_indices.data_ptr()
+    esize = fresh.element_size()
+    _native.call(
+        "cb_kv_deviation",
+        fresh.data_ptr(),
+        fresh.stride(0) * esize,
+        cached.data_ptr(),
+        cached.stride(0) * esize,
+        cached.shape[0],
+        index_ptr,
+        absolute_offset,
+        tokens,
+        fresh.shape[1],
+        _native.dtype_code(fresh.dtype),
+        out.data_ptr(),
+        _native.stream_handle(stream),
+    )
+    return out
+
+
+def recompute_budget(active: int, gap_count: int, base_count: int, ratio: float) -> int:
+    """Top-k size of ``_select`` (forced tokens are free, gaps never count)."""
+    cached = active - gap_count
+    available = active - base_count
+    if not cached or not available:
+        return 0
+    return min(max(int(cached * ratio), 1), available)
+
+
+def select_from_scores(
+    scores: torch.Tensor,
+    base_mask: torch.Tensor,
+    k: int,
+    selected_count: int,
+    stream: torch.cuda.Stream | None = None,
+) -> torch.Tensor:
+    """``cb_select_topk``: int64 ascending indices of base ∪ top-k (device)."""
+    _native.require_cuda(scores, base_mask)
+    if scores.dtype != torch.float32 or not scores.is_contiguous():
+        raise ValueError("scores must be a contiguous float32 vector")
+    if base_mask.dtype != torch.uint8 or base_mask.numel() != scores.numel():
+        raise ValueError("base mask must be a uint8 vector shaped like the scores")
+    out = torch.empty(selected_count, dtype=torch.long, device=scores.device)
+    if scores.numel() == 0:
+        return out
+    _native.call(
+        "cb_select_topk",
+        scores.data_ptr(),
+        base_mask.data_ptr(),
+        scores.numel(),
+        k,
+        out.data_ptr(),
+        out.numel(),
+        _native.stream_handle(stream),
+    )
+    return out
+
+
+def tp_all_reduce(scores: torch.Tensor, tp_group) -> torch.Tensor:
+    """Sum partial per-token scores over the TP ranks (NCCL over NVLink)."""
+    if hasattr(tp_group, "all_reduce") and hasattr(tp_group, "world_size"):
+        return tp_group.all_reduce(scores)  # vLLM GroupCoordinator
+    import torch.distributed as dist
+
+    dist.all_reduce(scores, group=tp_group)
+    return scores
+
+
+def tp_world_size(tp_group) -> int:
+    if tp_group is None:
+        return 1
+    if hasattr(tp_group, "world_size"):
+        return int(tp_group.world_size)
+    import torch.distributed as dist
+
+    return dist.get_world_size(tp_group)
+
+
+def select_tokens(
+    scores: torch.Tensor,
+    gap_mask: torch.Tensor | np.ndarray,
+    ratio: float,
+    forced_mask: torch.Tensor | np.ndarray | None = None,
+    tp_group=None,
+    global_selection: bool = True,
+    base_mask_device: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Full ``_select``: TP reduction, budget, masked top-k, ascending union."""
+    if global_selection and tp_world_size(tp_group) > 1:
+        scores = tp_all_reduce(scores, tp_group)
+    gaps = _as_host_mask(gap_mask, "gap_mask")
+    base = gaps.copy()
+    if forced_mask is not None:
+        forced = _as_host_mask(forced_mask, "forced_mask")
+        if forced.shape != gaps.shape:
+            raise ValueError("forced selection mask must match the active token shape")
+        base |= forced
+    active = scores.numel()
+    if gaps.shape[0] != active:
+        raise ValueError("gap mask must match the score vector")
+    base_count = int(base.sum())
+    k = recompute_budget(active, int(gaps.sum()), base_count, ratio)
+    if base_mask_device is None:
+        base_mask_device = torch.from_numpy(base.astype(np.uint8)).to(
+            scores.device, non_blocking=True
+        )
+    return select_from_scores(scores.contiguous(), base_mask_device, k, base_count + k)
+
+
+def sparse_q_masks(
+    gap_mask: np.ndarray, block_size: int, overflow_blocks: int, tail_query_tokens: int
+) -> tuple[np.ndarray, np.ndarray, bool]:
+    """(query mask, forced mask, tail_fallback) of the Sparse-Q selector.
+
+    Queries are the gap tokens; without gaps the last ``tail_query_tokens``
+    tokens act as queries and are forced.  With gaps, every token within
+    ``overflow_blocks * block_size`` of a gap is forced too.
+    """
+    gaps = gap_mask.astype(np.bool_, copy=False)
+    query = gaps.copy()
+    forced = gaps.copy()
+    has_gap = bool(gaps.any())
+    if not has_gap:
+        # same slice as ascend.py:659-660, including x[-0:] meaning "all"
+        tail = min(tail_query_tokens, gaps.shape[0])
+        query[-tail:] = True
+        forced[-tail:] = True
+    radius = overflow_blocks * block_size
+    if radius and has_gap:
+        counts = np.concatenate(([0], np.cumsum(gaps, dtype=np.int64)))
+        index = np.arange(gaps.shape[0])
+        left = np.clip(index - radius, 0, None)
+        right = np.clip(index + radius + 1, None, gaps.shape[0])
+        forced |= counts[right] > counts[left]
+    return query, forced, not has_gap

@@ -1,0 +1,486 @@
+// K2: fused per-layer blend load (APC prefix gather + gap zeroing + RoPE
+// relocation + placement) and the standalone relocate_key kernel.
+//
+// Reference semantics: PagedBlendLoader.prefetch / _zero_gaps /
+// _load_segments_fused / _load_segments_individually
+// (cacheblend_vllm/ascend.py:224-370) and relocate_key (ascend.py:52-103).
+// The staging row t of a layer is one of
+//   * t < apc_prefix      -> paged gather of slot[t]            (ascend.py:233-247)
+//   * gap                 -> zeros                              (ascend.py:280-287)
+//   * hit of segment s    -> K relocated from source to target  (ascend.py:357)
+//                            position, V copied; placed at t     (ascend.py:358-370)
+// all written by one launch: one warp per (token, plane) row, 16-byte vectors.
+// The hit source is any device-addressable memory: the device hit buffer
+// filled by copy-engine H2D, or mapped pinned host memory (zero-copy load).
+//
+// Relocation arithmetic is bit-exact with torch's per-op evaluation in the
+// key dtype: every product/sum is an fp32 op with round-to-nearest (explicit
+// __fmul_rn/__fadd_rn/__fsub_rn, never contracted to FMA) followed by
+// round-to-nearest-even back to the key dtype:
+//   dc = r(r(nc*oc) + r(ns*os))     ds = r(r(ns*oc) - r(nc*os))
+//   x1' = r(r(x1*dc) - r(x2*ds))    x2' = r(r(x2*dc) + r(x1*ds))
+#include "cb_common.cuh"
+
+namespace cb {
+namespace {
+
+template <typename T, int N>
+struct alignas(N * sizeof(T)) Pack {
+  T v[N];
+};
+
+// VM: vector memory access (the caller guarantees N*sizeof(T) alignment);
+// otherwise element by element, which only needs natural alignment.
+template <typename T, int N, bool VM>
+__device__ __forceinline__ Pack<T, N> load_pack(const T* p) {
+  Pack<T, N> r;
+  if constexpr (VM) {
+    using V = typename Vec<N * sizeof(T)>::T;
+    *reinterpret_cast<V*>(r.v) = *reinterpret_cast<const V*>(p);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.v[i] = p[i];
+  }
+  return r;
+}
+
+template <typename T, int N, bool VM>
+__device__ __forceinline__ void store_pack(T* p, const Pack<T, N>& x) {
+  if constexpr (VM) {
+    using V = typename Vec<N * sizeof(T)>::T;
+    *reinterpret_cast<V*>(p) = *reinterpret_cast<const V*>(x.v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = x.v[i];
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void delta_rotation(float nc, float ns, float oc, float os, float& dc,
+                                               float& ds) {
+  dc = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(nc, oc)), rnd<T>(__fmul_rn(ns, os))));
+  ds = rnd<T>(__fsub_rn(rnd<T>(__fmul_rn(ns, oc)), rnd<T>(__fmul_rn(nc, os))));
+}
+
+template <typename T>
+__device__ __forceinline__ void rotate_pair(float a, float b, float dc, float ds, T& oa, T& ob) {
+  oa = Elem<T>::from_f(__fsub_rn(rnd<T>(__fmul_rn(a, dc)), rnd<T>(__fmul_rn(b, ds))));
+  ob = Elem<T>::from_f(__fadd_rn(rnd<T>(__fmul_rn(b, dc)), rnd<T>(__fmul_rn(a, ds))));
+}
+
+struct RopeDesc {
+  const void* cos_sin;  // [max_position, rotary_dim], key dtype
+  int64_t max_position;
+  int rotary_dim;
+  int head_size;
+};
+
+// Relocates one token row (num_heads heads) with the whole warp.
+// E = elements per work item: 16 bytes on the vector path (VM), 1 (neox) or
+// 2 (one GPT-J pair) on the element-wise path.
+template <typename T, int E, bool NEOX, bool VM>
+__device__ void warp_relocate_row(const T* src, int64_t src_hs, T* dst, int64_t dst_hs,
+                                  int num_heads, const RopeDesc& rope, int64_t old_pos,
+                                  int64_t new_pos, int lane) {
+  const int R = rope.rotary_dim;
+  const int D = rope.head_size;
+  const int half = R / 2;
+  const T* cs = static_cast<const T*>(rope.cos_sin);
+  const T* old_cs = cs + old_pos * R;
+  const T* new_cs = cs + new_pos * R;
+  // rotary items per head: neox pairs (i, i+half) in groups of E; GPT-J
+  // interleaved pairs in vectors of E elements (E/2 pairs).
+  const int rot_items = NEOX ? half / E : R / E;
+  const int pass_items = (D - R) / E;
+  const int per_head = rot_items + pass_items;
+  const int items = num_heads * per_head;
+  for (int it = lane; it < items; it += 32) {
+    const int h = it / per_head;
+    const int c = it - h * per_head;
+    const T* s = src + h * src_hs;
+    T* d = dst + h * dst_hs;
+    if (c >= rot_items) {
+      const int off = R + (c - rot_items) * E;
+      store_pack<T, E, VM>(d + off, load_pack<T, E, VM>(s + off));
+      continue;
+    }
+    if constexpr (NEOX) {
+      const int i0 = c * E;
+      const Pack<T, E> a = load_pack<T, E, VM>(s + i0);
+      const Pack<T, E> b = load_pack<T, E, VM>(s + half + i0);
+      const Pack<T, E> oc = load_pack<T, E, VM>(old_cs + i0);
+      const Pack<T, E> os = load_pack<T, E, VM>(old_cs + half + i0);
+      const Pack<T, E> nc = load_pack<T, E, VM>(new_cs + i0);
+      const Pack<T, E> ns = load_pack<T, E, VM>(new_cs + half + i0);
+      Pack<T, E> ra, rb;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float dc, ds;
+        delta_rotation<T>(Elem<T>::to_f(nc.v[e]), Elem<T>::to_f(ns.v[e]), Elem<T>::to_f(oc.v[e]),
+                          Elem<T>::to_f(os.v[e]), dc, ds);
+        rotate_pair<T>(Elem<T>::to_f(a.v[e]), Elem<T>::to_f(b.v[e]), dc, ds, ra.v[e], rb.v[e]);
+      }
+      store_pack<T, E, VM>(d + i0, ra);
+      store_pack<T, E, VM>(d + half + i0, rb);
+    } else {
+      constexpr int P = E / 2;  // pairs per vector
+      const int i0 = c * E;     // element offset; pair index c*P
+      const Pack<T, E> x = load_pack<T, E, VM>(s + i0);
+      const Pack<T, P> oc = load_pack<T, P, VM>(old_cs + c * P);
+      const Pack<T, P> os = load_pack<T, P, VM>(old_cs + half + c * P);
+      const Pack<T, P> nc = load_pack<T, P, VM>(new_cs + c * P);
+      const Pack<T, P> ns = load_pack<T, P, VM>(new_cs + half + c * P);
+      Pack<T, E> r;
+#pragma unroll
+      for (int e = 0; e < P; ++e) {
+        float dc, ds;
+        delta_rotation<T>(Elem<T>::to_f(nc.v[e]), Elem<T>::to_f(ns.v[e]), Elem<T>::to_f(oc.v[e]),
+                          Elem<T>::to_f(os.v[e]), dc, ds);
+        rotate_pair<T>(Elem<T>::to_f(x.v[2 * e]), Elem<T>::to_f(x.v[2 * e + 1]), dc, ds,
+                       r.v[2 * e], r.v[2 * e + 1]);
+      }
+      store_pack<T, E, VM>(d + i0, r);
+    }
+  }
+}
+
+// Plain warp row copy / zero with VB-byte vectors (VB = E * sizeof(T)).
+template <int VB>
+__device__ __forceinline__ void warp_copy_heads(const char* src, int64_t src_hs, char* dst,
+                                                int64_t dst_hs, int num_heads, int units_per_head,
+                                                int lane) {
+  using V = typename Vec<VB>::T;
+  constexpr int U = 4;
+  const int units = num_heads * units_per_head;
+  for (int i0 = lane; i0 < units; i0 += 32 * U) {
+    V tmp[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * 32;
+      if (i < units) {
+        const int h = i / units_per_head;
+        const int j = i - h * units_per_head;
+        tmp[u] = ld_vec(reinterpret_cast<const V*>(src + h * src_hs + (int64_t)j * VB));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * 32;
+      if (i < units) {
+        const int h = i / units_per_head;
+        const int j = i - h * units_per_head;
+        *reinterpret_cast<V*>(dst + h * dst_hs + (int64_t)j * VB) = tmp[u];
+      }
+    }
+  }
+}
+
+template <int VB>
+__device__ __forceinline__ void warp_zero_heads(char* dst, int64_t dst_hs, int num_heads,
+                                                int units_per_head, int lane) {
+  using V = typename Vec<VB>::T;
+  const int units = num_heads * units_per_head;
+  V z;
+  memset(&z, 0, sizeof(V));
+  for (int i = lane; i < units; i += 32) {
+    const int h = i / units_per_head;
+    const int j = i - h * units_per_head;
+    *reinterpret_cast<V*>(dst + h * dst_hs + (int64_t)j * VB) = z;
+  }
+}
+
+struct LoadArgs {
+  char* out;
+  int64_t out_plane_stride;
+  int64_t out_token_stride;
+  int64_t out_head_stride;
+  int64_t alloc_end;
+  int64_t apc_prefix;
+  const char* k_cache;
+  const char* v_cache;
+  int64_t block_stride;
+  int64_t slot_stride;
+  int64_t head_stride;
+  int64_t num_slots;
+  uint32_t block_size;
+  const int64_t* slots;
+  int num_heads;
+  const int32_t* token_segment;
+  const cb_segment_t* segments;
+  int64_t num_segments;
+  RopeDesc rope;
+};
+
+template <typename T, int E, bool NEOX>
+__global__ void __launch_bounds__(256) blend_load_kernel(LoadArgs a) {
+  // 16-byte vectors on the vector path, single elements otherwise
+  constexpr bool VM = E * sizeof(T) == 16;
+  constexpr int VB = VM ? 16 : sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t tasks = 2 * a.alloc_end;
+  const int units = a.rope.head_size * static_cast<int>(sizeof(T)) / VB;
+  for (int64_t task = warp; task < tasks; task += nwarps) {
+    const int64_t t = task >> 1;
+    const int plane = static_cast<int>(task & 1);
+    char* dst = a.out + plane * a.out_plane_stride + t * a.out_token_stride;
+    if (t < a.apc_prefix) {
+      int64_t s = __ldg(a.slots + t);
+      if (s < 0) s += a.num_slots;
+      if (s < 0 || s >= a.num_slots) continue;
+      const uint32_t us = static_cast<uint32_t>(s);
+      const uint32_t blk = us / a.block_size;
+      const uint32_t off = us - blk * a.block_size;
+      const char* src = (plane ? a.v_cache : a.k_cache) + (int64_t)blk * a.block_stride +
+                        (int64_t)off * a.slot_stride;
+      warp_copy_heads<VB>(src, a.head_stride, dst, a.out_head_stride, a.num_heads, units, lane);
+      continue;
+    }
+    const int32_t seg_id = __ldg(a.token_segment + t);
+    if (seg_id < 0 || seg_id >= a.num_segments) {
+      warp_zero_heads<VB>(dst, a.out_head_stride, a.num_heads, units, lane);
+      continue;
+    }
+    const cb_segment_t seg = a.segments[seg_id];
+    const int64_t rel = t - seg.target_start;
+    const int64_t old_pos = seg.source_start + rel;
+    const bool rotate = plane == 0 && seg.rotate;
+    if (rel < 0 || rel >= seg.length ||
+        (rotate && (old_pos < 0 || old_pos >= a.rope.max_position || t >= a.rope.max_position))) {
+      // Inconsistent descriptor (rejected by host validation): never read
+      // outside the segment or the cos/sin table.
+      warp_zero_heads<VB>(dst, a.out_head_stride, a.num_heads, units, lane);
+      continue;
+    }
+    const char* src = reinterpret_cast<const char*>(plane ? seg.v_src : seg.k_src) +
+                      rel * seg.src_token_stride;
+    // Sources may be arbitrary device-addressable memory: take the scalar
+    // path for a row whose source is not aligned to the vector width.
+    const bool aligned = ((reinterpret_cast<uint64_t>(src) | (uint64_t)seg.src_head_stride) &
+                          (uint64_t)(VB - 1)) == 0;
+    if (((reinterpret_cast<uint64_t>(src) | (uint64_t)seg.src_head_stride) & (sizeof(T) - 1)) != 0) {
+      warp_zero_heads<VB>(dst, a.out_head_stride, a.num_heads, units, lane);  // not even
+      continue;                                                               // element-aligned
+    }
+    const int64_t src_hs = seg.src_head_stride / (int64_t)sizeof(T);
+    const int64_t dst_hs = a.out_head_stride / (int64_t)sizeof(T);
+    if (rotate) {
+      if (aligned)
+        warp_relocate_row<T, E, NEOX, VM>(reinterpret_cast<const T*>(src), src_hs,
+                                          reinterpret_cast<T*>(dst), dst_hs, a.num_heads, a.rope,
+                                          old_pos, t, lane);
+      else
+        warp_relocate_row<T, NEOX ? 1 : 2, NEOX, false>(reinterpret_cast<const T*>(src), src_hs,
+                                                        reinterpret_cast<T*>(dst), dst_hs,
+                                                        a.num_heads, a.rope, old_pos, t, lane);
+    } else if (aligned) {
+      warp_copy_heads<VB>(src, seg.src_head_stride, dst, a.out_head_stride, a.num_heads, units,
+                          lane);
+    } else {
+      warp_copy_heads<sizeof(T)>(src, seg.src_head_stride, dst, a.out_head_stride, a.num_heads,
+                                 a.rope.head_size, lane);
+    }
+  }
+}
+
+struct RelocArgs {
+  const char* key;
+  char* out;
+  int64_t token_stride;
+  int64_t out_token_stride;
+  int64_t num_tokens;
+  int num_heads;
+  const int64_t* old_pos;
+  const int64_t* new_pos;
+  RopeDesc rope;
+};
+
+template <typename T, int E, bool NEOX>
+__global__ void __launch_bounds__(256) relocate_kernel(RelocArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t t = warp; t < a.num_tokens; t += nwarps) {
+    const int64_t op = __ldg(a.old_pos + t);
+    const int64_t np = __ldg(a.new_pos + t);
+    if (op < 0 || op >= a.rope.max_position || np < 0 || np >= a.rope.max_position) continue;
+    warp_relocate_row<T, E, NEOX, E * sizeof(T) == 16>(reinterpret_cast<const T*>(a.key + t * a.token_stride),
+                                  a.rope.head_size,
+                                  reinterpret_cast<T*>(a.out + t * a.out_token_stride),
+                                  a.rope.head_size, a.num_heads, a.rope, op, np, lane);
+  }
+}
+
+inline int grid_for(int64_t warps) {
+  const int64_t blocks = (warps + 7) / 8;
+  return static_cast<int>(blocks < kSmCount * 8 ? blocks : kSmCount * 8);
+}
+
+// Chooses the 16-byte path when every address, stride and rotary split
+// allows it; otherwise the scalar path.
+bool use_vector_path(uint64_t addr_acc, int esize, int head_size, int rotary_dim, bool neox) {
+  const int E = 16 / esize;
+  if (vector_bytes(addr_acc) < 16) return false;
+  if ((head_size * esize) % 16) return false;
+  if ((rotary_dim * esize) % 16) return false;
+  if (neox ? ((rotary_dim / 2) % E) : (rotary_dim % E)) return false;
+  if ((head_size - rotary_dim) % E) return false;
+  return true;
+}
+
+template <typename T>
+int dispatch_load(const LoadArgs& a, bool vec, bool neox, int64_t max_ctas, cudaStream_t s) {
+  int grid = grid_for(2 * a.alloc_end);
+  if (max_ctas > 0 && grid > max_ctas) grid = static_cast<int>(max_ctas);
+  constexpr int EV = 16 / sizeof(T);
+  if (vec) {
+    if (neox)
+      blend_load_kernel<T, EV, true><<<grid, 256, 0, s>>>(a);
+    else
+      blend_load_kernel<T, EV, false><<<grid, 256, 0, s>>>(a);
+  } else {
+    if (neox)
+      blend_load_kernel<T, 1, true><<<grid, 256, 0, s>>>(a);
+    else
+      blend_load_kernel<T, 2, false><<<grid, 256, 0, s>>>(a);
+  }
+  return launch_status("cb_blend_load_layer");
+}
+
+template <typename T>
+int dispatch_reloc(const RelocArgs& a, bool vec, bool neox, cudaStream_t s) {
+  const int grid = grid_for(a.num_tokens);
+  constexpr int EV = 16 / sizeof(T);
+  if (vec) {
+    if (neox)
+      relocate_kernel<T, EV, true><<<grid, 256, 0, s>>>(a);
+    else
+      relocate_kernel<T, EV, false><<<grid, 256, 0, s>>>(a);
+  } else {
+    if (neox)
+      relocate_kernel<T, 1, true><<<grid, 256, 0, s>>>(a);
+    else
+      relocate_kernel<T, 2, false><<<grid, 256, 0, s>>>(a);
+  }
+  return launch_status("cb_relocate_key");
+}
+
+int check_rope(int64_t head_size, int64_t rotary_dim, int is_neox, int dtype) {
+  CB_REQUIRE(dtype_bytes(dtype) > 0, "unsupported dtype %d", dtype);
+  CB_REQUIRE(head_size > 0 && head_size < 65536, "head_size out of range");
+  CB_REQUIRE(rotary_dim > 0 && rotary_dim <= head_size && rotary_dim % 2 == 0,
+             "rotary_dim must be even and within head_size");
+  // The GPT-J scalar path moves (even, odd) element pairs.
+  CB_REQUIRE(is_neox || head_size % 2 == 0, "GPT-J style RoPE needs an even head_size");
+  return CB_OK;
+}
+
+}  // namespace
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" int cb_relocate_key(const void* key, void* out, int64_t token_stride,
+                               int64_t out_token_stride, int64_t num_tokens, int64_t num_heads,
+                               int64_t head_size, int64_t rotary_dim, int is_neox, int dtype,
+                               const void* cos_sin, int64_t max_position,
+                               const int64_t* old_positions, const int64_t* new_positions,
+                               void* stream) {
+  CB_BIND(stream, out);
+  int rc = check_rope(head_size, rotary_dim, is_neox, dtype);
+  if (rc != CB_OK) return rc;
+  CB_REQUIRE(num_tokens >= 0 && num_heads > 0, "bad token/head count");
+  if (num_tokens == 0) return CB_OK;
+  CB_REQUIRE(key && out && cos_sin && old_positions && new_positions, "null pointer argument");
+  CB_REQUIRE(max_position > 0, "empty cos_sin cache");
+  const int esize = dtype_bytes(dtype);
+  RelocArgs a{static_cast<const char*>(key),
+              static_cast<char*>(out),
+              token_stride,
+              out_token_stride,
+              num_tokens,
+              static_cast<int>(num_heads),
+              old_positions,
+              new_positions,
+              {cos_sin, max_position, static_cast<int>(rotary_dim), static_cast<int>(head_size)}};
+  const uint64_t acc = reinterpret_cast<uint64_t>(key) | reinterpret_cast<uint64_t>(out) |
+                       (uint64_t)token_stride | (uint64_t)out_token_stride |
+                       reinterpret_cast<uint64_t>(cos_sin);
+  const bool vec = use_vector_path(acc, esize, (int)head_size, (int)rotary_dim, is_neox != 0);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CB_DTYPE_BF16:
+      return dispatch_reloc<__nv_bfloat16>(a, vec, is_neox != 0, s);
+    case CB_DTYPE_FP16:
+      return dispatch_reloc<__half>(a, vec, is_neox != 0, s);
+    default:
+      return dispatch_reloc<float>(a, vec, is_neox != 0, s);
+  }
+}
+
+extern "C" int cb_blend_load_layer(void* out, int64_t out_plane_stride, int64_t out_token_stride,
+                                   int64_t out_head_stride, int64_t alloc_end, int64_t apc_prefix,
+                                   const void* k_cache, const void* v_cache, int64_t block_stride,
+                                   int64_t slot_stride, int64_t head_stride, int64_t num_blocks,
+                                   int64_t block_size, const int64_t* slots, int64_t num_heads,
+                                   int64_t head_size, int dtype, const int32_t* token_segment,
+                                   const cb_segment_t* segments, int64_t num_segments,
+                                   const void* cos_sin, int64_t max_position, int64_t rotary_dim,
+                                   int is_neox, int64_t max_ctas, void* stream) {
+  CB_BIND(stream, out);
+  int rc = check_rope(head_size, rotary_dim, is_neox, dtype);
+  if (rc != CB_OK) return rc;
+  CB_REQUIRE(alloc_end >= 0 && alloc_end < (int64_t(1) << 30), "alloc_end out of range");
+  CB_REQUIRE(apc_prefix >= 0 && apc_prefix <= alloc_end, "apc_prefix out of range");
+  CB_REQUIRE(num_heads > 0 && num_heads * head_size < (int64_t(1) << 24), "bad head count");
+  if (alloc_end == 0) return CB_OK;
+  CB_REQUIRE(out != nullptr, "null output");
+  if (apc_prefix > 0) {
+    CB_REQUIRE(k_cache && v_cache && slots, "APC prefix needs the paged cache and slots");
+    CB_REQUIRE(num_blocks > 0 && block_size > 0 && num_blocks * block_size < (int64_t(1) << 31),
+               "bad paged pool");
+  }
+  if (apc_prefix < alloc_end) CB_REQUIRE(token_segment != nullptr, "null token_segment");
+  CB_REQUIRE(num_segments == 0 || segments != nullptr, "null segments");
+  CB_REQUIRE(num_segments == 0 || cos_sin != nullptr, "segments need a cos_sin cache");
+  const int esize = dtype_bytes(dtype);
+  LoadArgs a{static_cast<char*>(out),
+             out_plane_stride,
+             out_token_stride,
+             out_head_stride,
+             alloc_end,
+             apc_prefix,
+             static_cast<const char*>(k_cache),
+             static_cast<const char*>(v_cache),
+             block_stride,
+             slot_stride,
+             head_stride,
+             num_blocks * block_size,
+             static_cast<uint32_t>(block_size > 0 ? block_size : 1),
+             slots,
+             static_cast<int>(num_heads),
+             token_segment,
+             segments,
+             num_segments,
+             {cos_sin, max_position, static_cast<int>(rotary_dim), static_cast<int>(head_size)}};
+  // Segment source addresses are validated for alignment by the host
+  // wrapper (it only builds 16-byte aligned descriptors on the vector path);
+  // here the staging and paged strides decide.
+  uint64_t acc = reinterpret_cast<uint64_t>(out) | (uint64_t)out_plane_stride |
+                 (uint64_t)out_token_stride | (uint64_t)out_head_stride |
+                 reinterpret_cast<uint64_t>(cos_sin);
+  if (apc_prefix > 0)
+    acc |= reinterpret_cast<uint64_t>(k_cache) | reinterpret_cast<uint64_t>(v_cache) |
+           (uint64_t)block_stride | (uint64_t)slot_stride | (uint64_t)head_stride;
+  const bool vec = use_vector_path(acc, esize, (int)head_size, (int)rotary_dim, is_neox != 0);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case CB_DTYPE_BF16:
+      return dispatch_load<__nv_bfloat16>(a, vec, is_neox != 0, max_ctas, s);
+    case CB_DTYPE_FP16:
+      return dispatch_load<__half>(a, vec, is_neox != 0, max_ctas, s);
+    default:
+      return dispatch_load<float>(a, vec, is_neox != 0, max_ctas, s);
+  }
+}

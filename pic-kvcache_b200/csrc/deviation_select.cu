@@ -1,0 +1,313 @@
+// K3: K-deviation scoring and masked radix top-k selection.
+//
+// kv_deviation (cacheblend_vllm/ascend.py:535-538):
+//   score[i] = sum_j (float(k_fresh[i, j]) - float(k_cached[abs_i, j]))^2
+// HBM-bound: 2 x width x esize bytes read and 4 bytes written per token.  One
+// warp per token; the reduction order is fixed so that the CPU oracle
+// reproduces the scores bit for bit: lane l owns units (16-byte vectors, or
+// single elements on the unaligned path) l, l+32, l+64, ... and accumulates
+// d = fresh - cached (fp32, RN) as acc = fmaf(d, d, acc) element by element;
+// then acc += shfl_xor(acc, o) for o = 16, 8, 4, 2, 1.
+//
+// select_topk (_select, cacheblend_vllm/ascend.py:757-796 after the
+// all-reduce): ascending indices of base ∪ top-k(non-base scores).  One CTA
+// of 1024 threads: four 8-bit radix passes over order-preserving keys find the
+// k-th largest key T and how many entries equal to T to keep (lowest indices
+// first); a two-pass ordered compaction writes the indices.  Scores are small
+// (<= 4 B x active tokens) and L2-resident, so the select is latency-bound.
+#include "cb_common.cuh"
+
+namespace cb {
+namespace {
+
+template <typename T, int UE>
+struct Unit;  // UE elements per unit
+template <typename T>
+struct Unit<T, 1> {
+  static __device__ __forceinline__ void acc(const char* f, const char* c, float& s) {
+    const float d = __fsub_rn(Elem<T>::to_f(*reinterpret_cast<const T*>(f)),
+                              Elem<T>::to_f(*reinterpret_cast<const T*>(c)));
+    s = __fmaf_rn(d, d, s);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void acc_vec16(const uint4& fv, const uint4& cv, float& s) {
+  constexpr int N = 16 / sizeof(T);
+  const T* f = reinterpret_cast<const T*>(&fv);
+  const T* c = reinterpret_cast<const T*>(&cv);
+#pragma unroll
+  for (int e = 0; e < N; ++e) {
+    const float d = __fsub_rn(Elem<T>::to_f(f[e]), Elem<T>::to_f(c[e]));
+    s = __fmaf_rn(d, d, s);
+  }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) deviation_kernel(const char* __restrict__ fresh,
+                                                        int64_t fresh_stride,
+                                                        const char* __restrict__ cached,
+                                                        int64_t cached_stride,
+                                                        int64_t cached_rows,
+                                                        const int64_t* __restrict__ abs_index,
+                                                        int64_t abs_offset, int64_t n, int width,
+                                                        float* __restrict__ scores) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t i = warp; i < n; i += nwarps) {
+    const int64_t ai = abs_index ? __ldg(abs_index + i) : abs_offset + i;
+    if (ai < 0 || ai >= cached_rows) {  // never read outside the cached rows
+      if (lane == 0) scores[i] = __int_as_float(0x7fc00000);
+      continue;
+    }
+    const char* f = fresh + i * fresh_stride;
+    const char* c = cached + ai * cached_stride;
+    float s = 0.0f;
+    if (VEC) {
+      const int units = width * static_cast<int>(sizeof(T)) / 16;
+      constexpr int U = 4;
+      for (int u0 = lane; u0 < units; u0 += 32 * U) {
+        uint4 fv[U], cv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int q = u0 + 32 * u;
+          if (q < units) {
+            fv[u] = ld_stream(reinterpret_cast<const uint4*>(f) + q);
+            cv[u] = ld_stream(reinterpret_cast<const uint4*>(c) + q);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (u0 + 32 * u < units) acc_vec16<T>(fv[u], cv[u], s);
+        }
+      }
+    } else {
+      for (int q = lane; q < width; q += 32)
+        Unit<T, 1>::acc(f + q * sizeof(T), c + q * sizeof(T), s);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    if (lane == 0) scores[i] = s;
+  }
+}
+
+// Order-preserving key: larger float -> larger key.  NaN (either sign) is
+// the largest, -0.0 equals +0.0.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  if (f != f) return 0xffffffffu;
+  if (f == 0.0f) f = 0.0f;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kSelThreads = 1024;
+
+// Block-wide exclusive scan of one int64 per thread (1024 threads).
+__device__ int64_t block_exclusive_scan(int64_t v, int64_t* warp_sums, int64_t& total) {
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  int64_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int64_t w = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_sums[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  const int64_t warp_prefix = wid ? warp_sums[wid - 1] : 0;
+  total = warp_sums[31];
+  __syncthreads();
+  return warp_prefix + x - v;
+}
+
+__global__ void __launch_bounds__(kSelThreads) select_topk_kernel(
+    const float* __restrict__ scores, const uint8_t* __restrict__ base, int64_t n, int64_t k,
+    int64_t* __restrict__ out, int64_t cap) {
+  __shared__ uint32_t hist[256];
+  __shared__ int64_t warp_sums[32];
+  __shared__ uint32_t s_digit;
+  __shared__ int64_t s_above;
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0, pmask = 0;
+  int64_t krem = k;
+  if (k > 0) {
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      if (tid < 256) hist[tid] = 0;
+      if (tid == 0) {
+        // k <= #candidates makes the search below always succeed; if a caller
+        // breaks that contract the threshold degrades to "keep every
+        // candidate", which still writes fewer than #base + k indices.
+        s_digit = 0;
+        s_above = 0;
+      }
+      __syncthreads();
+      for (int64_t i = tid; i < n; i += kSelThreads) {
+        if (base[i]) continue;
+        const uint32_t key = order_key(scores[i]);
+        if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid < 32) {
+        // lane L owns digits 255-8L .. 248-8L (descending)
+        uint32_t local[8];
+        uint32_t sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          local[j] = hist[255 - 8 * tid - j];
+          sum += local[j];
+        }
+        // exclusive prefix over lanes = count of digits above this lane's range
+        uint32_t incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (tid >= o) incl += y;
+        }
+        const uint32_t above = incl - sum;
+        if ((int64_t)above < krem && (int64_t)incl >= krem) {
+          uint32_t run = above;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if ((int64_t)(run + local[j]) >= krem) {
+              s_digit = 255 - 8 * tid - j;
+              s_above = run;
+              break;
+            }
+            run += local[j];
+          }
+        }
+      }
+      __syncthreads();
+      prefix |= s_digit << shift;
+      pmask |= 255u << shift;
+      krem -= s_above;
+      __syncthreads();
+    }
+  }
+  // prefix is the k-th largest key; keep every key > prefix and the first
+  // krem keys == prefix in index order.  k == 0 keeps base entries only.
+  const uint32_t thr = prefix;
+  const int64_t k_eq = k > 0 ? krem : 0;
+  const bool any = k > 0;
+  const int64_t per = (n + kSelThreads - 1) / kSelThreads;
+  const int64_t lo = per * tid < n ? per * tid : n;
+  const int64_t hi = lo + per < n ? lo + per : n;
+  int64_t c_sel = 0, c_eq = 0;
+  for (int64_t i = lo; i < hi; ++i) {
+    if (base[i]) {
+      ++c_sel;
+      continue;
+    }
+    if (!any) continue;
+    const uint32_t key = order_key(scores[i]);
+    if (key > thr)
+      ++c_sel;
+    else if (key == thr)
+      ++c_eq;
+  }
+  int64_t total;
+  int64_t sel_before = block_exclusive_scan(c_sel, warp_sums, total);
+  int64_t eq_before = block_exclusive_scan(c_eq, warp_sums, total);
+  for (int64_t i = lo; i < hi; ++i) {
+    bool take;
+    if (base[i]) {
+      take = true;
+    } else if (!any) {
+      take = false;
+    } else {
+      const uint32_t key = order_key(scores[i]);
+      if (key > thr) {
+        take = true;
+      } else if (key == thr) {
+        take = eq_before < k_eq;
+        ++eq_before;
+        if (take && sel_before + eq_before - 1 < cap) out[sel_before + eq_before - 1] = i;
+        continue;
+      } else {
+        take = false;
+      }
+    }
+    if (take) {
+      const int64_t pos = sel_before + (eq_before < k_eq ? eq_before : k_eq);
+      if (pos < cap) out[pos] = i;
+      ++sel_before;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" int cb_kv_deviation(const void* fresh, int64_t fresh_row_stride, const void* cached,
+                               int64_t cached_row_stride, int64_t cached_rows,
+                               const int64_t* abs_index,
+                               int64_t abs_offset, int64_t num_tokens, int64_t width, int dtype,
+                               float* scores, void* stream) {
+  CB_BIND(stream, scores);
+  const int esize = dtype_bytes(dtype);
+  CB_REQUIRE(esize > 0, "unsupported dtype %d", dtype);
+  CB_REQUIRE(num_tokens >= 0 && width > 0 && width < (int64_t(1) << 24), "bad shape");
+  if (num_tokens == 0) return CB_OK;
+  CB_REQUIRE(fresh && cached && scores, "null pointer argument");
+  CB_REQUIRE(cached_rows >= 0, "negative cached_rows");
+  const uint64_t acc = reinterpret_cast<uint64_t>(fresh) | reinterpret_cast<uint64_t>(cached) |
+                       (uint64_t)fresh_row_stride | (uint64_t)cached_row_stride |
+                       (uint64_t)(width * esize);
+  const bool vec = vector_bytes(acc) >= 16;
+  const int64_t blocks = (num_tokens + 7) / 8;
+  const int grid = static_cast<int>(blocks < kSmCount * 8 ? blocks : kSmCount * 8);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const char* f = static_cast<const char*>(fresh);
+  const char* c = static_cast<const char*>(cached);
+  const int w = static_cast<int>(width);
+#define CB_DEV_LAUNCH(T)                                                                      \
+  do {                                                                                        \
+    if (vec)                                                                                  \
+      deviation_kernel<T, true><<<grid, 256, 0, s>>>(f, fresh_row_stride, c,                  \
+                                                     cached_row_stride, cached_rows, abs_index,\
+                                                     abs_offset, num_tokens, w, scores);      \
+    else                                                                                      \
+      deviation_kernel<T, false><<<grid, 256, 0, s>>>(f, fresh_row_stride, c,                 \
+                                                      cached_row_stride, cached_rows,         \
+                                                      abs_index, abs_offset, num_tokens, w,   \
+                                                      scores);                                \
+  } while (0)
+  switch (dtype) {
+    case CB_DTYPE_BF16:
+      CB_DEV_LAUNCH(__nv_bfloat16);
+      break;
+    case CB_DTYPE_FP16:
+      CB_DEV_LAUNCH(__half);
+      break;
+    default:
+      CB_DEV_LAUNCH(float);
+      break;
+  }
+#undef CB_DEV_LAUNCH
+  return launch_status("cb_kv_deviation");
+}
+
+extern "C" int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t n, int64_t k,
+                              int64_t* out_index, int64_t out_capacity, void* stream) {
+  CB_BIND(stream, out_index);
+  CB_REQUIRE(n >= 0 && k >= 0 && k <= n && out_capacity >= 0, "bad n/k");
+  if (n == 0 || out_capacity == 0) return CB_OK;
+  CB_REQUIRE(scores && base_mask && out_index, "null pointer argument");
+  select_topk_kernel<<<1, kSelThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      scores, base_mask, n, k, out_index, out_capacity);
+  return launch_status("cb_select_topk");
+}
