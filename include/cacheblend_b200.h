@@ -140,7 +140,11 @@ typedef struct cb_segment_t {
  * (entries below apc_prefix are ignored); segments is cb_segment_t[num_segments]
  * in device memory.  max_ctas > 0 caps the grid: a load that reads mapped
  * host memory is PCIe-bound and needs only a few SMs' worth of loads in
- * flight, leaving the rest of the GPU to the serving stream.
+ * flight, leaving the rest of the GPU to the serving stream.  With
+ * max_ctas == 0 and 16-byte aligned rows the load is staged through shared
+ * memory by TMA bulk copies; its pipeline waits are bounded (2 s) and a wait
+ * that runs out stores a nonzero code into *device_error (nullable, device
+ * memory; 1 = producer, 2 = consumer) instead of hanging.
  */
 CB_API int cb_blend_load_layer(void* out, int64_t out_plane_stride, int64_t out_token_stride,
                         int64_t out_head_stride, int64_t alloc_end, int64_t apc_prefix,
@@ -151,7 +155,7 @@ CB_API int cb_blend_load_layer(void* out, int64_t out_plane_stride, int64_t out_
                         const int32_t* token_segment, const cb_segment_t* segments,
                         int64_t num_segments,
                         const void* cos_sin, int64_t max_position, int64_t rotary_dim,
-                        int is_neox, int64_t max_ctas, void* stream);
+                        int is_neox, int64_t max_ctas, int32_t* device_error, void* stream);
 
 /*
  * K-deviation score: scores[i] = sum_j (fresh[i, j] - cached[abs_i, j])^2 in

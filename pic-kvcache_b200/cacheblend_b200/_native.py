@@ -82,7 +82,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _i32,
         [_ptr, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr, _i64, _i64, _i64, _i64,
          _i64, _ptr, _i64, _i64, _i32, _ptr, _ptr, _i64, _ptr, _i64, _i64, _i32,
-         _i64, _ptr],
+         _i64, _ptr, _ptr],
     ),
     "cb_kv_deviation": (
         _i32,

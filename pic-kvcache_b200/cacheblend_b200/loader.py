@@ -59,6 +59,19 @@ def rope_head_stride(row: RowShape, rope_head_bytes: int) -> int:
     return row.head_stride
 
 
+_COPY_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _copy_stream(device: torch.device) -> torch.cuda.Stream:
+    """One host->device copy stream per device, shared by all loaders."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    stream = _COPY_STREAMS.get(index)
+    if stream is None:
+        stream = torch.cuda.Stream(device=index)
+        _COPY_STREAMS[index] = stream
+    return stream
+
+
 def byte_span(tensor: torch.Tensor, nbytes: int) -> torch.Tensor:
     """uint8 view of ``nbytes`` bytes of ``tensor``'s storage from its first element."""
     offset = tensor.storage_offset() * tensor.element_size()
@@ -95,9 +108,13 @@ class PagedBlendLoader:
         self._events: dict[int, torch.cuda.Event] = {}
         self._reuse_events: dict[int, torch.cuda.Event] = {}
         self._staging: list[torch.Tensor] = []
-        self._hit_buffer: torch.Tensor | None = None
-        self._copy_table: torch.Tensor | None = None
+        # copy mode: two device hit buffers (layer parity) so the H2D of layer
+        # l+1 on the copy stream overlaps the load kernel of layer l
+        self._hit_buffers: list[torch.Tensor | None] = [None, None]
+        self._copy_tables: list[torch.Tensor | None] = [None, None]
+        self._hit_free: dict[int, torch.cuda.Event] = {}
         self._slots: torch.Tensor | None = None
+        self._device_error: torch.Tensor | None = None
         self._token_segment: torch.Tensor | None = None
         self._host_refs: list[torch.Tensor] = []  # sources of in-flight host reads
         old, new = plan.hit_positions()
@@ -128,6 +145,7 @@ class PagedBlendLoader:
     # ------------------------------------------------------------------ setup
     def _setup(self, paged: PagedKV) -> None:
         if self._slots is None:
+            self._device_error = torch.zeros(1, dtype=torch.int32, device=paged.device)
             self._slots = device_slots(self.slot_mapping, paged, self.block_size)
             segment_map = torch.from_numpy(self.plan.token_segment_map())
             self._token_segment = segment_map.to(paged.device, non_blocking=True)
@@ -165,10 +183,12 @@ class PagedBlendLoader:
         for host, seg in zip(hosts, segments, strict=True):
             self._check_host(host, paged, seg.length)
         zero_copy = self.mode == "zerocopy" and all(host.is_pinned() for host in hosts)
+        parity = layer_id % 2
         if not zero_copy:
-            self._copy_hits(hosts, paged)
-            if self._copy_table is not None and kernel_rotates:
-                return self._copy_table, False
+            self._copy_hits(hosts, paged, parity)
+            cached = self._copy_tables[parity]
+            if cached is not None and kernel_rotates:
+                return cached, False
         table = self._base_table()
         if not kernel_rotates:
             table["rotate"] = 0
@@ -182,10 +202,11 @@ class PagedBlendLoader:
                 table["src_head_stride"][index] = rope_head_stride(dense_row(host), rope_head_bytes)
             self._host_refs.extend(hosts)
         else:
-            assert self._hit_buffer is not None
+            hit_buffer = self._hit_buffers[parity]
+            assert hit_buffer is not None
             offsets = np.cumsum([0] + [2 * seg.length * row_bytes for seg in segments[:-1]])
             lengths = np.array([seg.length for seg in segments], dtype=np.int64)
-            base = self._hit_buffer.data_ptr()
+            base = hit_buffer.data_ptr()
             table["k_src"] = (base + offsets).astype(np.uint64)
             table["v_src"] = (base + offsets + lengths * row_bytes).astype(np.uint64)
             table["src_token_stride"] = row_bytes
@@ -194,20 +215,25 @@ class PagedBlendLoader:
             paged.device, non_blocking=True
         )
         if not zero_copy and kernel_rotates:
-            self._copy_table = device_table  # identical for every layer
+            self._copy_tables[parity] = device_table  # identical for every layer of this parity
         return device_table, zero_copy
 
-    def _copy_hits(self, hosts: list[torch.Tensor], paged: PagedKV) -> None:
+    def _copy_hits(self, hosts: list[torch.Tensor], paged: PagedKV, parity: int) -> None:
         """Copy-engine H2D of every hit chunk into the packed device hit buffer.
 
         Per segment the buffer holds its K plane then its V plane.  Pieces that
         are adjacent in one pinned host allocation (chunk-major Store batches)
-        move as a single copy.
+        move as a single copy.  With an event pipeline the copies run on a
+        dedicated copy stream: they wait until the load kernel two layers back
+        has released this parity's buffer, and the load stream waits for them.
         """
         row_bytes = paged.row.row_bytes
         total = sum(2 * host.shape[1] * row_bytes for host in hosts)
-        if self._hit_buffer is None or self._hit_buffer.numel() < total:
-            self._hit_buffer = torch.empty(total, dtype=torch.uint8, device=paged.device)
+        hit_buffer = self._hit_buffers[parity]
+        if hit_buffer is None or hit_buffer.numel() < total:
+            hit_buffer = torch.empty(total, dtype=torch.uint8, device=paged.device)
+            self._hit_buffers[parity] = hit_buffer
+            self._copy_tables[parity] = None
         runs: list[list] = []  # [first piece, dst offset, bytes, next src ptr]
         offset = 0
         for host in hosts:
@@ -229,11 +255,21 @@ class PagedBlendLoader:
                 else:
                     runs.append([piece, offset, nbytes, ptr + nbytes])
                 offset += nbytes
-        dst = self._hit_buffer
-        for piece, dst_offset, nbytes, _ in runs:
-            src = byte_span(piece, nbytes)
-            dst[dst_offset : dst_offset + nbytes].copy_(src, non_blocking=True)
-            self._host_refs.append(src)
+        load_stream = torch.cuda.current_stream()
+        copy_stream = _copy_stream(paged.device) if self._load_stream is not None else load_stream
+        if copy_stream is not load_stream:
+            free = self._hit_free.pop(parity, None)
+            if free is not None:
+                copy_stream.wait_event(free)
+        with torch.cuda.stream(copy_stream):
+            for piece, dst_offset, nbytes, _ in runs:
+                src = byte_span(piece, nbytes)
+                hit_buffer[dst_offset : dst_offset + nbytes].copy_(src, non_blocking=True)
+                self._host_refs.append(src)
+        if copy_stream is not load_stream:
+            copied = torch.cuda.Event()
+            copied.record(copy_stream)
+            load_stream.wait_event(copied)
 
     # ----------------------------------------------------------- public API
     def prefetch(self, layer_id: int, rotary_emb) -> None:
@@ -256,6 +292,7 @@ class PagedBlendLoader:
                 event = torch.cuda.Event()
                 event.record(stream)
                 self._events[layer_id] = event
+                self._hit_free[index] = event  # this parity's hit buffer is consumed
         self._buffers[layer_id] = buffer
         if trace:
             assert self.tracer is not None
@@ -312,6 +349,7 @@ class PagedBlendLoader:
             rotary_dim,
             int(neox),
             ZERO_COPY_CTAS if zero_copy else 0,
+            self._device_error.data_ptr(),
             _native.stream_handle(stream),
         )
         if not kernel_rotates and self._rotate.any():
@@ -331,6 +369,10 @@ class PagedBlendLoader:
             old = torch.arange(seg.source_start, seg.source_start + seg.length, device=device)
             new = torch.arange(seg.target_start, seg.target_end, device=device)
             buffer[0, rows] = relocate_key(rotary_emb, old, new, buffer[0, rows])
+
+    def device_error(self) -> int:
+        """Pipeline timeout code reported by the load kernels (0 = none); synchronizes."""
+        return 0 if self._device_error is None else int(self._device_error.item())
 
     def get(self, layer_id: int) -> torch.Tensor:
         event = self._events.pop(layer_id, None)

@@ -144,8 +144,10 @@ __device__ void warp_relocate_row(const T* src, int64_t src_hs, T* dst, int64_t 
   }
 }
 
-// Plain warp row copy / zero with VB-byte vectors (VB = E * sizeof(T)).
-template <int VB>
+// Plain warp row copy with VB-byte vectors.  GSRC: the source is global
+// memory read once (non-coherent streaming loads); otherwise a generic load
+// (shared-memory staging).
+template <int VB, bool GSRC = true>
 __device__ __forceinline__ void warp_copy_heads(const char* src, int64_t src_hs, char* dst,
                                                 int64_t dst_hs, int num_heads, int units_per_head,
                                                 int lane) {
@@ -160,7 +162,11 @@ __device__ __forceinline__ void warp_copy_heads(const char* src, int64_t src_hs,
       if (i < units) {
         const int h = i / units_per_head;
         const int j = i - h * units_per_head;
-        tmp[u] = ld_vec(reinterpret_cast<const V*>(src + h * src_hs + (int64_t)j * VB));
+        const V* p = reinterpret_cast<const V*>(src + h * src_hs + (int64_t)j * VB);
+        if constexpr (GSRC)
+          tmp[u] = ld_vec(p);
+        else
+          tmp[u] = *p;
       }
     }
 #pragma unroll
@@ -284,6 +290,276 @@ __global__ void __launch_bounds__(256) blend_load_kernel(LoadArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// TMA-staged variant: a producer warp moves whole token rows (or per-head
+// pieces) HBM -> shared memory with cp.async.bulk into a kStages-deep ring of
+// 16 KiB tiles guarded by mbarriers; eight consumer warps relocate K / copy V
+// out of shared memory into the staging buffer with 16-byte stores.  Bytes in
+// flight cost no registers (up to 3 CTAs x 64 KiB per SM), which is what an
+// HBM-bound gather with dependent address computation needs.  Used when every
+// address is 16-byte aligned and the sources are device memory.
+namespace tma {
+constexpr int kStages = 4;
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = 32 * (1 + kConsumerWarps);
+constexpr int kTileBytes = 16384;
+constexpr int kMaxRows = 64;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s: a wait that long is a bug
+
+enum : int32_t {
+  kNone = 0,          // past alloc_end
+  kSmemCopy = 1,      // staged by TMA, copied out
+  kSmemRotate = 2,    // staged by TMA, relocated out
+  kZero = 3,          // gap (or an inconsistent descriptor): zeros
+  kDirectCopy = 4,    // source not 16-byte aligned: element-wise global copy
+  kDirectRotate = 5,  // same, relocated
+};
+
+struct RowMeta {
+  int64_t src;
+  int64_t src_hs;
+  int32_t kind;
+  int32_t old_pos;
+};
+
+constexpr size_t kSmemBytes = kStages * kTileBytes + kStages * kMaxRows * sizeof(RowMeta) +
+                              2 * kStages * sizeof(uint64_t);
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity, called by all 32 lanes
+// of a warp; the result is warp-uniform.  Lanes that already observed the
+// phase keep polling it (a completed phase stays observable until the peer
+// side can advance the barrier again, which requires this warp).  Gives up
+// after kTimeoutNs measured by lane 0.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  uint64_t start = 0;
+  const int lane = threadIdx.x & 31;
+  for (uint32_t spin = 0;; ++spin) {
+    const bool mine = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, mine)) return true;
+    if ((spin & 255u) == 0) {
+      int expired = 0;
+      if (lane == 0) {
+        const uint64_t now = global_ns();
+        if (start == 0)
+          start = now;
+        else if (now - start > kTimeoutNs)
+          expired = 1;
+      }
+      if (__shfl_sync(0xffffffffu, expired, 0)) return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void report(int32_t* error, int32_t code) {
+  if (error != nullptr) atomicCAS(error, 0, code);
+}
+
+// Classifies one staging row (producer side).
+__device__ RowMeta classify_row(const LoadArgs& a, int plane, int64_t t, int head_bytes,
+                                int esize) {
+  RowMeta m{0, 0, kNone, 0};
+  if (t >= a.alloc_end) return m;
+  m.kind = kZero;
+  int64_t src;
+  int64_t src_hs;
+  bool rotate = false;
+  if (t < a.apc_prefix) {
+    int64_t slot = __ldg(a.slots + t);
+    if (slot < 0) slot += a.num_slots;
+    if (slot < 0 || slot >= a.num_slots) return m;
+    const uint32_t us = static_cast<uint32_t>(slot);
+    const uint32_t blk = us / a.block_size;
+    const uint32_t off = us - blk * a.block_size;
+    src = reinterpret_cast<int64_t>(plane ? a.v_cache : a.k_cache) + (int64_t)blk * a.block_stride +
+          (int64_t)off * a.slot_stride;
+    src_hs = a.head_stride;
+  } else {
+    const int32_t seg_id = __ldg(a.token_segment + t);
+    if (seg_id < 0 || seg_id >= a.num_segments) return m;
+    const cb_segment_t seg = a.segments[seg_id];
+    const int64_t rel = t - seg.target_start;
+    rotate = plane == 0 && seg.rotate;
+    m.old_pos = static_cast<int32_t>(seg.source_start + rel);
+    if (rel < 0 || rel >= seg.length) return m;
+    if (rotate && (seg.source_start + rel < 0 || seg.source_start + rel >= a.rope.max_position ||
+                   t >= a.rope.max_position))
+      return m;
+    src = static_cast<int64_t>(plane ? seg.v_src : seg.k_src) + rel * seg.src_token_stride;
+    src_hs = seg.src_head_stride;
+  }
+  const uint64_t addr_bits = static_cast<uint64_t>(src) | static_cast<uint64_t>(src_hs);
+  if (addr_bits & static_cast<uint64_t>(esize - 1)) return m;  // not even element-aligned: zeros
+  m.src = src;
+  m.src_hs = src_hs;
+  if ((addr_bits & 15u) == 0 && (head_bytes & 15) == 0)
+    m.kind = rotate ? kSmemRotate : kSmemCopy;
+  else
+    m.kind = rotate ? kDirectRotate : kDirectCopy;
+  return m;
+}
+
+template <typename T, bool NEOX>
+__global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a, int rows_per_tile,
+                                                                   int64_t tiles, int32_t* error) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char* ring = smem;
+  RowMeta* meta = reinterpret_cast<RowMeta*>(smem + kStages * kTileBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + kStages * kMaxRows);
+  uint64_t* empty = full + kStages;
+  constexpr int E = 16 / sizeof(T);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head_bytes = a.rope.head_size * static_cast<int>(sizeof(T));
+  const int row_bytes = a.num_heads * head_bytes;
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---- producer: classify the tile's rows, then stage them with TMA
+    int j = 0;
+    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
+      const int st = j % kStages;
+      const uint32_t phase = (j / kStages) & 1u;
+      if (!mbar_wait(&empty[st], phase ^ 1u)) {
+        if (lane == 0) report(error, 1);
+        return;
+      }
+      const int plane = static_cast<int>(tile & 1);
+      const int64_t tok0 = (tile >> 1) * rows_per_tile;
+      uint32_t bytes = 0;
+      for (int r = lane; r < rows_per_tile; r += 32) {
+        const RowMeta m = classify_row(a, plane, tok0 + r, head_bytes, sizeof(T));
+        meta[st * kMaxRows + r] = m;
+        if (m.kind == kSmemCopy || m.kind == kSmemRotate) bytes += row_bytes;
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+      __syncwarp();
+      if (lane == 0) {
+        if (bytes)
+          mbar_arrive_expect_tx(&full[st], bytes);
+        else
+          mbar_arrive(&full[st]);
+      }
+      __syncwarp();
+      for (int r = lane; r < rows_per_tile; r += 32) {
+        const RowMeta m = meta[st * kMaxRows + r];
+        if (m.kind != kSmemCopy && m.kind != kSmemRotate) continue;
+        unsigned char* dst = ring + st * kTileBytes + r * row_bytes;
+        if (m.src_hs == head_bytes) {
+          bulk_load(dst, reinterpret_cast<const void*>(m.src), row_bytes, &full[st]);
+        } else {
+          for (int h = 0; h < a.num_heads; ++h)
+            bulk_load(dst + h * head_bytes, reinterpret_cast<const void*>(m.src + h * m.src_hs),
+                      head_bytes, &full[st]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- consumers
+  const int cw = warp - 1;
+  const int units = head_bytes / 16;
+  int j = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
+    const int st = j % kStages;
+    const uint32_t phase = (j / kStages) & 1u;
+    if (!mbar_wait(&full[st], phase)) {
+      if (lane == 0) report(error, 2);
+      return;
+    }
+    const int plane = static_cast<int>(tile & 1);
+    const int64_t tok0 = (tile >> 1) * rows_per_tile;
+    for (int r = cw; r < rows_per_tile; r += kConsumerWarps) {
+      const RowMeta m = meta[st * kMaxRows + r];
+      if (m.kind == kNone) continue;
+      const int64_t t = tok0 + r;
+      char* dst = a.out + plane * a.out_plane_stride + t * a.out_token_stride;
+      const char* staged = reinterpret_cast<const char*>(ring + st * kTileBytes + r * row_bytes);
+      const int64_t dst_hs = a.out_head_stride / (int64_t)sizeof(T);
+      switch (m.kind) {
+        case kSmemCopy:
+          warp_copy_heads<16, false>(staged, head_bytes, dst, a.out_head_stride, a.num_heads, units,
+                                     lane);
+          break;
+        case kSmemRotate:
+          warp_relocate_row<T, E, NEOX, true>(reinterpret_cast<const T*>(staged),
+                                              a.rope.head_size, reinterpret_cast<T*>(dst), dst_hs,
+                                              a.num_heads, a.rope, m.old_pos, t, lane);
+          break;
+        case kDirectCopy:
+          warp_copy_heads<sizeof(T)>(reinterpret_cast<const char*>(m.src), m.src_hs, dst,
+                                     a.out_head_stride, a.num_heads, a.rope.head_size, lane);
+          break;
+        case kDirectRotate:
+          warp_relocate_row<T, NEOX ? 1 : 2, NEOX, false>(
+              reinterpret_cast<const T*>(m.src), m.src_hs / (int64_t)sizeof(T),
+              reinterpret_cast<T*>(dst), dst_hs, a.num_heads, a.rope, m.old_pos, t, lane);
+          break;
+        default:
+          warp_zero_heads<16>(dst, a.out_head_stride, a.num_heads, units, lane);
+          break;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+}
+
+}  // namespace tma
+
 struct RelocArgs {
   const char* key;
   char* out;
@@ -329,8 +605,33 @@ bool use_vector_path(uint64_t addr_acc, int esize, int head_size, int rotary_dim
   return true;
 }
 
+template <typename T, bool NEOX>
+int launch_tma_load(const LoadArgs& a, int32_t* error, cudaStream_t s) {
+  const int row_bytes = a.num_heads * a.rope.head_size * static_cast<int>(sizeof(T));
+  int rows = tma::kTileBytes / row_bytes;
+  if (rows > tma::kMaxRows) rows = tma::kMaxRows;
+  const int64_t tiles = 2 * ((a.alloc_end + rows - 1) / rows);
+  const int64_t cap = static_cast<int64_t>(kSmCount) * 2;
+  const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+  auto kernel = tma::blend_load_tma_kernel<T, NEOX>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(tma::kSmemBytes));
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  kernel<<<grid, tma::kThreads, tma::kSmemBytes, s>>>(a, rows, tiles, error);
+  return launch_status("cb_blend_load_layer");
+}
+
 template <typename T>
-int dispatch_load(const LoadArgs& a, bool vec, bool neox, int64_t max_ctas, cudaStream_t s) {
+int dispatch_load(const LoadArgs& a, bool vec, bool neox, int64_t max_ctas, int32_t* error,
+                  cudaStream_t s) {
+  const int64_t row_bytes = (int64_t)a.num_heads * a.rope.head_size * (int64_t)sizeof(T);
+  if (vec && max_ctas <= 0 && row_bytes <= tma::kTileBytes) {
+    // device-memory sources: TMA-staged pipeline
+    return neox ? launch_tma_load<T, true>(a, error, s) : launch_tma_load<T, false>(a, error, s);
+  }
   int grid = grid_for(2 * a.alloc_end);
   if (max_ctas > 0 && grid > max_ctas) grid = static_cast<int>(max_ctas);
   constexpr int EV = 16 / sizeof(T);
@@ -427,7 +728,8 @@ extern "C" int cb_blend_load_layer(void* out, int64_t out_plane_stride, int64_t 
                                    int64_t head_size, int dtype, const int32_t* token_segment,
                                    const cb_segment_t* segments, int64_t num_segments,
                                    const void* cos_sin, int64_t max_position, int64_t rotary_dim,
-                                   int is_neox, int64_t max_ctas, void* stream) {
+                                   int is_neox, int64_t max_ctas, int32_t* device_error,
+                                   void* stream) {
   CB_BIND(stream, out);
   int rc = check_rope(head_size, rotary_dim, is_neox, dtype);
   if (rc != CB_OK) return rc;
@@ -477,10 +779,10 @@ extern "C" int cb_blend_load_layer(void* out, int64_t out_plane_stride, int64_t 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (dtype) {
     case CB_DTYPE_BF16:
-      return dispatch_load<__nv_bfloat16>(a, vec, is_neox != 0, max_ctas, s);
+      return dispatch_load<__nv_bfloat16>(a, vec, is_neox != 0, max_ctas, device_error, s);
     case CB_DTYPE_FP16:
-      return dispatch_load<__half>(a, vec, is_neox != 0, max_ctas, s);
+      return dispatch_load<__half>(a, vec, is_neox != 0, max_ctas, device_error, s);
     default:
-      return dispatch_load<float>(a, vec, is_neox != 0, max_ctas, s);
+      return dispatch_load<float>(a, vec, is_neox != 0, max_ctas, device_error, s);
   }
 }
