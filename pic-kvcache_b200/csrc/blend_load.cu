@@ -75,25 +75,81 @@ struct RopeDesc {
   int head_size;
 };
 
-// Relocates one token row (num_heads heads) with the whole warp.
+// ---- packed 2 x 16-bit arithmetic ------------------------------------------
+// mul/add/sub.rn on bf16x2 / f16x2 round the exact result once to the 16-bit
+// type.  That equals torch's evaluation (fp32 op, then round to the 16-bit
+// type): a product of two 8-bit (bf16) or 11-bit (fp16) significands is exact
+// in fp32, and a sum is either exact in fp32 or its smaller operand lies
+// below half an ulp of the 16-bit result, where fp32 rounding cannot move the
+// final rounding.  Explicit .rn keeps ptxas from contracting mul+add to fma.
+template <typename T>
+struct Packed;
+template <>
+struct Packed<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+};
+template <>
+struct Packed<__half> {
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t add(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+};
+
+// Delta rotation + rotation of one packed pair of lanes:
+//   dc = nc*oc + ns*os, ds = ns*oc - nc*os, a' = a*dc - b*ds, b' = b*dc + a*ds
+template <typename T>
+__device__ __forceinline__ void packed_delta(uint32_t nc, uint32_t ns, uint32_t oc, uint32_t os,
+                                             uint32_t& dc, uint32_t& ds) {
+  using P = Packed<T>;
+  dc = P::add(P::mul(nc, oc), P::mul(ns, os));
+  ds = P::sub(P::mul(ns, oc), P::mul(nc, os));
+}
+
+// Relocates one token row (num_heads heads) with the whole warp.  old_cs /
+// new_cs point at the rotary_dim-element cos|sin rows of the two positions.
 // E = elements per work item: 16 bytes on the vector path (VM), 1 (neox) or
-// 2 (one GPT-J pair) on the element-wise path.
+// 2 (one GPT-J pair) on the element-wise path.  16-bit types on the vector
+// path use packed arithmetic, everything else per-element fp32 ops + rounding.
 template <typename T, int E, bool NEOX, bool VM>
 __device__ void warp_relocate_row(const T* src, int64_t src_hs, T* dst, int64_t dst_hs,
-                                  int num_heads, const RopeDesc& rope, int64_t old_pos,
-                                  int64_t new_pos, int lane) {
-  const int R = rope.rotary_dim;
-  const int D = rope.head_size;
+                                  int num_heads, int head_size, int rotary_dim, const T* old_cs,
+                                  const T* new_cs, int lane) {
+  const int R = rotary_dim;
+  const int D = head_size;
   const int half = R / 2;
-  const T* cs = static_cast<const T*>(rope.cos_sin);
-  const T* old_cs = cs + old_pos * R;
-  const T* new_cs = cs + new_pos * R;
   // rotary items per head: neox pairs (i, i+half) in groups of E; GPT-J
   // interleaved pairs in vectors of E elements (E/2 pairs).
   const int rot_items = NEOX ? half / E : R / E;
   const int pass_items = (D - R) / E;
   const int per_head = rot_items + pass_items;
   const int items = num_heads * per_head;
+  constexpr bool kPacked = VM && sizeof(T) == 2;
   for (int it = lane; it < items; it += 32) {
     const int h = it / per_head;
     const int c = it - h * per_head;
@@ -104,7 +160,61 @@ __device__ void warp_relocate_row(const T* src, int64_t src_hs, T* dst, int64_t 
       store_pack<T, E, VM>(d + off, load_pack<T, E, VM>(s + off));
       continue;
     }
-    if constexpr (NEOX) {
+    if constexpr (kPacked) {
+      using P = Packed<T>;
+      if constexpr (NEOX) {
+        const int i0 = c * E;  // E == 8: four packed pairs of (i, i+1)
+        const uint4 a = *reinterpret_cast<const uint4*>(s + i0);
+        const uint4 b = *reinterpret_cast<const uint4*>(s + half + i0);
+        const uint4 oc = *reinterpret_cast<const uint4*>(old_cs + i0);
+        const uint4 os = *reinterpret_cast<const uint4*>(old_cs + half + i0);
+        const uint4 nc = *reinterpret_cast<const uint4*>(new_cs + i0);
+        const uint4 ns = *reinterpret_cast<const uint4*>(new_cs + half + i0);
+        const uint32_t* A = &a.x;
+        const uint32_t* B = &b.x;
+        const uint32_t* OC = &oc.x;
+        const uint32_t* OS = &os.x;
+        const uint32_t* NC = &nc.x;
+        const uint32_t* NS = &ns.x;
+        uint4 ra, rb;
+        uint32_t* RA = &ra.x;
+        uint32_t* RB = &rb.x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint32_t dc, ds;
+          packed_delta<T>(NC[k], NS[k], OC[k], OS[k], dc, ds);
+          RA[k] = P::sub(P::mul(A[k], dc), P::mul(B[k], ds));
+          RB[k] = P::add(P::mul(B[k], dc), P::mul(A[k], ds));
+        }
+        *reinterpret_cast<uint4*>(d + i0) = ra;
+        *reinterpret_cast<uint4*>(d + half + i0) = rb;
+      } else {
+        const int i0 = c * E;  // 8 elements = pairs c*4 .. c*4+3
+        const uint4 x = *reinterpret_cast<const uint4*>(s + i0);
+        const uint2 oc = *reinterpret_cast<const uint2*>(old_cs + c * 4);
+        const uint2 os = *reinterpret_cast<const uint2*>(old_cs + half + c * 4);
+        const uint2 nc = *reinterpret_cast<const uint2*>(new_cs + c * 4);
+        const uint2 ns = *reinterpret_cast<const uint2*>(new_cs + half + c * 4);
+        uint32_t dc[2], ds[2];
+        packed_delta<T>(nc.x, ns.x, oc.x, os.x, dc[0], ds[0]);
+        packed_delta<T>(nc.y, ns.y, oc.y, os.y, dc[1], ds[1]);
+        const uint32_t* X = &x.x;
+        uint4 r;
+        uint32_t* Rw = &r.x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          // broadcast pair k's (dc, ds) to both halves
+          const uint32_t sel = (k & 1) ? 0x3232u : 0x1010u;
+          const uint32_t dck = __byte_perm(dc[k >> 1], 0, sel);
+          const uint32_t dsk = __byte_perm(ds[k >> 1], 0, sel);
+          const uint32_t swapped = __byte_perm(X[k], 0, 0x1032u);      // (b, a)
+          const uint32_t m1 = P::mul(X[k], dck);                        // (a*dc, b*dc)
+          const uint32_t m2 = P::mul(swapped, dsk) ^ 0x00008000u;       // (-(b*ds), a*ds)
+          Rw[k] = P::add(m1, m2);  // (a*dc - b*ds, b*dc + a*ds); x - y == x + (-y) exactly
+        }
+        *reinterpret_cast<uint4*>(d + i0) = r;
+      }
+    } else if constexpr (NEOX) {
       const int i0 = c * E;
       const Pack<T, E> a = load_pack<T, E, VM>(s + i0);
       const Pack<T, E> b = load_pack<T, E, VM>(s + half + i0);
@@ -142,6 +252,12 @@ __device__ void warp_relocate_row(const T* src, int64_t src_hs, T* dst, int64_t 
       store_pack<T, E, VM>(d + i0, r);
     }
   }
+}
+
+// Table rows of a position (cos half then sin half).
+template <typename T>
+__device__ __forceinline__ const T* rope_row(const RopeDesc& rope, int64_t pos) {
+  return static_cast<const T*>(rope.cos_sin) + pos * rope.rotary_dim;
 }
 
 // Plain warp row copy with VB-byte vectors.  GSRC: the source is global
@@ -272,14 +388,16 @@ __global__ void __launch_bounds__(256) blend_load_kernel(LoadArgs a) {
     const int64_t src_hs = seg.src_head_stride / (int64_t)sizeof(T);
     const int64_t dst_hs = a.out_head_stride / (int64_t)sizeof(T);
     if (rotate) {
+      const T* ocs = rope_row<T>(a.rope, old_pos);
+      const T* ncs = rope_row<T>(a.rope, t);
       if (aligned)
         warp_relocate_row<T, E, NEOX, VM>(reinterpret_cast<const T*>(src), src_hs,
-                                          reinterpret_cast<T*>(dst), dst_hs, a.num_heads, a.rope,
-                                          old_pos, t, lane);
+                                          reinterpret_cast<T*>(dst), dst_hs, a.num_heads,
+                                          a.rope.head_size, a.rope.rotary_dim, ocs, ncs, lane);
       else
-        warp_relocate_row<T, NEOX ? 1 : 2, NEOX, false>(reinterpret_cast<const T*>(src), src_hs,
-                                                        reinterpret_cast<T*>(dst), dst_hs,
-                                                        a.num_heads, a.rope, old_pos, t, lane);
+        warp_relocate_row<T, NEOX ? 1 : 2, NEOX, false>(
+            reinterpret_cast<const T*>(src), src_hs, reinterpret_cast<T*>(dst), dst_hs,
+            a.num_heads, a.rope.head_size, a.rope.rotary_dim, ocs, ncs, lane);
     } else if (aligned) {
       warp_copy_heads<VB>(src, seg.src_head_stride, dst, a.out_head_stride, a.num_heads, units,
                           lane);
@@ -456,6 +574,9 @@ __global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a,
   const int lane = threadIdx.x & 31;
   const int head_bytes = a.rope.head_size * static_cast<int>(sizeof(T));
   const int row_bytes = a.num_heads * head_bytes;
+  // per stage: rows_per_tile data rows, then one cos|sin row pair per data row
+  const int cs_row_bytes = a.rope.rotary_dim * static_cast<int>(sizeof(T));
+  const int cs_offset = rows_per_tile * row_bytes;
   if (threadIdx.x == 0) {
     for (int st = 0; st < kStages; ++st) {
       mbar_init(&full[st], 1);
@@ -481,7 +602,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a,
       for (int r = lane; r < rows_per_tile; r += 32) {
         const RowMeta m = classify_row(a, plane, tok0 + r, head_bytes, sizeof(T));
         meta[st * kMaxRows + r] = m;
-        if (m.kind == kSmemCopy || m.kind == kSmemRotate) bytes += row_bytes;
+        if (m.kind == kSmemCopy) bytes += row_bytes;
+        if (m.kind == kSmemRotate) bytes += row_bytes + 2 * cs_row_bytes;
       }
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
@@ -503,6 +625,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a,
           for (int h = 0; h < a.num_heads; ++h)
             bulk_load(dst + h * head_bytes, reinterpret_cast<const void*>(m.src + h * m.src_hs),
                       head_bytes, &full[st]);
+        }
+        if (m.kind == kSmemRotate) {
+          unsigned char* cs = ring + st * kTileBytes + cs_offset + r * 2 * cs_row_bytes;
+          bulk_load(cs, rope_row<T>(a.rope, m.old_pos), cs_row_bytes, &full[st]);
+          bulk_load(cs + cs_row_bytes, rope_row<T>(a.rope, tok0 + r), cs_row_bytes, &full[st]);
         }
       }
     }
@@ -534,11 +661,15 @@ __global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a,
           warp_copy_heads<16, false>(staged, head_bytes, dst, a.out_head_stride, a.num_heads, units,
                                      lane);
           break;
-        case kSmemRotate:
+        case kSmemRotate: {
+          const T* cs = reinterpret_cast<const T*>(ring + st * kTileBytes + cs_offset +
+                                                   r * 2 * cs_row_bytes);
           warp_relocate_row<T, E, NEOX, true>(reinterpret_cast<const T*>(staged),
                                               a.rope.head_size, reinterpret_cast<T*>(dst), dst_hs,
-                                              a.num_heads, a.rope, m.old_pos, t, lane);
+                                              a.num_heads, a.rope.head_size, a.rope.rotary_dim,
+                                              cs, cs + a.rope.rotary_dim, lane);
           break;
+        }
         case kDirectCopy:
           warp_copy_heads<sizeof(T)>(reinterpret_cast<const char*>(m.src), m.src_hs, dst,
                                      a.out_head_stride, a.num_heads, a.rope.head_size, lane);
@@ -546,7 +677,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a,
         case kDirectRotate:
           warp_relocate_row<T, NEOX ? 1 : 2, NEOX, false>(
               reinterpret_cast<const T*>(m.src), m.src_hs / (int64_t)sizeof(T),
-              reinterpret_cast<T*>(dst), dst_hs, a.num_heads, a.rope, m.old_pos, t, lane);
+              reinterpret_cast<T*>(dst), dst_hs, a.num_heads, a.rope.head_size,
+              a.rope.rotary_dim, rope_row<T>(a.rope, m.old_pos), rope_row<T>(a.rope, t), lane);
           break;
         default:
           warp_zero_heads<16>(dst, a.out_head_stride, a.num_heads, units, lane);
@@ -581,10 +713,11 @@ __global__ void __launch_bounds__(256) relocate_kernel(RelocArgs a) {
     const int64_t op = __ldg(a.old_pos + t);
     const int64_t np = __ldg(a.new_pos + t);
     if (op < 0 || op >= a.rope.max_position || np < 0 || np >= a.rope.max_position) continue;
-    warp_relocate_row<T, E, NEOX, E * sizeof(T) == 16>(reinterpret_cast<const T*>(a.key + t * a.token_stride),
-                                  a.rope.head_size,
-                                  reinterpret_cast<T*>(a.out + t * a.out_token_stride),
-                                  a.rope.head_size, a.num_heads, a.rope, op, np, lane);
+    warp_relocate_row<T, E, NEOX, E * sizeof(T) == 16>(
+        reinterpret_cast<const T*>(a.key + t * a.token_stride), a.rope.head_size,
+        reinterpret_cast<T*>(a.out + t * a.out_token_stride), a.rope.head_size, a.num_heads,
+        a.rope.head_size, a.rope.rotary_dim, rope_row<T>(a.rope, op), rope_row<T>(a.rope, np),
+        lane);
   }
 }
 
@@ -608,7 +741,8 @@ bool use_vector_path(uint64_t addr_acc, int esize, int head_size, int rotary_dim
 template <typename T, bool NEOX>
 int launch_tma_load(const LoadArgs& a, int32_t* error, cudaStream_t s) {
   const int row_bytes = a.num_heads * a.rope.head_size * static_cast<int>(sizeof(T));
-  int rows = tma::kTileBytes / row_bytes;
+  const int cs_bytes = 2 * a.rope.rotary_dim * static_cast<int>(sizeof(T));
+  int rows = tma::kTileBytes / (row_bytes + cs_bytes);
   if (rows > tma::kMaxRows) rows = tma::kMaxRows;
   const int64_t tiles = 2 * ((a.alloc_end + rows - 1) / rows);
   const int64_t cap = static_cast<int64_t>(kSmCount) * 2;
@@ -628,7 +762,8 @@ template <typename T>
 int dispatch_load(const LoadArgs& a, bool vec, bool neox, int64_t max_ctas, int32_t* error,
                   cudaStream_t s) {
   const int64_t row_bytes = (int64_t)a.num_heads * a.rope.head_size * (int64_t)sizeof(T);
-  if (vec && max_ctas <= 0 && row_bytes <= tma::kTileBytes) {
+  const int64_t cs_bytes = 2 * (int64_t)a.rope.rotary_dim * (int64_t)sizeof(T);
+  if (vec && max_ctas <= 0 && row_bytes + cs_bytes <= tma::kTileBytes) {
     // device-memory sources: TMA-staged pipeline
     return neox ? launch_tma_load<T, true>(a, error, s) : launch_tma_load<T, false>(a, error, s);
   }

@@ -20,7 +20,7 @@ def _bits(t: torch.Tensor) -> np.ndarray:
 
 
 def _case(device, *, hnd: bool, misalign: bool, apc: int, heads=4, hd=128, bs=16, pool=512,
-          tokens=2048, chunk=256, seed=0):
+          tokens=2048, chunk=256, seed=0, neox=True):
     rng = np.random.default_rng(seed)
     gen = torch.Generator(device=device).manual_seed(seed)
     if hnd:
@@ -56,7 +56,7 @@ def _case(device, *, hnd: bool, misalign: bool, apc: int, heads=4, hd=128, bs=16
     cos_sin = oracle.f32_to_bf16(np.concatenate((np.cos(freqs), np.sin(freqs)), -1).astype(np.float32))
     return dict(cache=cache, hit=hit, table=table, hosts=hosts, slots=slots, alloc_end=alloc_end,
                 token_segment=token_segment, cos_sin=cos_sin, sources=sources, hit_idx=hit_idx,
-                heads=heads, hd=hd, bs=bs, chunk=chunk, apc=apc, hnd=hnd)
+                heads=heads, hd=hd, bs=bs, chunk=chunk, apc=apc, hnd=hnd, neox=neox)
 
 
 def _run(case, device, max_ctas: int):
@@ -74,8 +74,8 @@ def _run(case, device, max_ctas: int):
         "cb_blend_load_layer", out.data_ptr(), out.stride(0) * esize, out.stride(1) * esize, hd * esize,
         c["alloc_end"], c["apc"], cache[0].data_ptr(), cache[1].data_ptr(), cache.stride(1) * esize,
         cache.stride(2) * esize, cache.stride(3) * esize, cache.shape[1], c["bs"], slots.data_ptr(), heads,
-        hd, 0, token_segment.data_ptr(), table.data_ptr(), 4, cos_sin.data_ptr(), cos_sin.shape[0], hd, 1,
-        max_ctas, error.data_ptr(), _native.stream_handle(),
+        hd, 0, token_segment.data_ptr(), table.data_ptr(), 4, cos_sin.data_ptr(), cos_sin.shape[0], hd,
+        int(c["neox"]), max_ctas, error.data_ptr(), _native.stream_handle(),
     )
     torch.cuda.synchronize()
     assert int(error.item()) == 0
@@ -89,7 +89,8 @@ def _expected(case):
     segs = [(int(c["sources"][i]), int(c["hit_idx"][i]) * c["chunk"], c["chunk"], c["hosts"][i])
             for i in range(4)]
     return oracle.blend_load(oracle.BF16, c["alloc_end"], c["apc"], k_np, v_np, c["slots"][: c["alloc_end"]],
-                             c["bs"], segs, np.ones(4, dtype=np.int32), c["cos_sin"], c["hd"], c["hd"], True)
+                             c["bs"], segs, np.ones(4, dtype=np.int32), c["cos_sin"], c["hd"], c["hd"],
+                             c["neox"])
 
 
 @pytest.mark.parametrize("hnd", [False, True])
@@ -102,6 +103,42 @@ def test_blend_load_paths_match_oracle(cuda, hnd, misalign, max_ctas):
 
 @pytest.mark.parametrize("heads", [1, 2, 8, 16])
 def test_blend_load_tma_tile_shapes(cuda, heads):
-    # rows per 16 KiB tile from 64 (1 head) down to 8 (16 heads)
+    # rows per 16 KiB tile from 64 (1 head) down to 4 (16 heads)
     case = _case(cuda, hnd=False, misalign=False, apc=0, heads=heads, seed=10 + heads)
     assert np.array_equal(_run(case, cuda, 0), _expected(case))
+
+
+@pytest.mark.parametrize("max_ctas", [0, 64])
+def test_blend_load_gptj_matches_oracle(cuda, max_ctas):
+    case = _case(cuda, hnd=False, misalign=False, apc=100, seed=21, neox=False)
+    assert np.array_equal(_run(case, cuda, max_ctas), _expected(case))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("neox", [True, False])
+@pytest.mark.parametrize("contiguous", [True, False])
+def test_relocate_key_random_vs_oracle(cuda, dtype, neox, contiguous):
+    from cacheblend_b200.rope import relocate_key
+
+    gen = torch.Generator(device=cuda).manual_seed(7)
+    hd, heads, tokens, max_pos = 128, 8, 3000, 40960
+    inv = 1.0 / (1e6 ** (torch.arange(0, hd, 2, dtype=torch.float64) / hd))
+    freqs = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+
+    class Rope:
+        head_size = rotary_dim = hd
+        is_neox_style = neox
+        cos_sin_cache = torch.cat((freqs.cos(), freqs.sin()), -1).float().to(cuda)
+
+    base = torch.randn(tokens, heads * hd + (0 if contiguous else 3), generator=gen, device=cuda).to(dtype)
+    key = base[:, : heads * hd] if contiguous else base[:, 3:]  # 6-byte offset rows: scalar path
+    old = torch.randint(0, max_pos, (tokens,), generator=gen, device=cuda)
+    new = torch.randint(0, max_pos, (tokens,), generator=gen, device=cuda)
+    out = relocate_key(Rope(), old, new, key)
+    code = {torch.bfloat16: oracle.BF16, torch.float16: oracle.FP16, torch.float32: oracle.FP32}[dtype]
+    table = Rope.cos_sin_cache.to(dtype).cpu()
+    to_np = (lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)) if dtype == torch.bfloat16 \
+        else (lambda t: t.contiguous().numpy())
+    want = oracle.relocate(to_np(key.cpu()), to_np(table), old.cpu().numpy(), new.cpu().numpy(), hd, hd, neox,
+                           code)
+    assert np.array_equal(to_np(out.cpu()), want)
