@@ -417,10 +417,10 @@ __global__ void __launch_bounds__(256) blend_load_kernel(LoadArgs a) {
 // HBM-bound gather with dependent address computation needs.  Used when every
 // address is 16-byte aligned and the sources are device memory.
 namespace tma {
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = 32 * (1 + kConsumerWarps);
-constexpr int kTileBytes = 16384;
+constexpr int kTileBytes = 20480;  // 8 rows of 8 bf16 heads x 128 + their cos|sin rows
 constexpr int kMaxRows = 64;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s: a wait that long is a bug
 
@@ -440,8 +440,15 @@ struct RowMeta {
   int32_t old_pos;
 };
 
-constexpr size_t kSmemBytes = kStages * kTileBytes + kStages * kMaxRows * sizeof(RowMeta) +
-                              2 * kStages * sizeof(uint64_t);
+constexpr int kSmemSegments = 256;  // segment tables up to this size are copied to smem
+constexpr size_t kFixedSmemBytes = kStages * kTileBytes + kStages * kMaxRows * sizeof(RowMeta) +
+                                   2 * kStages * sizeof(uint64_t);
+// dynamic shared memory of a launch: ring + row metadata + barriers + the
+// segment table when it is small enough to live in shared memory
+inline size_t smem_bytes(int64_t num_segments) {
+  return kFixedSmemBytes +
+         (num_segments <= kSmemSegments ? num_segments * sizeof(cb_segment_t) : 0);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -517,9 +524,27 @@ __device__ __forceinline__ void report(int32_t* error, int32_t code) {
   if (error != nullptr) atomicCAS(error, 0, code);
 }
 
-// Classifies one staging row (producer side).
-__device__ RowMeta classify_row(const LoadArgs& a, int plane, int64_t t, int head_bytes,
-                                int esize) {
+// Raw per-row inputs the producer prefetches one tile ahead: the slot of an
+// APC-prefix row, or the segment index of any other row.
+struct RowRaw {
+  int64_t slot;
+  int32_t seg;
+};
+
+__device__ __forceinline__ RowRaw load_raw(const LoadArgs& a, int64_t t) {
+  RowRaw raw{-1, -1};
+  if (t >= a.alloc_end) return raw;
+  if (t < a.apc_prefix)
+    raw.slot = __ldg(a.slots + t);
+  else
+    raw.seg = __ldg(a.token_segment + t);
+  return raw;
+}
+
+// Classifies one staging row (producer side); `segs` is the segment table in
+// shared memory when it fits there, else in global memory.
+__device__ RowMeta classify_row(const LoadArgs& a, const cb_segment_t* segs, int plane, int64_t t,
+                                const RowRaw& raw, int head_bytes, int esize) {
   RowMeta m{0, 0, kNone, 0};
   if (t >= a.alloc_end) return m;
   m.kind = kZero;
@@ -527,7 +552,7 @@ __device__ RowMeta classify_row(const LoadArgs& a, int plane, int64_t t, int hea
   int64_t src_hs;
   bool rotate = false;
   if (t < a.apc_prefix) {
-    int64_t slot = __ldg(a.slots + t);
+    int64_t slot = raw.slot;
     if (slot < 0) slot += a.num_slots;
     if (slot < 0 || slot >= a.num_slots) return m;
     const uint32_t us = static_cast<uint32_t>(slot);
@@ -537,9 +562,9 @@ __device__ RowMeta classify_row(const LoadArgs& a, int plane, int64_t t, int hea
           (int64_t)off * a.slot_stride;
     src_hs = a.head_stride;
   } else {
-    const int32_t seg_id = __ldg(a.token_segment + t);
+    const int32_t seg_id = raw.seg;
     if (seg_id < 0 || seg_id >= a.num_segments) return m;
-    const cb_segment_t seg = a.segments[seg_id];
+    const cb_segment_t seg = segs[seg_id];
     const int64_t rel = t - seg.target_start;
     rotate = plane == 0 && seg.rotate;
     m.old_pos = static_cast<int32_t>(seg.source_start + rel);
@@ -562,13 +587,14 @@ __device__ RowMeta classify_row(const LoadArgs& a, int plane, int64_t t, int hea
 }
 
 template <typename T, bool NEOX>
-__global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a, int rows_per_tile,
+__global__ void __launch_bounds__(kThreads, 3) blend_load_tma_kernel(LoadArgs a, int rows_per_tile,
                                                                    int64_t tiles, int32_t* error) {
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* ring = smem;
   RowMeta* meta = reinterpret_cast<RowMeta*>(smem + kStages * kTileBytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + kStages * kMaxRows);
   uint64_t* empty = full + kStages;
+  cb_segment_t* seg_smem = reinterpret_cast<cb_segment_t*>(empty + kStages);
   constexpr int E = 16 / sizeof(T);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -584,14 +610,37 @@ __global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a,
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  const bool segs_in_smem = a.num_segments <= kSmemSegments;
+  if (segs_in_smem) {
+    // 8-byte words: cb_segment_t's own alignment, whatever the caller's pointer
+    const int words = static_cast<int>(a.num_segments * sizeof(cb_segment_t) / sizeof(uint2));
+    const uint2* from = reinterpret_cast<const uint2*>(a.segments);
+    uint2* to = reinterpret_cast<uint2*>(seg_smem);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) to[i] = from[i];
+  }
   __syncthreads();
+  const cb_segment_t* segs = segs_in_smem ? seg_smem : a.segments;
 
   if (warp == 0) {
-    // ---- producer: classify the tile's rows, then stage them with TMA
+    // ---- producer: classify the tile's rows, then stage them with TMA.  The
+    // raw per-row indices of the next tile are loaded before waiting for a
+    // free stage, so their latency hides behind the ring.
+    RowRaw raw[2], raw_next[2];
+    {
+      const int64_t tok0 = (static_cast<int64_t>(blockIdx.x) >> 1) * rows_per_tile;
+      raw[0] = load_raw(a, blockIdx.x < tiles && lane < rows_per_tile ? tok0 + lane : a.alloc_end);
+      raw[1] = load_raw(a, blockIdx.x < tiles && lane + 32 < rows_per_tile ? tok0 + lane + 32
+                                                                             : a.alloc_end);
+    }
     int j = 0;
     for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++j) {
       const int st = j % kStages;
       const uint32_t phase = (j / kStages) & 1u;
+      const int64_t next = tile + gridDim.x;
+      const int64_t next0 = (next >> 1) * rows_per_tile;
+      raw_next[0] = load_raw(a, next < tiles && lane < rows_per_tile ? next0 + lane : a.alloc_end);
+      raw_next[1] = load_raw(a, next < tiles && lane + 32 < rows_per_tile ? next0 + lane + 32
+                                                                           : a.alloc_end);
       if (!mbar_wait(&empty[st], phase ^ 1u)) {
         if (lane == 0) report(error, 1);
         return;
@@ -599,12 +648,17 @@ __global__ void __launch_bounds__(kThreads, 2) blend_load_tma_kernel(LoadArgs a,
       const int plane = static_cast<int>(tile & 1);
       const int64_t tok0 = (tile >> 1) * rows_per_tile;
       uint32_t bytes = 0;
-      for (int r = lane; r < rows_per_tile; r += 32) {
-        const RowMeta m = classify_row(a, plane, tok0 + r, head_bytes, sizeof(T));
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int r = lane + 32 * q;
+        if (r >= rows_per_tile) continue;
+        const RowMeta m = classify_row(a, segs, plane, tok0 + r, raw[q], head_bytes, sizeof(T));
         meta[st * kMaxRows + r] = m;
         if (m.kind == kSmemCopy) bytes += row_bytes;
         if (m.kind == kSmemRotate) bytes += row_bytes + 2 * cs_row_bytes;
       }
+      raw[0] = raw_next[0];
+      raw[1] = raw_next[1];
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
       __syncwarp();
@@ -745,16 +799,17 @@ int launch_tma_load(const LoadArgs& a, int32_t* error, cudaStream_t s) {
   int rows = tma::kTileBytes / (row_bytes + cs_bytes);
   if (rows > tma::kMaxRows) rows = tma::kMaxRows;
   const int64_t tiles = 2 * ((a.alloc_end + rows - 1) / rows);
-  const int64_t cap = static_cast<int64_t>(kSmCount) * 2;
+  const int64_t cap = static_cast<int64_t>(kSmCount) * 3;
   const int grid = static_cast<int>(tiles < cap ? tiles : cap);
   auto kernel = tma::blend_load_tma_kernel<T, NEOX>;
+  const size_t smem = tma::smem_bytes(a.num_segments);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(tma::kSmemBytes));
+                                       static_cast<int>(smem));
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
     return CB_ERR_CUDA;
   }
-  kernel<<<grid, tma::kThreads, tma::kSmemBytes, s>>>(a, rows, tiles, error);
+  kernel<<<grid, tma::kThreads, smem, s>>>(a, rows, tiles, error);
   return launch_status("cb_blend_load_layer");
 }
 

@@ -15,6 +15,8 @@
 // k-th largest key T and how many entries equal to T to keep (lowest indices
 // first); a two-pass ordered compaction writes the indices.  Scores are small
 // (<= 4 B x active tokens) and L2-resident, so the select is latency-bound.
+#include <cooperative_groups.h>
+
 #include "cb_common.cuh"
 
 namespace cb {
@@ -247,6 +249,150 @@ __global__ void __launch_bounds__(kSelThreads) select_topk_kernel(
   }
 }
 
+// ---- cluster select ---------------------------------------------------------
+// Eight CTAs of one thread-block cluster split the scores into contiguous
+// slices held in shared memory as order keys (+ base flags).  Each radix pass
+// builds a local 256-bin histogram, merges it into rank 0's histogram through
+// distributed shared memory, and every CTA derives the same digit from it.
+// The ordered compaction needs, per CTA, the selected counts of the lower
+// ranks, again read through DSMEM.  Scores cross HBM/L2 once.
+namespace cg = cooperative_groups;
+constexpr int kClusterCtas = 8;
+constexpr int kMaxSlice = 44 * 1024;  // keys per CTA: 5 bytes each in shared memory
+
+__device__ __forceinline__ void find_digit(const uint32_t* hist, int64_t krem, uint32_t* s_digit,
+                                           int64_t* s_above) {
+  const int lane = threadIdx.x;  // called by warp 0
+  uint32_t local[8];
+  uint32_t sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    local[j] = hist[255 - 8 * lane - j];
+    sum += local[j];
+  }
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t above = incl - sum;
+  if ((int64_t)above < krem && (int64_t)incl >= krem) {
+    uint32_t run = above;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if ((int64_t)(run + local[j]) >= krem) {
+        *s_digit = 255 - 8 * lane - j;
+        *s_above = run;
+        break;
+      }
+      run += local[j];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
+    const float* __restrict__ scores, const uint8_t* __restrict__ base, int64_t n, int64_t k,
+    int64_t* __restrict__ out, int64_t cap, int slice) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  extern __shared__ __align__(16) uint32_t dyn[];
+  uint32_t* keys = dyn;
+  uint8_t* flags = reinterpret_cast<uint8_t*>(keys + slice);
+  // rank 0's copy is the cluster histogram, double-buffered by pass parity:
+  // buffer p&1 is zeroed at the start of pass p, and its last readers (pass
+  // p-2) finished before the cluster barrier that opened pass p-1.
+  __shared__ uint32_t hist[2][256];
+  __shared__ uint32_t local[256];
+  __shared__ int64_t warp_sums[32];
+  __shared__ int64_t totals[2];    // this CTA's (selected, tied) counts
+  __shared__ uint32_t s_digit;
+  __shared__ int64_t s_above;
+  const int tid = threadIdx.x;
+  const int64_t lo = (int64_t)rank * slice;
+  const int64_t hi = lo + slice < n ? lo + slice : n;
+  const int m = hi > lo ? static_cast<int>(hi - lo) : 0;
+  for (int i = tid; i < m; i += kSelThreads) {
+    keys[i] = order_key(scores[lo + i]);
+    flags[i] = base[lo + i] != 0;
+  }
+  uint32_t prefix = 0, pmask = 0;
+  int64_t krem = k;
+  if (k > 0) {
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      uint32_t* root_hist = cluster.map_shared_rank(&hist[pass & 1][0], 0);
+      if (tid < 256) {
+        local[tid] = 0;
+        if (rank == 0) hist[pass & 1][tid] = 0;
+      }
+      if (tid == 0) {
+        s_digit = 0;  // see select_topk_kernel: degrades safely if k > #candidates
+        s_above = 0;
+      }
+      cluster.sync();
+      for (int i = tid; i < m; i += kSelThreads) {
+        const uint32_t key = keys[i];
+        if (!flags[i] && (key & pmask) == prefix) atomicAdd(&local[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid < 256 && local[tid]) atomicAdd(&root_hist[tid], local[tid]);
+      cluster.sync();
+      if (tid < 32) find_digit(root_hist, krem, &s_digit, &s_above);
+      __syncthreads();
+      prefix |= s_digit << shift;
+      pmask |= 255u << shift;
+      krem -= s_above;
+      __syncthreads();  // all threads read s_digit before the next pass resets it
+    }
+  }
+  const uint32_t thr = prefix;
+  const int64_t k_eq = k > 0 ? krem : 0;
+  const bool any = k > 0;
+  const int per = (m + kSelThreads - 1) / kSelThreads;
+  const int a0 = per * tid < m ? per * tid : m;
+  const int a1 = a0 + per < m ? a0 + per : m;
+  int64_t c_sel = 0, c_eq = 0;
+  for (int i = a0; i < a1; ++i) {
+    if (flags[i]) {
+      ++c_sel;
+    } else if (any) {
+      if (keys[i] > thr)
+        ++c_sel;
+      else if (keys[i] == thr)
+        ++c_eq;
+    }
+  }
+  int64_t sel_total, eq_total;
+  int64_t sel_before = block_exclusive_scan(c_sel, warp_sums, sel_total);
+  int64_t eq_before = block_exclusive_scan(c_eq, warp_sums, eq_total);
+  if (tid == 0) {
+    totals[0] = sel_total;
+    totals[1] = eq_total;
+  }
+  cluster.sync();
+  int64_t sel_off = 0, eq_off = 0;
+  for (int r = 0; r < rank; ++r) {
+    const int64_t* other = cluster.map_shared_rank(totals, r);
+    sel_off += other[0];
+    eq_off += other[1];
+  }
+  cluster.sync();  // no CTA may leave while a peer still reads its totals
+  sel_before += sel_off;
+  eq_before += eq_off;
+  for (int i = a0; i < a1; ++i) {
+    const int64_t index = lo + i;
+    if (flags[i] || (any && keys[i] > thr)) {
+      const int64_t pos = sel_before + (eq_before < k_eq ? eq_before : k_eq);
+      if (pos < cap) out[pos] = index;
+      ++sel_before;
+    } else if (any && keys[i] == thr) {
+      if (eq_before < k_eq && sel_before + eq_before < cap) out[sel_before + eq_before] = index;
+      ++eq_before;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace cb
 
@@ -307,7 +453,37 @@ extern "C" int cb_select_topk(const float* scores, const uint8_t* base_mask, int
   CB_REQUIRE(n >= 0 && k >= 0 && k <= n && out_capacity >= 0, "bad n/k");
   if (n == 0 || out_capacity == 0) return CB_OK;
   CB_REQUIRE(scores && base_mask && out_index, "null pointer argument");
-  select_topk_kernel<<<1, kSelThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      scores, base_mask, n, k, out_index, out_capacity);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n <= (int64_t)kClusterCtas * kMaxSlice) {
+    const int slice = static_cast<int>((n + kClusterCtas - 1) / kClusterCtas);
+    const size_t dyn = ((size_t)slice * 5 + 15) / 16 * 16;
+    cudaError_t e = cudaFuncSetAttribute(select_cluster_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(dyn));
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+      return CB_ERR_CUDA;
+    }
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(kClusterCtas, 1, 1);
+    config.blockDim = dim3(kSelThreads, 1, 1);
+    config.dynamicSmemBytes = dyn;
+    config.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kClusterCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    e = cudaLaunchKernelEx(&config, select_cluster_kernel, scores, base_mask, n, k, out_index,
+                           out_capacity, slice);
+    if (e != cudaSuccess) {
+      set_error("cb_select_topk cluster launch failed: %s", cudaGetErrorString(e));
+      return CB_ERR_CUDA;
+    }
+    return launch_status("cb_select_topk");
+  }
+  select_topk_kernel<<<1, kSelThreads, 0, s>>>(scores, base_mask, n, k, out_index, out_capacity);
   return launch_status("cb_select_topk");
 }
