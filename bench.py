@@ -73,6 +73,9 @@ class Shape:
     ratio: float
 
 
+SPARSE_Q_CONFIG = {"name": "qwen3-30b-a3b-98k-sparse_q", "layers": 48, "q_heads": 32, "kv_heads": 4,
+                   "head_dim": 128, "tokens": 98304, "query_chunks": 16, "check_layer": 6}
+
 CONFIGS = {
     1: Shape("qwen3-0.6b-cpu-plumbing", 28, 8, 16, 128, 4096, 256, 12, 16, 2048, 40960, 1e6, 1, 0.15),
     2: Shape("qwen3-8b-32k-kv_deviation", 36, 8, 32, 128, 32768, 256, 89, 16, 2304, 40960, 1e6, 1, 0.15),
@@ -574,13 +577,73 @@ def run_reference(args, shape: Shape, world: int, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
+    """Config 3: Sparse-Q scoring at the boundary layer (tensor-core bound)."""
+    from cacheblend_b200.selection import select_tokens, sparse_q_key_mass, sparse_q_masks
+
+    cfg = SPARSE_Q_CONFIG
+    device = torch.device("cuda", local)
+    hq, hkv = cfg["q_heads"] // world, cfg["kv_heads"] // world
+    ctx = cfg["tokens"] - 1  # the last prompt token stays with vLLM (connector.py:664-673)
+    rng = np.random.default_rng(3)
+    gen = torch.Generator(device=device).manual_seed(30 + rank)
+    chunks = rng.choice(ctx // 256, size=cfg["query_chunks"] - 1, replace=False)
+    positions = np.sort(np.concatenate([c * 256 + np.arange(256) for c in chunks]
+                                       + [np.arange((ctx // 256) * 256, ctx)]))
+    key = torch.randn(ctx, hkv, 128, generator=gen, device=device).to(torch.bfloat16)
+    query = torch.randn(ctx, hq, 128, generator=gen, device=device).to(torch.bfloat16)
+    gaps = np.zeros(ctx, dtype=bool)
+    gaps[positions] = True
+    qmask, forced, _ = sparse_q_masks(gaps, 16, 1, 64)
+    rows = np.flatnonzero(qmask)
+    workspace = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    error = torch.zeros(1, dtype=torch.int32, device=device)
+    scale = 128 ** -0.5
+    flops = float(sum(2 * 128 * cfg["q_heads"] * (int(p) + 1) for p in positions)) / world
+
+    def step():
+        mass = sparse_q_key_mass(query, key, rows, positions, scale, workspace=workspace, device_error=error)
+        if world > 1:
+            torch.distributed.all_reduce(mass)
+        return select_tokens(mass, gaps, 0.15, forced)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    achieved = flops / (ms / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "metric": "sparse-q scored span tokens/s (boundary layer, TP-sharded)", "value": ctx / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": cfg["name"], "keys": ctx, "queries": int(positions.size),
+                       "q_heads_per_rank": hq, "kv_heads_per_rank": hkv},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "flops_note": "one causal QK^T counted once (two passes run)"},
+            "device_error": int(error.item()), "clocks": clocks.summary(),
+        }), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
+    parser.add_argument("--config", type=int, choices=sorted(CONFIGS) + [3], default=2)
     parser.add_argument("--e2e-steps", type=int, default=5)
     parser.add_argument("--sample-layers", type=int, default=2)
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -590,6 +653,12 @@ def main() -> None:
     parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
                         help="host->device mode of the e2e loader (CACHEBLEND_B200_LOAD)")
     args = parser.parse_args()
+    if args.config == 3:
+        world, rank, local, group = dist_setup(args)
+        sparse_q_bench(args, world, rank, local)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     shape = CONFIGS[args.config]
     if args.layers:
         from dataclasses import replace

@@ -186,6 +186,37 @@ CB_API int cb_kv_deviation(const void* fresh, int64_t fresh_row_stride,
 CB_API int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t n, int64_t k,
                    int64_t* out_index, int64_t out_capacity, void* stream);
 
+/*
+ * Workspace bytes cb_sparse_q_scores needs for `num_queries` sparse queries
+ * (dense per-KV-head query rows, per-row log-sum-exp, row positions, tile
+ * position bounds).  head_size must be 128, dtype bf16 or fp16, and the query
+ * heads a multiple of the KV heads with (q heads / KV heads) dividing 128.
+ */
+CB_API int cb_sparse_q_workspace_size(int64_t num_queries, int64_t num_q_heads,
+                               int64_t num_kv_heads, int64_t head_size, int dtype,
+                               int64_t* bytes);
+
+/*
+ * Sparse-Q attention mass per key (Qwen3BlendExecutor._sparse_q_scores,
+ * cacheblend_vllm/ascend.py:638-711, the score part): for every KV head,
+ * query group head and sparse query i (query row query_rows[i] of `query`,
+ * position query_positions[i]) the causal softmax over keys 0..position of
+ * round_dtype(q . k) * scale is added into scores[key] (fp32, [num_keys]).
+ * query: [tokens, num_q_heads, 128] rows `query_token_stride` bytes apart;
+ * key: [num_keys, num_kv_heads, 128] rows `key_token_stride` bytes apart.
+ * Positions must lie in [0, num_keys).  Runs on the tcgen05 tensor cores in
+ * two passes (row log-sum-exp, then per-key mass); `workspace` (1 KiB
+ * aligned, device memory, cb_sparse_q_workspace_size bytes) holds the
+ * intermediate state.  Pipeline waits are bounded (2 s); a timeout stores a
+ * nonzero code into *device_error (nullable).
+ */
+CB_API int cb_sparse_q_scores(const void* query, int64_t query_token_stride, const void* key,
+                       int64_t key_token_stride, int64_t num_keys, int64_t num_q_heads,
+                       int64_t num_kv_heads, int64_t head_size, int dtype,
+                       const int64_t* query_rows, const int64_t* query_positions,
+                       int64_t num_queries, float scale, float* scores, void* workspace,
+                       int64_t workspace_bytes, int32_t* device_error, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,6 +15,8 @@
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -192,3 +194,109 @@ def sparse_q_masks(
         right = np.clip(index + radius + 1, None, gaps.shape[0])
         forced |= counts[right] > counts[left]
     return query, forced, not has_gap
+
+
+def sparse_q_workspace_bytes(num_queries: int, num_q_heads: int, num_kv_heads: int,
+                             head_size: int, dtype: torch.dtype) -> int:
+    out = ctypes.c_int64(0)
+    _native.call(
+        "cb_sparse_q_workspace_size", num_queries, num_q_heads, num_kv_heads, head_size,
+        _native.dtype_code(dtype), ctypes.addressof(out),
+    )
+    return int(out.value)
+
+
+def sparse_q_key_mass(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    query_rows: np.ndarray,
+    query_positions: np.ndarray,
+    scale: float,
+    workspace: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> torch.Tensor:
+    """fp32 [num_keys] attention mass per key from the given sparse queries (cb_sparse_q_scores)."""
+    _native.require_cuda(query, key)
+    if query.ndim != 3 or key.ndim != 3:
+        raise ValueError("query must be [tokens, q_heads, head] and key [keys, kv_heads, head]")
+    if query.dtype != key.dtype:
+        raise ValueError("query and key must share a dtype (one tcgen05 operand type)")
+    if query.stride(-1) != 1 or query.stride(-2) != query.shape[-1]:
+        raise ValueError("query heads must be contiguous")
+    if key.stride(-1) != 1 or key.stride(-2) != key.shape[-1]:
+        raise ValueError("key heads must be contiguous")
+    rows = np.ascontiguousarray(query_rows, dtype=np.int64)
+    positions = np.ascontiguousarray(query_positions, dtype=np.int64)
+    num_keys = key.shape[0]
+    if rows.shape != positions.shape:
+        raise ValueError("one position per query row is required")
+    if rows.size and (rows.min() < 0 or rows.max() >= query.shape[0]):
+        raise IndexError("query row out of range")
+    if positions.size and (positions.min() < 0 or positions.max() >= num_keys):
+        raise IndexError("query position outside the key context")
+    num_q_heads, head = query.shape[1], query.shape[2]
+    num_kv_heads = key.shape[1]
+    needed = sparse_q_workspace_bytes(rows.size, num_q_heads, num_kv_heads, head, query.dtype)
+    if workspace is None or workspace.numel() < needed:
+        workspace = torch.empty(needed + 1024, dtype=torch.uint8, device=query.device)
+    base = workspace.data_ptr()
+    aligned = (base + 1023) // 1024 * 1024
+    usable = workspace.numel() - (aligned - base)
+    scores = torch.empty(num_keys, dtype=torch.float32, device=query.device)
+    rows_dev = torch.from_numpy(rows).to(query.device, non_blocking=True)
+    pos_dev = torch.from_numpy(positions).to(query.device, non_blocking=True)
+    esize = query.element_size()
+    _native.call(
+        "cb_sparse_q_scores",
+        query.data_ptr(), query.stride(0) * esize, key.data_ptr(), key.stride(0) * esize, num_keys,
+        num_q_heads, num_kv_heads, head, _native.dtype_code(query.dtype), rows_dev.data_ptr(),
+        pos_dev.data_ptr(), rows.size, float(scale), scores.data_ptr(), aligned, usable,
+        0 if device_error is None else device_error.data_ptr(), _native.stream_handle(stream),
+    )
+    return scores
+
+
+def sparse_q_scores(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    absolute_indices: torch.Tensor | np.ndarray,
+    gap_mask: torch.Tensor | np.ndarray,
+    scale: float,
+    block_size: int,
+    overflow_blocks: int,
+    tail_query_tokens: int,
+    device_error: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor, dict[str, int | bool]]:
+    """``_sparse_q_scores`` (ascend.py:638-711): scores of the active tokens, forced mask, stats.
+
+    ``query_score_chunk_size`` only bounded the reference's temporary tensor;
+    the tensor-core kernel streams keys through TMEM and never materialises a
+    [queries, context] tensor, so it has no chunk parameter.
+    """
+    gaps = _as_host_mask(gap_mask, "gap_mask")
+    absolute = (
+        absolute_indices.astype(np.int64, copy=False)
+        if isinstance(absolute_indices, np.ndarray)
+        else absolute_indices.detach().to("cpu", torch.long).numpy()
+    )
+    if gaps.shape[0] != query.shape[0] or absolute.shape[0] != query.shape[0]:
+        raise ValueError("gap mask and absolute indices must match the active tokens")
+    query_mask, forced, tail_fallback = sparse_q_masks(
+        gaps, block_size, overflow_blocks, tail_query_tokens
+    )
+    rows = np.flatnonzero(query_mask)
+    full = sparse_q_key_mass(query, key, rows, absolute[rows], scale, device_error=device_error)
+    index = torch.from_numpy(absolute).to(query.device, non_blocking=True)
+    scores = full.index_select(0, index)
+    gap_count = int(gaps.sum())
+    stats = {
+        "active_tokens": int(query.shape[0]),
+        "gap_tokens": gap_count,
+        "cached_tokens": int(query.shape[0]) - gap_count,
+        "sparse_query_tokens": int(rows.size),
+        "tail_fallback": tail_fallback,
+        "overflow_blocks": overflow_blocks,
+    }
+    forced_dev = torch.from_numpy(forced).to(query.device, non_blocking=True)
+    return scores, forced_dev, stats

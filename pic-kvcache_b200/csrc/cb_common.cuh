@@ -126,6 +126,14 @@ inline int dtype_bytes(int dtype) {
     }                                 \
   } while (0)
 
+#define CB_SUPPORTED(cond, ...)       \
+  do {                                \
+    if (!(cond)) {                    \
+      ::cb::set_error(__VA_ARGS__);   \
+      return CB_ERR_UNSUPPORTED;      \
+    }                                 \
+  } while (0)
+
 #define CB_BIND(stream, device_ptr)                         \
   do {                                                      \
     int _cb_rc = ::cb::bind_stream((stream), (device_ptr)); \

@@ -1,0 +1,832 @@
+// K4: Sparse-Q attention-mass scorer on the 5th-generation tensor cores.
+//
+// Semantics: Qwen3BlendExecutor._sparse_q_scores (cacheblend_vllm/ascend.py:638-711).
+// For every KV head h, group g and sparse query q at position pos_q, and every key
+// k <= pos_q:   s = round_T(q . k) * scale   (T = bf16/fp16: the matmul output dtype)
+//               p = softmax_k(s)             (fp32)
+//               mass[k] += p
+// summed over heads, groups and queries.  Keys beyond pos_q are masked (their
+// exp is exactly 0 in the reference).
+//
+// Layout: rows = (query, group) pairs of one KV head, r = qi * groups + g, in
+// 128-row tiles; keys in 128-key tiles.  Two passes over the causal tiles:
+//   pass 1  S  = Q K^T in TMEM (lane = row): per-row online max/sum in the log2
+//           domain -> lse2[h][r] = m + log2(l)   (workspace)
+//   pass 2  S' = K Q^T in TMEM (lane = key): each thread owns one key and sums
+//           exp2(round_T(s') * scale*log2e - lse2[row]) over the rows of every
+//           query tile -> one fp32 store per key, no atomics.
+// Each CTA (persistent, one per SM) is warp-specialized: warp 0 issues TMA
+// tensor loads (128x64 boxes, SWIZZLE_128B, no cluster features), warp 1 lane 0
+// issues tcgen05.mma (M=128, N=128, K=16 x 8) into one of two TMEM
+// accumulators, warp 2 owns the TMEM allocation, warps 4-7 are the softmax /
+// accumulation warpgroup reading TMEM with tcgen05.ld.  Every mbarrier wait is
+// bounded (2 s); a wait that runs out records a code in *device_error, the CTA
+// drains its MMAs and TMA loads, frees TMEM and returns.
+#include <cuda.h>  // CUtensorMap types; the encoder is fetched through the runtime
+
+#include <type_traits>
+
+#include "cb_common.cuh"
+
+namespace cb {
+namespace sq {
+
+constexpr int kTile = 128;            // rows / keys per tile
+constexpr int kHead = 128;            // head_size handled by the kernels (elements)
+constexpr int kHalfBytes = kTile * 64 * 2;  // one 128x64 16-bit SW128 box
+constexpr int kTileBytes = 2 * kHalfBytes;  // 32 KiB: a full 128x128 operand
+constexpr int kStages = 3;            // streamed-operand ring
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 256;   // two 128-column fp32 accumulators
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Single-thread bounded wait (producer / MMA lanes).
+__device__ __forceinline__ bool wait1(uint64_t* bar, uint32_t parity) {
+  uint64_t start = 0;
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try(bar, parity)) return true;
+    if ((spin & 255u) == 0) {
+      const uint64_t now = global_ns();
+      if (start == 0)
+        start = now;
+      else if (now - start > kTimeoutNs)
+        return false;
+    }
+  }
+}
+// Warp-uniform bounded wait (epilogue warps).
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity) {
+  uint64_t start = 0;
+  const int lane = threadIdx.x & 31;
+  for (uint32_t spin = 0;; ++spin) {
+    const bool mine = mbar_try(bar, parity);
+    if (__all_sync(0xffffffffu, mine)) return true;
+    if ((spin & 255u) == 0) {
+      int expired = 0;
+      if (lane == 0) {
+        const uint64_t now = global_ns();
+        if (start == 0)
+          start = now;
+        else if (now - start > kTimeoutNs)
+          expired = 1;
+      }
+      if (__shfl_sync(0xffffffffu, expired, 0)) return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(void* smem, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* smem, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// K-major, SWIZZLE_128B shared-memory matrix descriptor (sm_100 format):
+// start>>4 | LBO(16 B)>>4 << 16 | SBO(1024 B = 8 rows x 128 B)>>4 << 32 |
+// version 1 << 46 | layout SWIZZLE_128B (2) << 61.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+  return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+// K step kk (16 elements = 32 B) of a 128x128 operand stored as two 128x64
+// SW128 halves 16 KiB apart.
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile_addr, int kk) {
+  return sw128_desc(tile_addr + (kk >> 2) * kHalfBytes + (kk & 3) * 32);
+}
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// 32 lanes x 32 consecutive fp32 columns of this warp's TMEM sub-partition.
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(addr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// fp32 accumulator value rounded to the 16-bit matmul output type and widened.
+template <typename T>
+__device__ __forceinline__ float round_logit(uint32_t bits) {
+  return Elem<T>::to_f(Elem<T>::from_f(__uint_as_float(bits)));
+}
+
+// Instruction descriptor: D f32 (bits 4-5 = 1), A and B bf16 (1) or f16 (0)
+// in bits 7-9 / 10-12, both K-major (bits 15, 16 = 0), N>>3 in bits 17-22,
+// M>>4 in bits 24-28; M = N = 128.
+template <typename T>
+__host__ __device__ constexpr uint32_t instr_desc() {
+  constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(kTile >> 3) << 17) |
+         ((uint32_t)(kTile >> 4) << 24);
+}
+
+struct Shared {
+  // operand buffers live in dynamic shared memory (1024-B aligned), barriers here
+  uint64_t a_full[2], a_empty[2];
+  uint64_t b_full[kStages], b_empty[kStages];
+  uint64_t t_full[2], t_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct Common {
+  int num_kv_heads;
+  int groups;
+  int rows_pad;        // padded rows per KV head
+  int q_tiles;         // rows_pad / 128
+  int k_tiles;         // ceil(num_keys / 128)
+  int64_t num_keys;
+  float scale_log2;    // scale * log2(e)
+  const int32_t* row_pos;   // [rows_pad]: position of each row, -1 for padding
+  const int32_t* tile_max;  // [q_tiles]
+  const int32_t* tile_min;  // [q_tiles]
+  float* lse;               // [num_kv_heads][rows_pad] (pass 1 out, pass 2 in)
+  float* scores;            // [num_keys] (pass 2 out)
+  int32_t* error;
+};
+
+__device__ __forceinline__ void report(const Common& c, Shared& sh, int code) {
+  if (c.error != nullptr) atomicCAS(c.error, 0, code);
+  *reinterpret_cast<volatile int*>(&sh.abort) = 1;
+}
+
+__device__ __forceinline__ bool aborted(Shared& sh) {
+  return *reinterpret_cast<volatile int*>(&sh.abort) != 0;
+}
+
+// Setup shared by both passes: barriers + TMEM allocation.
+__device__ __forceinline__ void setup(Shared& sh, int warp, int a_empty_count, int b_empty_count) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.a_full[i], 1);
+      mbar_init(&sh.a_empty[i], a_empty_count);
+      mbar_init(&sh.t_full[i], 1);
+      mbar_init(&sh.t_empty[i], 4);  // one arrive per epilogue warp
+    }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sh.b_full[s], 1);
+      mbar_init(&sh.b_empty[s], b_empty_count);
+    }
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sh.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+__device__ __forceinline__ void teardown(Shared& sh, int warp) {
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sh.tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// MMA issuer drain: wait until every MMA this thread issued has completed.
+__device__ __forceinline__ void drain_mma(Shared& sh) {
+  umma_commit(&sh.drain);
+  wait1(&sh.drain, 0);
+}
+
+// ============================================================ pass 1: row LSE
+// items: (h, qt) with qt descending (later queries see more keys).
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    lse_pass_kernel(const __grid_constant__ CUtensorMap q_map,
+                    const __grid_constant__ CUtensorMap k_map, Common c) {
+  extern __shared__ __align__(1024) unsigned char dyn[];
+  __shared__ Shared sh;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dyn) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* a_buf = base;                   // 2 x Q tiles
+  unsigned char* b_buf = base + 2 * kTileBytes;  // kStages x K tiles
+  setup(sh, warp, 1, 1);
+  const int items = c.num_kv_heads * c.q_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int t = 0, it = 0;
+      int armed[kStages];
+      for (int s = 0; s < kStages; ++s) armed[s] = -1;
+      int a_armed[2] = {-1, -1};
+      for (int item = blockIdx.x; item < items && !aborted(sh); item += gridDim.x, ++it) {
+        const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+        const int h = item % c.num_kv_heads;
+        const int ab = it & 1;
+        if (!wait1(&sh.a_empty[ab], ((it >> 1) & 1) ^ 1)) { report(c, sh, 1); break; }
+        mbar_expect_tx(&sh.a_full[ab], kTileBytes);
+        tma_load_3d(a_buf + ab * kTileBytes, &q_map, &sh.a_full[ab], 0, qt * kTile, h);
+        tma_load_3d(a_buf + ab * kTileBytes + kHalfBytes, &q_map, &sh.a_full[ab], 64, qt * kTile, h);
+        a_armed[ab] = (it >> 1) & 1;
+        const int kt_end = min(c.tile_max[qt] / kTile, c.k_tiles - 1);  // tile_max >= 0 here
+        for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+          const int s = t % kStages;
+          if (!wait1(&sh.b_empty[s], ((t / kStages) & 1) ^ 1)) { report(c, sh, 1); break; }
+          mbar_expect_tx(&sh.b_full[s], kTileBytes);
+          tma_load_3d(b_buf + s * kTileBytes, &k_map, &sh.b_full[s], 0, h, kt * kTile);
+          tma_load_3d(b_buf + s * kTileBytes + kHalfBytes, &k_map, &sh.b_full[s], 64, h, kt * kTile);
+          armed[s] = (t / kStages) & 1;
+        }
+      }
+      // drain: every armed load has landed before the CTA may exit
+      for (int s = 0; s < kStages; ++s)
+        if (armed[s] >= 0) wait1(&sh.b_full[s], armed[s]);
+      for (int i = 0; i < 2; ++i)
+        if (a_armed[i] >= 0) wait1(&sh.a_full[i], a_armed[i]);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc<T>();
+      const uint32_t a_addr = smem_u32(a_buf);
+      const uint32_t b_addr = smem_u32(b_buf);
+      int t = 0, it = 0;
+      for (int item = blockIdx.x; item < items && !aborted(sh); item += gridDim.x, ++it) {
+        const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+        const int ab = it & 1;
+        if (!wait1(&sh.a_full[ab], (it >> 1) & 1)) { report(c, sh, 2); break; }
+        const int kt_end = min(c.tile_max[qt] / kTile, c.k_tiles - 1);
+        bool ok = true;
+        for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+          const int s = t % kStages;
+          const int tb = t & 1;
+          if (!wait1(&sh.b_full[s], (t / kStages) & 1) ||
+              !wait1(&sh.t_empty[tb], ((t >> 1) & 1) ^ 1)) {
+            report(c, sh, 2);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = sh.tmem_base + tb * kTile;
+#pragma unroll
+          for (int kk = 0; kk < kHead / 16; ++kk)
+            umma(d, operand_desc(a_addr + ab * kTileBytes, kk),
+                 operand_desc(b_addr + s * kTileBytes, kk), idesc, kk > 0);
+          umma_commit(&sh.b_empty[s]);
+          umma_commit(&sh.t_full[tb]);
+        }
+        umma_commit(&sh.a_empty[ab]);
+        if (!ok) break;
+      }
+      drain_mma(sh);
+    }
+  } else if (warp >= 4) {
+    const int ew = warp - 4;             // TMEM lanes 32*ew .. +31
+    const int row_in_tile = ew * 32 + lane;
+    int t = 0;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+      const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+      const int h = item % c.num_kv_heads;
+      const int r = qt * kTile + row_in_tile;
+      const int pos = c.row_pos[r];
+      const int kt_end = min(c.tile_max[qt] / kTile, c.k_tiles - 1);
+      float m = -INFINITY, l = 0.0f;
+      bool ok = true;
+      for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+        const int tb = t & 1;
+        if (!wait_warp(&sh.t_full[tb], (t >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t v[4][32];
+        const uint32_t addr = sh.tmem_base + tb * kTile + (static_cast<uint32_t>(ew * 32) << 16);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld32(addr + q * 32, v[q]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
+        // columns [0, valid) of this tile are keys <= pos
+        const int valid = min(max(pos - kt * kTile + 1, 0), kTile);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (q * 32 >= valid) break;
+          float x[32];
+          float cmax = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            x[j] = (q * 32 + j < valid) ? round_logit<T>(v[q][j]) * c.scale_log2 : -INFINITY;
+            cmax = fmaxf(cmax, x[j]);
+          }
+          const float m_new = fmaxf(m, cmax);
+          float sum = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum += ex2(x[j] - m_new);
+          l = l * ex2(m - m_new) + sum;
+          m = m_new;
+        }
+      }
+      if (!ok) {
+        if (lane == 0) report(c, sh, 3);
+        break;
+      }
+      c.lse[(int64_t)h * c.rows_pad + r] = (l > 0.0f) ? m + lg2(l) : INFINITY;
+    }
+  }
+  teardown(sh, warp);
+}
+
+// ============================================================ pass 2: key mass
+// items: key tiles kt ascending (earlier keys are seen by more queries).
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    mass_pass_kernel(const __grid_constant__ CUtensorMap q_map,
+                     const __grid_constant__ CUtensorMap k_map, Common c) {
+  extern __shared__ __align__(1024) unsigned char dyn[];
+  __shared__ Shared sh;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dyn) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* a_buf = base;                   // 2 x K tiles
+  unsigned char* b_buf = base + 2 * kTileBytes;  // kStages x (Q tile)
+  float* side = reinterpret_cast<float*>(b_buf + kStages * kTileBytes);  // per stage: lse[128], pos[128]
+  // b_empty: the MMA commit + the four epilogue warps (they read lse/pos)
+  setup(sh, warp, 1, 1 + 4);
+  const int items = c.k_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int t = 0, it = 0;
+      int armed[kStages];
+      for (int s = 0; s < kStages; ++s) armed[s] = -1;
+      int a_armed[2] = {-1, -1};
+      for (int kt = blockIdx.x; kt < items && !aborted(sh); kt += gridDim.x) {
+        for (int h = 0; h < c.num_kv_heads && !aborted(sh); ++h, ++it) {
+          const int ab = it & 1;
+          if (!wait1(&sh.a_empty[ab], ((it >> 1) & 1) ^ 1)) { report(c, sh, 1); break; }
+          mbar_expect_tx(&sh.a_full[ab], kTileBytes);
+          tma_load_3d(a_buf + ab * kTileBytes, &k_map, &sh.a_full[ab], 0, h, kt * kTile);
+          tma_load_3d(a_buf + ab * kTileBytes + kHalfBytes, &k_map, &sh.a_full[ab], 64, h, kt * kTile);
+          a_armed[ab] = (it >> 1) & 1;
+          for (int qt = 0; qt < c.q_tiles; ++qt) {
+            if (c.tile_max[qt] < kt * kTile) continue;  // no row of this tile sees these keys
+            const int s = t % kStages;
+            if (!wait1(&sh.b_empty[s], ((t / kStages) & 1) ^ 1)) { report(c, sh, 1); break; }
+            mbar_expect_tx(&sh.b_full[s], kTileBytes + 2 * kTile * 4);
+            tma_load_3d(b_buf + s * kTileBytes, &q_map, &sh.b_full[s], 0, qt * kTile, h);
+            tma_load_3d(b_buf + s * kTileBytes + kHalfBytes, &q_map, &sh.b_full[s], 64, qt * kTile, h);
+            bulk_load(side + s * 2 * kTile, c.lse + (int64_t)h * c.rows_pad + qt * kTile, kTile * 4,
+                      &sh.b_full[s]);
+            bulk_load(side + s * 2 * kTile + kTile, c.row_pos + qt * kTile, kTile * 4, &sh.b_full[s]);
+            armed[s] = (t / kStages) & 1;
+            ++t;
+          }
+        }
+      }
+      for (int s = 0; s < kStages; ++s)
+        if (armed[s] >= 0) wait1(&sh.b_full[s], armed[s]);
+      for (int i = 0; i < 2; ++i)
+        if (a_armed[i] >= 0) wait1(&sh.a_full[i], a_armed[i]);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc<T>();
+      const uint32_t a_addr = smem_u32(a_buf);
+      const uint32_t b_addr = smem_u32(b_buf);
+      int t = 0, it = 0;
+      bool ok = true;
+      for (int kt = blockIdx.x; kt < items && ok && !aborted(sh); kt += gridDim.x) {
+        for (int h = 0; h < c.num_kv_heads && ok; ++h, ++it) {
+          const int ab = it & 1;
+          if (!wait1(&sh.a_full[ab], (it >> 1) & 1)) { report(c, sh, 2); ok = false; break; }
+          for (int qt = 0; qt < c.q_tiles; ++qt) {
+            if (c.tile_max[qt] < kt * kTile) continue;
+            const int s = t % kStages;
+            const int tb = t & 1;
+            if (!wait1(&sh.b_full[s], (t / kStages) & 1) ||
+                !wait1(&sh.t_empty[tb], ((t >> 1) & 1) ^ 1)) {
+              report(c, sh, 2);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = sh.tmem_base + tb * kTile;
+#pragma unroll
+            for (int kk = 0; kk < kHead / 16; ++kk)
+              umma(d, operand_desc(a_addr + ab * kTileBytes, kk),
+                   operand_desc(b_addr + s * kTileBytes, kk), idesc, kk > 0);
+            umma_commit(&sh.b_empty[s]);
+            umma_commit(&sh.t_full[tb]);
+            ++t;
+          }
+          umma_commit(&sh.a_empty[ab]);
+        }
+      }
+      drain_mma(sh);
+    }
+  } else if (warp >= 4) {
+    const int ew = warp - 4;
+    const int key_in_tile = ew * 32 + lane;
+    int t = 0;
+    bool ok = true;
+    for (int kt = blockIdx.x; kt < items && ok; kt += gridDim.x) {
+      const int key = kt * kTile + key_in_tile;
+      float acc = 0.0f;
+      for (int h = 0; h < c.num_kv_heads && ok; ++h) {
+        for (int qt = 0; qt < c.q_tiles; ++qt) {
+          if (c.tile_max[qt] < kt * kTile) continue;
+          const int s = t % kStages;
+          const int tb = t & 1;
+          if (!wait_warp(&sh.b_full[s], (t / kStages) & 1) ||
+              !wait_warp(&sh.t_full[tb], (t >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t v[4][32];
+          const uint32_t addr = sh.tmem_base + tb * kTile + (static_cast<uint32_t>(ew * 32) << 16);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_ld32(addr + q * 32, v[q]);
+          tmem_wait_ld();
+          tc_fence_before();
+          const float4* lse4 = reinterpret_cast<const float4*>(side + s * 2 * kTile);
+          const int4* pos4 = reinterpret_cast<const int4*>(side + s * 2 * kTile + kTile);
+          if (key <= c.tile_min[qt]) {
+            // every row of the tile sees this key: no mask
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+#pragma unroll
+              for (int j4 = 0; j4 < 8; ++j4) {
+                const float4 l4 = lse4[q * 8 + j4];
+                const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  acc += ex2(fmaf(round_logit<T>(v[q][j4 * 4 + e]), c.scale_log2, -lv[e]));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+#pragma unroll
+              for (int j4 = 0; j4 < 8; ++j4) {
+                const float4 l4 = lse4[q * 8 + j4];
+                const int4 p4 = pos4[q * 8 + j4];
+                const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+                const int pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float p = ex2(fmaf(round_logit<T>(v[q][j4 * 4 + e]), c.scale_log2, -lv[e]));
+                  acc += key <= pv[e] ? p : 0.0f;
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&sh.t_empty[tb]);
+            mbar_arrive(&sh.b_empty[s]);
+          }
+          ++t;
+        }
+      }
+      if (ok && key < c.num_keys) c.scores[key] = acc;
+    }
+    if (!ok && lane == 0) report(c, sh, 3);
+  }
+  teardown(sh, warp);
+}
+
+// ============================================================ prep
+// Dense per-KV-head query rows: qd[h][qi*groups+g][:] = query[rows[qi]][h*groups+g][:],
+// zero rows up to rows_pad; row positions; per-tile position bounds.
+__global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ query,
+                                                   int64_t query_token_stride,
+                                                   const int64_t* __restrict__ rows,
+                                                   const int64_t* __restrict__ positions,
+                                                   int64_t num_queries, int num_kv_heads, int groups,
+                                                   int rows_pad, int head_bytes, char* __restrict__ qd,
+                                                   int32_t* __restrict__ row_pos,
+                                                   int32_t* __restrict__ tile_max,
+                                                   int32_t* __restrict__ tile_min) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t total = static_cast<int64_t>(num_kv_heads) * rows_pad;
+  const int units = head_bytes / 16;
+  for (int64_t task = warp; task < total; task += nwarps) {
+    const int h = static_cast<int>(task / rows_pad);
+    const int r = static_cast<int>(task - (int64_t)h * rows_pad);
+    const int64_t qi = r / groups;
+    const int g = r - static_cast<int>(qi) * groups;
+    uint4* dst = reinterpret_cast<uint4*>(qd + task * head_bytes);
+    if (qi < num_queries) {
+      const uint4* src = reinterpret_cast<const uint4*>(
+          query + rows[qi] * query_token_stride + (int64_t)(h * groups + g) * head_bytes);
+      for (int u = lane; u < units; u += 32) dst[u] = src[u];
+    } else {
+      for (int u = lane; u < units; u += 32) dst[u] = make_uint4(0, 0, 0, 0);
+    }
+    if (h == 0 && lane == 0) row_pos[r] = qi < num_queries ? static_cast<int32_t>(positions[qi]) : -1;
+  }
+  // tile bounds: one warp per query tile
+  const int q_tiles = rows_pad / kTile;
+  for (int64_t qt = warp; qt < q_tiles; qt += nwarps) {
+    int mx = -1, mn = 0x7fffffff;
+    for (int r = lane; r < kTile; r += 32) {
+      const int64_t qi = (qt * kTile + r) / groups;
+      const int p = qi < num_queries ? static_cast<int>(positions[qi]) : -1;
+      mx = max(mx, p);
+      mn = min(mn, p);  // padding (-1) makes the tile "partially visible": always masked
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    }
+    if (lane == 0) {
+      tile_max[qt] = mx;
+      tile_min[qt] = mn;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+struct Workspace {
+  size_t qd, lse, row_pos, tile_max, tile_min, total;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+Workspace layout(int64_t num_queries, int64_t num_q_heads, int64_t num_kv_heads, int esize) {
+  const int64_t groups = num_q_heads / num_kv_heads;
+  const int64_t rows = num_queries * groups;
+  const int64_t rows_pad = (rows + kTile - 1) / kTile * kTile;
+  const int64_t q_tiles = rows_pad / kTile;
+  Workspace w{};
+  size_t off = 0;
+  w.qd = off;
+  off = align_up(off + (size_t)num_kv_heads * rows_pad * kHead * esize, 1024);
+  w.lse = off;
+  off = align_up(off + (size_t)num_kv_heads * rows_pad * 4, 1024);
+  w.row_pos = off;
+  off = align_up(off + (size_t)rows_pad * 4, 256);
+  w.tile_max = off;
+  off = align_up(off + (size_t)q_tiles * 4, 256);
+  w.tile_min = off;
+  off = align_up(off + (size_t)q_tiles * 4, 256);
+  w.total = off;
+  return w;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encoder(EncodeTiled* fn) {
+  void* ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || ptr == nullptr) {
+    set_error("cuTensorMapEncodeTiled unavailable: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  *fn = reinterpret_cast<EncodeTiled>(ptr);
+  return CB_OK;
+}
+
+// 3-D map with a 64 x b1 x b2 box of 16-bit elements, SWIZZLE_128B (inner box
+// = 128 B), out-of-range elements read as zero.
+int encode_3d(EncodeTiled encode, CUtensorMap* map, int dtype, const void* base, uint64_t d0,
+              uint64_t d1, uint64_t d2, uint64_t stride1, uint64_t stride2, uint32_t b1,
+              uint32_t b2) {
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1, stride2};
+  const cuuint32_t box[3] = {64, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType type =
+      dtype == CB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode(map, type, 3, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return CB_ERR_INVALID;
+  }
+  return CB_OK;
+}
+
+constexpr size_t kDynSmem1 = 1024 + (2 + kStages) * kTileBytes;
+constexpr size_t kDynSmem2 = 1024 + (2 + kStages) * kTileBytes + kStages * 2 * kTile * 4;
+
+template <typename T>
+int launch_passes(const CUtensorMap& q_map, const CUtensorMap& k_map, const Common& c,
+                  cudaStream_t s) {
+  const int grid1 = min(c.num_kv_heads * c.q_tiles, kSmCount);
+  const int grid2 = min(c.k_tiles, kSmCount);
+  cudaError_t e = cudaFuncSetAttribute(lse_pass_kernel<T>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kDynSmem1));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(mass_pass_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kDynSmem2));
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  lse_pass_kernel<T><<<grid1, kThreads, kDynSmem1, s>>>(q_map, k_map, c);
+  int rc = launch_status("cb_sparse_q_scores (row pass)");
+  if (rc != CB_OK) return rc;
+  mass_pass_kernel<T><<<grid2, kThreads, kDynSmem2, s>>>(q_map, k_map, c);
+  return launch_status("cb_sparse_q_scores (key pass)");
+}
+
+int check_shape(int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int dtype) {
+  CB_SUPPORTED(dtype == CB_DTYPE_BF16 || dtype == CB_DTYPE_FP16,
+               "Sparse-Q tensor-core scorer needs bf16 or fp16 query/key");
+  CB_SUPPORTED(head_size == kHead, "Sparse-Q tensor-core scorer supports head_size 128 (got %lld)",
+               (long long)head_size);
+  CB_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
+             "query heads must be a multiple of KV heads");
+  const int64_t groups = num_q_heads / num_kv_heads;
+  CB_SUPPORTED(groups <= kTile && kTile % groups == 0, "query groups must divide 128");
+  return CB_OK;
+}
+
+}  // namespace sq
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" int cb_sparse_q_workspace_size(int64_t num_queries, int64_t num_q_heads,
+                                          int64_t num_kv_heads, int64_t head_size, int dtype,
+                                          int64_t* bytes) {
+  CB_REQUIRE(bytes != nullptr, "null output");
+  int rc = sq::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
+  if (rc != CB_OK) return rc;
+  CB_REQUIRE(num_queries >= 0, "negative query count");
+  *bytes = static_cast<int64_t>(sq::layout(num_queries, num_q_heads, num_kv_heads, 2).total);
+  return CB_OK;
+}
+
+extern "C" int cb_sparse_q_scores(const void* query, int64_t query_token_stride, const void* key,
+                                  int64_t key_token_stride, int64_t num_keys, int64_t num_q_heads,
+                                  int64_t num_kv_heads, int64_t head_size, int dtype,
+                                  const int64_t* query_rows, const int64_t* query_positions,
+                                  int64_t num_queries, float scale, float* scores, void* workspace,
+                                  int64_t workspace_bytes, int32_t* device_error, void* stream) {
+  CB_BIND(stream, scores);
+  int rc = sq::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
+  if (rc != CB_OK) return rc;
+  CB_REQUIRE(num_keys >= 0 && num_keys < (int64_t(1) << 31), "num_keys out of range");
+  CB_REQUIRE(num_queries >= 0 && num_queries * (num_q_heads / num_kv_heads) < (int64_t(1) << 30),
+             "too many queries");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (num_keys == 0) return CB_OK;
+  CB_REQUIRE(scores != nullptr && key != nullptr, "null pointer argument");
+  if (num_queries == 0) {
+    // no query sees any key: the mass is zero everywhere
+    cudaError_t e = cudaMemsetAsync(scores, 0, num_keys * sizeof(float), s);
+    if (e != cudaSuccess) {
+      set_error("cudaMemsetAsync failed: %s", cudaGetErrorString(e));
+      return CB_ERR_CUDA;
+    }
+    return CB_OK;
+  }
+  CB_REQUIRE(query && query_rows && query_positions && workspace, "null pointer argument");
+  const int esize = 2;
+  const sq::Workspace w = sq::layout(num_queries, num_q_heads, num_kv_heads, esize);
+  CB_REQUIRE(workspace_bytes >= (int64_t)w.total, "workspace too small: %lld < %lld bytes",
+             (long long)workspace_bytes, (long long)w.total);
+  CB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 1023) == 0, "workspace must be 1 KiB aligned");
+  const uint64_t row_bytes = (uint64_t)num_kv_heads * head_size * esize;
+  CB_REQUIRE(((reinterpret_cast<uintptr_t>(key) | (uint64_t)key_token_stride |
+               (reinterpret_cast<uintptr_t>(query) | (uint64_t)query_token_stride)) & 15) == 0,
+             "query/key rows must be 16-byte aligned");
+  CB_REQUIRE(key_token_stride >= (int64_t)row_bytes, "key rows overlap");
+  const int groups = static_cast<int>(num_q_heads / num_kv_heads);
+  const int rows_pad = static_cast<int>((num_queries * groups + sq::kTile - 1) / sq::kTile * sq::kTile);
+  char* ws = static_cast<char*>(workspace);
+  sq::Common c{};
+  c.num_kv_heads = static_cast<int>(num_kv_heads);
+  c.groups = groups;
+  c.rows_pad = rows_pad;
+  c.q_tiles = rows_pad / sq::kTile;
+  c.k_tiles = static_cast<int>((num_keys + sq::kTile - 1) / sq::kTile);
+  c.num_keys = num_keys;
+  c.scale_log2 = scale * 1.4426950408889634f;
+  c.row_pos = reinterpret_cast<const int32_t*>(ws + w.row_pos);
+  c.tile_max = reinterpret_cast<const int32_t*>(ws + w.tile_max);
+  c.tile_min = reinterpret_cast<const int32_t*>(ws + w.tile_min);
+  c.lse = reinterpret_cast<float*>(ws + w.lse);
+  c.scores = scores;
+  c.error = device_error;
+
+  {
+    const int64_t warps = num_kv_heads * rows_pad;
+    const int64_t blocks = (warps + 7) / 8;
+    const int grid = static_cast<int>(blocks < kSmCount * 8 ? blocks : kSmCount * 8);
+    sq::prep_kernel<<<grid, 256, 0, s>>>(
+        static_cast<const char*>(query), query_token_stride, query_rows, query_positions,
+        num_queries, c.num_kv_heads, groups, rows_pad, static_cast<int>(head_size * esize),
+        ws + w.qd, reinterpret_cast<int32_t*>(ws + w.row_pos),
+        reinterpret_cast<int32_t*>(ws + w.tile_max), reinterpret_cast<int32_t*>(ws + w.tile_min));
+    rc = launch_status("cb_sparse_q_scores (prep)");
+    if (rc != CB_OK) return rc;
+  }
+  sq::EncodeTiled encode;
+  rc = sq::get_encoder(&encode);
+  if (rc != CB_OK) return rc;
+  alignas(64) CUtensorMap q_map;
+  alignas(64) CUtensorMap k_map;
+  // dense queries: (d, row, head) with strides (row: 256 B, head: rows_pad*256 B)
+  rc = sq::encode_3d(encode, &q_map, dtype, ws + w.qd, head_size, rows_pad, num_kv_heads,
+                     head_size * esize, (uint64_t)rows_pad * head_size * esize, sq::kTile, 1);
+  if (rc != CB_OK) return rc;
+  // keys: (d, kv head, token) with strides (head: 256 B, token: key_token_stride)
+  rc = sq::encode_3d(encode, &k_map, dtype, key, head_size, num_kv_heads, num_keys,
+                     head_size * esize, key_token_stride, 1, sq::kTile);
+  if (rc != CB_OK) return rc;
+  if (dtype == CB_DTYPE_BF16) return sq::launch_passes<__nv_bfloat16>(q_map, k_map, c, s);
+  return sq::launch_passes<__half>(q_map, k_map, c, s);
+}

@@ -230,6 +230,44 @@ def main() -> None:
             [stats["sparse_query_tokens"], int(stats["tail_fallback"]), stats["gap_tokens"]], dtype=np.int64
         )
 
+    # ---- 6b. _sparse_q_scores at the real head size (128), bf16
+    for case, (active, ctx, hq, hkv, chunk_q, overflow, gap_spans, tail) in enumerate(
+        [
+            (300, 400, 8, 2, 8, 1, [(20, 60), (200, 260)], 64),
+            (200, 200, 16, 2, 8, 1, [], 64),  # tail fallback, no prefix
+        ]
+    ):
+        executor = object.__new__(Qwen3BlendExecutor)
+        executor.tp_group = None
+        executor.block_size = 16
+        executor.config = CacheBlendConfig.from_extra_config(
+            {"selection_strategy": "sparse_q", "check_layers": [1], "query_score_chunk_size": chunk_q,
+             "overflow_blocks": overflow, "tail_query_tokens": tail, "recompute_ratios": [0.15],
+             "strict_version_check": False}
+        )
+        query = torch.randn(active, hq, 128, generator=gen).to(torch.bfloat16)
+        key = torch.randn(ctx, hkv, 128, generator=gen).to(torch.bfloat16)
+        absolute = torch.arange(ctx - active, ctx)
+        gaps = torch.zeros(active, dtype=torch.bool)
+        for a, b in gap_spans:
+            gaps[a:b] = True
+        scale = 1.0 / math.sqrt(128)
+        scores, forced, stats = executor._sparse_q_scores(query, key, absolute, gaps, scale)
+        selected = executor._select(scores, gaps, 1, forced_mask=forced)
+        tag = f"sq128_{case}"
+        gold[f"{tag}_query"] = bits(query)
+        gold[f"{tag}_key"] = bits(key)
+        gold[f"{tag}_absolute"] = absolute.numpy()
+        gold[f"{tag}_gaps"] = gaps.numpy()
+        gold[f"{tag}_meta"] = np.array([chunk_q, overflow, tail, 16], dtype=np.int64)
+        gold[f"{tag}_scale"] = np.array([scale])
+        gold[f"{tag}_scores"] = scores.numpy()
+        gold[f"{tag}_forced"] = forced.numpy()
+        gold[f"{tag}_selected"] = selected.numpy()
+        gold[f"{tag}_stats"] = np.array(
+            [stats["sparse_query_tokens"], int(stats["tail_fallback"]), stats["gap_tokens"]], dtype=np.int64
+        )
+
     np.savez_compressed(OUT, **gold)
 
     # ---- 7. store op sequence: every call, its result, bytes and LRU order

@@ -157,3 +157,18 @@ def test_bf16_rounding_is_nearest_even():
     # 1 + 2^-8 is a tie -> even (1.0); 1 + 3*2^-8 is a tie -> even (1 + 2^-6)
     assert oracle.bf16_to_f32(oracle.f32_to_bf16(values))[:3].tolist() == [1.0, 1.0, 1.015625]
     assert np.isinf(oracle.bf16_to_f32(oracle.f32_to_bf16(values))[-1])
+
+
+@pytest.mark.parametrize("case", range(2))
+def test_sparse_q_head128_matches_reference(golden, case):
+    tag = f"sq128_{case}"
+    chunk, overflow, tail, block_size = (int(x) for x in golden[f"{tag}_meta"])
+    scores, forced, stats = oracle.sparse_q_scores(
+        oracle.bf16_to_f32(golden[f"{tag}_query"]), oracle.bf16_to_f32(golden[f"{tag}_key"]),
+        golden[f"{tag}_absolute"], golden[f"{tag}_gaps"], float(golden[f"{tag}_scale"][0]), block_size,
+        overflow, tail, chunk,
+    )
+    np.testing.assert_allclose(scores, golden[f"{tag}_scores"], rtol=1e-4, atol=1e-6)
+    assert np.array_equal(forced, golden[f"{tag}_forced"])
+    assert stats["sparse_query_tokens"] == golden[f"{tag}_stats"][0]
+    assert np.array_equal(oracle.select(scores, golden[f"{tag}_gaps"], 0.15, forced), golden[f"{tag}_selected"])
