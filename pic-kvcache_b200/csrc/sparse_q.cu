@@ -36,8 +36,11 @@ constexpr int kHead = 128;            // head_size handled by the kernels (eleme
 constexpr int kHalfBytes = kTile * 64 * 2;  // one 128x64 16-bit SW128 box
 constexpr int kTileBytes = 2 * kHalfBytes;  // 32 KiB: a full 128x128 operand
 constexpr int kStages = 3;            // streamed-operand ring
-constexpr int kThreads = 256;
-constexpr uint32_t kTmemCols = 256;   // two 128-column fp32 accumulators
+// warps: 0 TMA producer, 1 MMA issuer, 2 TMEM owner, 3 spare, 4-7 and 8-11
+// the two epilogue warpgroups (alternate tiles)
+constexpr int kThreads = 384;
+constexpr int kTmemBufs = 4;          // four 128-column fp32 accumulators
+constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 // ---------------------------------------------------------------- PTX helpers
@@ -187,6 +190,33 @@ __device__ __forceinline__ float round_logit(uint32_t bits) {
   return Elem<T>::to_f(Elem<T>::from_f(__uint_as_float(bits)));
 }
 
+// Rounds two fp32 accumulator values to the 16-bit matmul output type
+// (round to nearest even, one packed cvt) and widens them back.
+template <typename T>
+__device__ __forceinline__ void round_pair(uint32_t lo_bits, uint32_t hi_bits, float& lo, float& hi);
+template <>
+__device__ __forceinline__ void round_pair<__nv_bfloat16>(uint32_t lo_bits, uint32_t hi_bits,
+                                                          float& lo, float& hi) {
+  uint32_t packed;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "r"(hi_bits), "r"(lo_bits));
+  lo = __uint_as_float(packed << 16);
+  hi = __uint_as_float(packed & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void round_pair<__half>(uint32_t lo_bits, uint32_t hi_bits, float& lo,
+                                                   float& hi) {
+  uint32_t packed;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(packed) : "r"(hi_bits), "r"(lo_bits));
+  const __half2 h2 = *reinterpret_cast<const __half2*>(&packed);
+  lo = __low2float(h2);
+  hi = __high2float(h2);
+}
+
+// Named barrier over the two epilogue warpgroups (256 threads).
+__device__ __forceinline__ void epilogue_sync() {
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+}
+
 // Instruction descriptor: D f32 (bits 4-5 = 1), A and B bf16 (1) or f16 (0)
 // in bits 7-9 / 10-12, both K-major (bits 15, 16 = 0), N>>3 in bits 17-22,
 // M>>4 in bits 24-28; M = N = 128.
@@ -201,10 +231,11 @@ struct Shared {
   // operand buffers live in dynamic shared memory (1024-B aligned), barriers here
   uint64_t a_full[2], a_empty[2];
   uint64_t b_full[kStages], b_empty[kStages];
-  uint64_t t_full[2], t_empty[2];
+  uint64_t t_full[kTmemBufs], t_empty[kTmemBufs];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  float merge[2][kTile];  // second warpgroup's partial row stats / key sums
 };
 
 struct Common {
@@ -238,8 +269,10 @@ __device__ __forceinline__ void setup(Shared& sh, int warp, int a_empty_count, i
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sh.a_full[i], 1);
       mbar_init(&sh.a_empty[i], a_empty_count);
+    }
+    for (int i = 0; i < kTmemBufs; ++i) {
       mbar_init(&sh.t_full[i], 1);
-      mbar_init(&sh.t_empty[i], 4);  // one arrive per epilogue warp
+      mbar_init(&sh.t_empty[i], 4);  // one arrive per warp of the owning warpgroup
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sh.b_full[s], 1);
@@ -340,9 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int kt = 0; kt <= kt_end; ++kt, ++t) {
           const int s = t % kStages;
-          const int tb = t & 1;
+          const int tb = t & (kTmemBufs - 1);
           if (!wait1(&sh.b_full[s], (t / kStages) & 1) ||
-              !wait1(&sh.t_empty[tb], ((t >> 1) & 1) ^ 1)) {
+              !wait1(&sh.t_empty[tb], ((t / kTmemBufs) & 1) ^ 1)) {
             report(c, sh, 2);
             ok = false;
             break;
@@ -362,55 +395,82 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_mma(sh);
     }
   } else if (warp >= 4) {
-    const int ew = warp - 4;             // TMEM lanes 32*ew .. +31
+    const int wg = (warp - 4) >> 2;       // epilogue warpgroup: takes tiles with t % 2 == wg
+    const int ew = warp & 3;              // TMEM lanes 32*ew .. +31
     const int row_in_tile = ew * 32 + lane;
-    int t = 0;
+    int t0 = 0;
+    bool ok = true;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
       const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
       const int h = item % c.num_kv_heads;
       const int r = qt * kTile + row_in_tile;
       const int pos = c.row_pos[r];
       const int kt_end = min(c.tile_max[qt] / kTile, c.k_tiles - 1);
-      float m = -INFINITY, l = 0.0f;
-      bool ok = true;
-      for (int kt = 0; kt <= kt_end; ++kt, ++t) {
-        const int tb = t & 1;
-        if (!wait_warp(&sh.t_full[tb], (t >> 1) & 1)) { ok = false; break; }
+      float m = -INFINITY, l = 0.0f;  // log2-domain running max and sum of this row
+      for (int kt = 0; kt <= kt_end && ok; ++kt) {
+        const int t = t0 + kt;
+        if ((t & 1) != wg) continue;
+        const int tb = t & (kTmemBufs - 1);
+        if (!wait_warp(&sh.t_full[tb], (t / kTmemBufs) & 1)) { ok = false; break; }
         tc_fence_after();
-        uint32_t v[4][32];
         const uint32_t addr = sh.tmem_base + tb * kTile + (static_cast<uint32_t>(ew * 32) << 16);
+        const int valid = min(max(pos - kt * kTile + 1, 0), kTile);  // keys <= pos
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld32(addr + q * 32, v[q]);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
-        // columns [0, valid) of this tile are keys <= pos
-        const int valid = min(max(pos - kt * kTile + 1, 0), kTile);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (q * 32 >= valid) break;
-          float x[32];
-          float cmax = -INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            x[j] = (q * 32 + j < valid) ? round_logit<T>(v[q][j]) * c.scale_log2 : -INFINITY;
-            cmax = fmaxf(cmax, x[j]);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t v[2][32];
+          tmem_ld32(addr + half * 64, v[0]);
+          tmem_ld32(addr + half * 64 + 32, v[1]);
+          tmem_wait_ld();
+          if (half == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
           }
-          const float m_new = fmaxf(m, cmax);
-          float sum = 0.0f;
+          const int lim = valid - half * 64;  // valid columns in this half
+          if (lim <= 0) continue;
+          float x[64];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) sum += ex2(x[j] - m_new);
-          l = l * ex2(m - m_new) + sum;
+          for (int j = 0; j < 32; ++j) round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], x[2 * j], x[2 * j + 1]);
+          if (lim < 64) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j)
+              if (j >= lim) x[j] = -INFINITY;
+          }
+          float cmax = x[0];
+#pragma unroll
+          for (int j = 1; j < 64; ++j) cmax = fmaxf(cmax, x[j]);
+          const float m_new = fmaxf(m, cmax * c.scale_log2);  // scale > 0: max commutes
+          float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 64; j += 2) {
+            sum0 += ex2(fmaf(x[j], c.scale_log2, -m_new));
+            sum1 += ex2(fmaf(x[j + 1], c.scale_log2, -m_new));
+          }
+          l = l * ex2(m - m_new) + (sum0 + sum1);
           m = m_new;
         }
       }
-      if (!ok) {
-        if (lane == 0) report(c, sh, 3);
-        break;
+      t0 += kt_end + 1;
+      // merge the two warpgroups' partial statistics of this row.  After an
+      // error both warpgroups still pass every barrier (without waiting on the
+      // pipeline) so neither blocks in bar.sync.
+      if (wg == 1) {
+        sh.merge[0][row_in_tile] = m;
+        sh.merge[1][row_in_tile] = l;
       }
-      c.lse[(int64_t)h * c.rows_pad + r] = (l > 0.0f) ? m + lg2(l) : INFINITY;
+      epilogue_sync();
+      if (wg == 0) {
+        const float m1 = sh.merge[0][row_in_tile];
+        const float l1 = sh.merge[1][row_in_tile];
+        const float mx = fmaxf(m, m1);
+        float total = 0.0f;
+        if (l > 0.0f) total += l * ex2(m - mx);
+        if (l1 > 0.0f) total += l1 * ex2(m1 - mx);
+        c.lse[(int64_t)h * c.rows_pad + r] = total > 0.0f ? mx + lg2(total) : INFINITY;
+      }
+      epilogue_sync();
     }
+    if (!ok && lane == 0) report(c, sh, 3);
   }
   teardown(sh, warp);
 }
@@ -430,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* a_buf = base;                   // 2 x K tiles
   unsigned char* b_buf = base + 2 * kTileBytes;  // kStages x (Q tile)
   float* side = reinterpret_cast<float*>(b_buf + kStages * kTileBytes);  // per stage: lse[128], pos[128]
-  // b_empty: the MMA commit + the four epilogue warps (they read lse/pos)
+  // b_empty: the MMA commit + the four warps of the warpgroup that read lse/pos
   setup(sh, warp, 1, 1 + 4);
   const int items = c.k_tiles;
 
@@ -482,9 +542,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int qt = 0; qt < c.q_tiles; ++qt) {
             if (c.tile_max[qt] < kt * kTile) continue;
             const int s = t % kStages;
-            const int tb = t & 1;
+            const int tb = t & (kTmemBufs - 1);
             if (!wait1(&sh.b_full[s], (t / kStages) & 1) ||
-                !wait1(&sh.t_empty[tb], ((t >> 1) & 1) ^ 1)) {
+                !wait1(&sh.t_empty[tb], ((t / kTmemBufs) & 1) ^ 1)) {
               report(c, sh, 2);
               ok = false;
               break;
@@ -505,71 +565,81 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_mma(sh);
     }
   } else if (warp >= 4) {
-    const int ew = warp - 4;
+    const int wg = (warp - 4) >> 2;
+    const int ew = warp & 3;
     const int key_in_tile = ew * 32 + lane;
     int t = 0;
     bool ok = true;
-    for (int kt = blockIdx.x; kt < items && ok; kt += gridDim.x) {
+    for (int kt = blockIdx.x; kt < items; kt += gridDim.x) {
       const int key = kt * kTile + key_in_tile;
-      float acc = 0.0f;
+      float acc0 = 0.0f, acc1 = 0.0f;
       for (int h = 0; h < c.num_kv_heads && ok; ++h) {
         for (int qt = 0; qt < c.q_tiles; ++qt) {
           if (c.tile_max[qt] < kt * kTile) continue;
+          const int mine = (t & 1) == wg;
           const int s = t % kStages;
-          const int tb = t & 1;
-          if (!wait_warp(&sh.b_full[s], (t / kStages) & 1) ||
-              !wait_warp(&sh.t_full[tb], (t >> 1) & 1)) {
+          const int tb = t & (kTmemBufs - 1);
+          const uint32_t tp = (t / kTmemBufs) & 1;
+          const uint32_t sp = (t / kStages) & 1;
+          ++t;
+          if (!mine) continue;
+          if (!wait_warp(&sh.b_full[s], sp) || !wait_warp(&sh.t_full[tb], tp)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint32_t v[4][32];
           const uint32_t addr = sh.tmem_base + tb * kTile + (static_cast<uint32_t>(ew * 32) << 16);
+          const float* lse = side + s * 2 * kTile;
+          const int* pos = reinterpret_cast<const int*>(side + s * 2 * kTile + kTile);
+          const bool full = key <= c.tile_min[qt];  // every row of the tile sees this key
 #pragma unroll
-          for (int q = 0; q < 4; ++q) tmem_ld32(addr + q * 32, v[q]);
-          tmem_wait_ld();
-          tc_fence_before();
-          const float4* lse4 = reinterpret_cast<const float4*>(side + s * 2 * kTile);
-          const int4* pos4 = reinterpret_cast<const int4*>(side + s * 2 * kTile + kTile);
-          if (key <= c.tile_min[qt]) {
-            // every row of the tile sees this key: no mask
+          for (int half = 0; half < 2; ++half) {
+            uint32_t v[2][32];
+            tmem_ld32(addr + half * 64, v[0]);
+            tmem_ld32(addr + half * 64 + 32, v[1]);
+            tmem_wait_ld();
+            if (half == 1) {  // TMEM no longer needed: hand the accumulator back to the MMA
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
+            }
+            const float2* lse2 = reinterpret_cast<const float2*>(lse + half * 64);
+            const int2* pos2 = reinterpret_cast<const int2*>(pos + half * 64);
+            if (full) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+              for (int j = 0; j < 32; ++j) {
+                float a, b;
+                round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], a, b);
+                const float2 l2 = lse2[j];
+                acc0 += ex2(fmaf(a, c.scale_log2, -l2.x));
+                acc1 += ex2(fmaf(b, c.scale_log2, -l2.y));
+              }
+            } else {
 #pragma unroll
-              for (int j4 = 0; j4 < 8; ++j4) {
-                const float4 l4 = lse4[q * 8 + j4];
-                const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  acc += ex2(fmaf(round_logit<T>(v[q][j4 * 4 + e]), c.scale_log2, -lv[e]));
+              for (int j = 0; j < 32; ++j) {
+                float a, b;
+                round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], a, b);
+                const float2 l2 = lse2[j];
+                const int2 p2 = pos2[j];
+                const float pa = ex2(fmaf(a, c.scale_log2, -l2.x));
+                const float pb = ex2(fmaf(b, c.scale_log2, -l2.y));
+                acc0 += key <= p2.x ? pa : 0.0f;
+                acc1 += key <= p2.y ? pb : 0.0f;
               }
             }
-          } else {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-#pragma unroll
-              for (int j4 = 0; j4 < 8; ++j4) {
-                const float4 l4 = lse4[q * 8 + j4];
-                const int4 p4 = pos4[q * 8 + j4];
-                const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-                const int pv[4] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float p = ex2(fmaf(round_logit<T>(v[q][j4 * 4 + e]), c.scale_log2, -lv[e]));
-                  acc += key <= pv[e] ? p : 0.0f;
-                }
-              }
+            if (half == 1) {  // lse / positions of this stage read: release it
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&sh.b_empty[s]);
             }
           }
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&sh.t_empty[tb]);
-            mbar_arrive(&sh.b_empty[s]);
-          }
-          ++t;
         }
       }
-      if (ok && key < c.num_keys) c.scores[key] = acc;
+      // merge the two warpgroups' sums for this key tile (reached by both
+      // warpgroups for every item, also after an error)
+      if (wg == 1) sh.merge[0][key_in_tile] = acc0 + acc1;
+      epilogue_sync();
+      if (wg == 0 && key < c.num_keys) c.scores[key] = (acc0 + acc1) + sh.merge[0][key_in_tile];
+      epilogue_sync();
     }
     if (!ok && lane == 0) report(c, sh, 3);
   }
