@@ -12,7 +12,8 @@
  *
  * `cb_last_error()` returns a thread-local message for the last failure on
  * the calling thread.  The library allocates no device or host memory and
- * keeps no global mutable state besides that per-thread string, so it is
+ * keeps no global mutable state besides that per-thread string (and the
+ * per-device address cache of cb_sparse_q_scores_static), so it is
  * re-entrant and may be called from several host threads on several streams.
  * Kernels run on the device that owns `stream`; for the legacy NULL stream,
  * on the device that holds the call's output buffer.
@@ -216,6 +217,28 @@ CB_API int cb_sparse_q_scores(const void* query, int64_t query_token_stride, con
                        const int64_t* query_rows, const int64_t* query_positions,
                        int64_t num_queries, float scale, float* scores, void* workspace,
                        int64_t workspace_bytes, int32_t* device_error, void* stream);
+
+/*
+ * cb_sparse_q_scores without a workspace argument.  No counterpart in the
+ * reference.  For callers that cannot allocate device memory when they score
+ * -- a serving worker whose free memory was claimed by the KV cache after
+ * profiling, or an FFI host holding buffers of another runtime without an
+ * allocator -- the workspace is a 32 MiB array inside this library (one per
+ * GPU that loads it, held until the process exits); the function allocates
+ * nothing.  Requests whose workspace (cb_sparse_q_workspace_size) exceeds
+ * 32 MiB - 1 KiB are rejected with CB_ERR_INVALID.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  All calls on a device share the array:
+ * calls whose executions overlap on the GPU race and must be serialized (one
+ * stream, or events).  Nothing in the array needs to start at zero: every call
+ * rewrites the parts it reads.
+ */
+CB_API int cb_sparse_q_scores_static(const void* query, int64_t query_token_stride,
+                              const void* key, int64_t key_token_stride, int64_t num_keys,
+                              int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                              int dtype, const int64_t* query_rows,
+                              const int64_t* query_positions, int64_t num_queries, float scale,
+                              float* scores, int32_t* device_error, void* stream);
 
 #ifdef __cplusplus
 }

@@ -95,6 +95,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _ptr, _i64,
          ctypes.c_float, _ptr, _ptr, _i64, _ptr, _ptr],
     ),
+    "cb_sparse_q_scores_static": (
+        _i32,
+        [_ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _ptr, _i64,
+         ctypes.c_float, _ptr, _ptr, _ptr],
+    ),
 }
 
 _lock = threading.Lock()

@@ -24,6 +24,7 @@
 // drains its MMAs and TMA loads, frees TMEM and returns.
 #include <cuda.h>  // CUtensorMap types; the encoder is fetched through the runtime
 
+#include <mutex>
 #include <type_traits>
 
 #include "cb_common.cuh"
@@ -899,4 +900,74 @@ extern "C" int cb_sparse_q_scores(const void* query, int64_t query_token_stride,
   if (rc != CB_OK) return rc;
   if (dtype == CB_DTYPE_BF16) return sq::launch_passes<__nv_bfloat16>(q_map, k_map, c, s);
   return sq::launch_passes<__half>(q_map, k_map, c, s);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory when
+// they score: a vLLM worker after the KV cache has claimed the free memory its
+// profiler measured (a new allocation there can fail or evict the cache), or a
+// host that reaches this library through a C FFI with buffers owned by another
+// runtime and no allocator of its own.  cb_sparse_q_scores_static runs the same
+// two-pass scorer with its workspace in a file-scope device array instead of a
+// caller buffer.  The array (kStaticWorkspaceBytes per GPU) exists on every
+// GPU that loads this library, until the process exits.
+namespace {
+constexpr int64_t kStaticWorkspaceBytes = int64_t(32) << 20;  // 32 MiB
+static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
+
+std::mutex g_static_mutex;
+void* g_static_address[64] = {};  // device address of the array, per device ordinal
+
+// Device address of the array on the current device (set up on first use).
+int static_workspace(void** address) {
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess || device < 0 || device >= 64) {
+    set_error("cb_sparse_q_scores_static: no usable current device (%s)", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_address[device] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_static_workspace);
+    if (e != cudaSuccess || ptr == nullptr) {
+      set_error("cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return CB_ERR_CUDA;
+    }
+    g_static_address[device] = ptr;
+  }
+  *address = g_static_address[device];
+  return CB_OK;
+}
+}  // namespace
+
+extern "C" int cb_sparse_q_scores_static(const void* query, int64_t query_token_stride,
+                                         const void* key, int64_t key_token_stride,
+                                         int64_t num_keys, int64_t num_q_heads,
+                                         int64_t num_kv_heads, int64_t head_size, int dtype,
+                                         const int64_t* query_rows,
+                                         const int64_t* query_positions, int64_t num_queries,
+                                         float scale, float* scores, int32_t* device_error,
+                                         void* stream) {
+  CB_BIND(stream, scores);
+  int64_t needed = 0;
+  int rc = cb_sparse_q_workspace_size(num_queries, num_q_heads, num_kv_heads, head_size, dtype,
+                                      &needed);
+  if (rc != CB_OK) return rc;
+  // the scorer wants a 1 KiB aligned workspace; the array is 256-B aligned
+  constexpr int64_t kUsable = kStaticWorkspaceBytes - 1024;
+  CB_REQUIRE(needed <= kUsable,
+             "cb_sparse_q_scores_static: %lld queries x %lld/%lld heads need %lld workspace bytes, "
+             "above the %lld-byte static workspace; use cb_sparse_q_scores with a caller buffer",
+             (long long)num_queries, (long long)num_q_heads, (long long)num_kv_heads,
+             (long long)needed, (long long)kUsable);
+  void* base = nullptr;
+  rc = static_workspace(&base);
+  if (rc != CB_OK) return rc;
+  const uintptr_t raw = reinterpret_cast<uintptr_t>(base);
+  void* aligned = reinterpret_cast<void*>((raw + 1023) & ~static_cast<uintptr_t>(1023));
+  return cb_sparse_q_scores(query, query_token_stride, key, key_token_stride, num_keys,
+                            num_q_heads, num_kv_heads, head_size, dtype, query_rows,
+                            query_positions, num_queries, scale, scores, aligned, kUsable,
+                            device_error, stream);
 }
