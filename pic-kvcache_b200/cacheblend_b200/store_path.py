@@ -1,0 +1,197 @@
+"""Store path: layerwise writeback of complete chunks into the pinned LRU (K5).
+
+Same ordering and publication semantics as the reference connector's Store
+stream (cacheblend_vllm/connector.py:384-549):
+
+* ``enqueue`` (``_enqueue_store_batch``): take one of
+  ``max_inflight_store_batches`` slots, make the single Store stream wait for
+  the serving stream, gather the batch's paged KV into a per-request reusable
+  device staging buffer, copy it to a fresh pinned host batch on the same
+  stream, record an event and hand the batch to a publisher thread;
+* ``_publish_after_event``: wait for the event, publish every chunk's host view
+  with ``put_layer_host``; any exception aborts all of the batch's segments;
+* ``wait_for_save``: synchronize the Store stream, join every publication,
+  then drop the staging buffers (they may still be read until then).
+
+B200 specifics: the staging is chunk-major ``[chunks, 2, chunk, H, D]`` so the
+gather is one ``cb_paged_gather`` launch, the D2H is one copy-engine transfer
+of the whole batch, and every published chunk view is contiguous (one DMA
+when the chunk is loaded again).
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from concurrent.futures import Future, ThreadPoolExecutor
+from typing import Any
+
+import torch
+
+from . import _native
+from .kv_layout import describe_paged, device_slots, gather_chunk_major
+from .storage import LocalPinnedCPUStore
+from .trace import PipelineTracer
+
+
+class StorePipeline:
+    """One Store stream, its staging buffers and its publisher threads."""
+
+    def __init__(
+        self,
+        store: LocalPinnedCPUStore,
+        block_size: int,
+        chunk_size: int,
+        store_workers: int = 1,
+        max_inflight_store_batches: int = 8,
+        tracer: PipelineTracer | None = None,
+        device: torch.device | None = None,
+    ):
+        self.store = store
+        self.block_size = block_size
+        self.chunk_size = chunk_size
+        self.tracer = tracer or PipelineTracer("store")
+        self._slots = threading.Semaphore(max_inflight_store_batches)
+        self._pool = ThreadPoolExecutor(max_workers=store_workers,
+                                        thread_name_prefix="cacheblend-b200-save")
+        self._lock = threading.Lock()
+        self._futures: set[Future[bool]] = set()
+        self._pending_counts: dict[str, int] = {}
+        self._staging: dict[str, torch.Tensor] = {}
+        self._retired: list[torch.Tensor] = []
+        self.stream = torch.cuda.Stream(device=device) if device is not None else torch.cuda.Stream()
+
+    # ------------------------------------------------------------- enqueue
+    def enqueue(
+        self,
+        pending: list[tuple[Any, int, int]],
+        kv_layer: Any,
+        slots: torch.Tensor,
+        request_id: str,
+        store_enqueued_ns: int | None = None,
+    ) -> None:
+        """Gather + D2H of one request's chunks of one layer on the Store stream."""
+        self._slots.acquire()
+        try:
+            paged = describe_paged(kv_layer, self.block_size)
+            _native.require_cuda(paged.key)
+            chunks = len(pending)
+            if chunks * self.chunk_size != slots.numel():
+                raise ValueError("slots must cover the pending chunks exactly")
+            serving = torch.cuda.current_stream(paged.device)
+            shape = (chunks, 2, self.chunk_size, *paged.row.dims)
+            with torch.cuda.stream(self.stream):
+                self.stream.wait_stream(serving)
+                staging = self._staging.get(request_id)
+                if staging is None or tuple(staging.shape) != shape:
+                    if staging is not None:
+                        # a later layer may store fewer chunks after a capacity
+                        # rejection; keep the old buffer alive until the Store
+                        # stream drains (its D2H may still read it)
+                        self._retired.append(staging)
+                    staging = torch.empty(shape, dtype=paged.dtype, device=paged.device)
+                    self._staging[request_id] = staging
+                device_slots_ = device_slots(slots, paged, self.block_size)
+                gather_chunk_major(paged, device_slots_, staging, stream=self.stream)
+                host = torch.empty(shape, dtype=paged.dtype, pin_memory=True)
+                host.copy_(staging, non_blocking=True)
+                event = torch.cuda.Event()
+                event.record(self.stream)
+                device_slots_.record_stream(self.stream)
+            future = self._pool.submit(
+                self._publish_after_event, event, pending, host, request_id, store_enqueued_ns
+            )
+        except Exception:
+            self._slots.release()
+            raise
+        with self._lock:
+            self._futures.add(future)
+            self._pending_counts[request_id] = self._pending_counts.get(request_id, 0) + 1
+        future.add_done_callback(self._done)
+
+    def _done(self, future: Future[bool]) -> None:
+        self._slots.release()
+
+    # ------------------------------------------------------------- publish
+    def publish_host_batch(self, pending: list[tuple[Any, int, int]], host: torch.Tensor) -> bool:
+        """Publish each chunk of a chunk-major host batch as a view (no host copy)."""
+        committed = False
+        for index, (segment_id, layer_id, _length) in enumerate(pending):
+            result = self.store.put_layer_host(segment_id, layer_id, host[index])
+            if result is not None:
+                committed |= result
+        return committed
+
+    def _publish_after_event(
+        self,
+        event: torch.cuda.Event,
+        pending: list[tuple[Any, int, int]],
+        host: torch.Tensor,
+        request_id: str | None = None,
+        store_enqueued_ns: int | None = None,
+    ) -> bool:
+        try:
+            event.synchronize()
+            committed = self.publish_host_batch(pending, host)
+            if self.tracer.enabled:
+                self.tracer.emit(
+                    "save_store_finished",
+                    request_id=request_id,
+                    layer_id=pending[0][1] if pending else None,
+                    chunks=len(pending),
+                    tokens=sum(length for _, _, length in pending),
+                    duration_us=(
+                        (time.monotonic_ns() - store_enqueued_ns) / 1000
+                        if store_enqueued_ns is not None
+                        else None
+                    ),
+                    committed_segment=committed,
+                )
+            return committed
+        except Exception:
+            for segment_id, _, _ in pending:
+                self.store.abort_put(segment_id)
+            return False
+
+    # ---------------------------------------------------------------- wait
+    def wait_for_save(self) -> dict[str, int]:
+        """Store stream drained and every publication joined; returns stores per request."""
+        futures: tuple[Future[bool], ...] = ()
+        counts: dict[str, int] = {}
+        try:
+            self.stream.synchronize()
+            with self._lock:
+                futures = tuple(self._futures)
+                counts = dict(self._pending_counts)
+                self._pending_counts.clear()
+            for future in futures:
+                future.result()
+        finally:
+            with self._lock:
+                self._futures.difference_update(futures)
+            # gathers and D2H copies are ordered on the Store stream, so the
+            # staging may only be released after the synchronization above
+            self._staging.clear()
+            self._retired.clear()
+        return counts
+
+    def drain(self) -> None:
+        try:
+            while True:
+                with self._lock:
+                    futures = tuple(self._futures)
+                if not futures:
+                    return
+                for future in futures:
+                    future.result()
+                with self._lock:
+                    self._futures.difference_update(futures)
+        finally:
+            self._staging.clear()
+            self._retired.clear()
+
+    def close(self) -> None:
+        try:
+            self.drain()
+        finally:
+            self._pool.shutdown(wait=True, cancel_futures=False)
