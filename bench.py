@@ -76,6 +76,10 @@ class Shape:
 SPARSE_Q_CONFIG = {"name": "qwen3-30b-a3b-98k-sparse_q", "layers": 48, "q_heads": 32, "kv_heads": 4,
                    "head_dim": 128, "tokens": 98304, "query_chunks": 16, "check_layer": 6}
 
+STORE_CONFIG = {"name": "qwen3-8b-store-64x8k", "layers": 36, "kv_heads": 8, "head_dim": 128, "requests": 64,
+                "tokens": 8192, "chunk": 256, "block_size": 16, "local_cpu_gb": 16.0, "inflight": 8,
+                "workers": 1}
+
 CONFIGS = {
     1: Shape("qwen3-0.6b-cpu-plumbing", 28, 8, 16, 128, 4096, 256, 12, 16, 2048, 40960, 1e6, 1, 0.15),
     2: Shape("qwen3-8b-32k-kv_deviation", 36, 8, 32, 128, 32768, 256, 89, 16, 2304, 40960, 1e6, 1, 0.15),
@@ -637,13 +641,184 @@ def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
         }), flush=True)
 
 
+def store_connector(cfg: dict, world: int, rank: int, device):
+    """A producer-only ``CacheBlendConnectorV1`` worker built the way vLLM builds it."""
+    from types import SimpleNamespace
+
+    from cacheblend_b200.connector import CacheBlendConnectorV1
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+
+    transfer = SimpleNamespace(
+        engine_id=f"bench-store-{rank}", kv_role="kv_producer", kv_connector="CacheBlendConnectorV1",
+        kv_load_failure_policy="fail",
+        kv_connector_extra_config={"chunk_size": cfg["chunk"], "local_cpu_gb": cfg["local_cpu_gb"],
+                                   "max_inflight_store_batches": cfg["inflight"],
+                                   "store_workers": cfg["workers"], "strict_version_check": False})
+    vllm_config = SimpleNamespace(
+        kv_transfer_config=transfer, cache_config=SimpleNamespace(block_size=cfg["block_size"]),
+        parallel_config=SimpleNamespace(tensor_parallel_size=world, pipeline_parallel_size=1),
+        model_config=SimpleNamespace(model="Qwen/Qwen3-8B", revision="", dtype="bfloat16"))
+    connector = CacheBlendConnectorV1(vllm_config, KVConnectorRole.WORKER)
+    heads = cfg["kv_heads"] // world
+    pool = cfg["requests"] * cfg["tokens"] // cfg["block_size"]
+    gen = torch.Generator(device=device).manual_seed(50 + rank)
+    caches = {}
+    for layer in range(cfg["layers"]):
+        kv = torch.empty(2, pool, cfg["block_size"], heads, cfg["head_dim"], dtype=torch.bfloat16, device=device)
+        kv.normal_(generator=gen)
+        caches[f"model.layers.{layer}.self_attn.attn"] = kv
+    connector.register_kv_caches(caches)
+    return connector, caches, heads
+
+
+def store_metadata(cfg: dict, step: int, rng_tokens: np.ndarray, blocks: np.ndarray):
+    """64 prefilled requests; token ids shift per step so every step stores new chunks."""
+    from cacheblend_b200.connector import CacheBlendConnectorMetadata, RequestMetadata, _slot_mapping
+
+    meta = CacheBlendConnectorMetadata()
+    per_req = cfg["tokens"] // cfg["block_size"]
+    for r in range(cfg["requests"]):
+        tokens = ((rng_tokens[r] + 7919 * step) % 151_936).tolist()
+        slots = _slot_mapping(blocks[r * per_req : (r + 1) * per_req].tolist(), cfg["block_size"], cfg["tokens"])
+        meta.requests.append(RequestMetadata(f"s{step}-r{r}", tokens, slots, None, True, cfg["tokens"]))
+    return meta
+
+
+def store_step(connector, caches: dict, meta) -> None:
+    """One forward's Store path: every layer's save_kv_layer, then wait_for_save."""
+    connector.bind_connector_metadata(meta)
+    for name, kv in caches.items():
+        connector.save_kv_layer(name, kv, None)
+    connector.wait_for_save()
+    connector.get_finished({request.request_id for request in meta.requests})
+
+
+def store_cpu_sample(cfg: dict, heads: int, threads: int) -> dict:
+    """Oracle gather of 4 requests x 1 layer into host memory, extrapolated."""
+    import oracle
+
+    rng = np.random.default_rng(5)
+    reqs, bs = 4, cfg["block_size"]
+    pool = reqs * cfg["tokens"] // bs
+    k = rng.integers(0, 1 << 16, size=(pool, bs, heads, cfg["head_dim"]), dtype=np.uint16) & 0xBFFF
+    v = rng.integers(0, 1 << 16, size=k.shape, dtype=np.uint16) & 0xBFFF
+    slots = (rng.permutation(pool)[:, None] * bs + np.arange(bs)[None, :]).reshape(-1)
+    per = cfg["tokens"]
+    t0 = time.perf_counter()
+    for r in range(reqs):
+        oracle.paged_gather(k, v, slots[r * per : (r + 1) * per], bs, threads)
+    dt = time.perf_counter() - t0
+    step_s = dt / reqs * cfg["requests"] * cfg["layers"]
+    return {"value": cfg["requests"] * cfg["tokens"] / step_s, "step_s": step_s}
+
+
+def store_reference(args, world: int) -> None:
+    import oracle
+
+    cfg = STORE_CONFIG
+    threads = oracle.threads(0)
+    heads = cfg["kv_heads"] // world
+    for _ in range(args.warmup):
+        store_cpu_sample(cfg, heads, threads)
+    samples = [store_cpu_sample(cfg, heads, threads) for _ in range(args.steps)]
+    value = statistics.median(x["value"] for x in samples)
+    print(json.dumps({
+        "impl": "reference", "metric": "stored prompt tokens/s (all layers: gather + D2H + LRU publication)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.median(x["step_s"] for x in samples) * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": cfg["name"], "parallelism": f"tp{world}"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": "oracle gather of 4 requests x 1 layer, extrapolated to 64 x 36"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def store_bench(args, world: int, rank: int, local: int) -> None:
+    """Config 5: Store path (gather complete chunks -> D2H -> LRU publication) for 36 layers."""
+    cfg = STORE_CONFIG
+    device = torch.device("cuda", local)
+    connector, caches, heads = store_connector(cfg, world, rank, device)
+    rng = np.random.default_rng(9)
+    rng_tokens = rng.integers(0, 151_936, size=(cfg["requests"], cfg["tokens"]), dtype=np.int64)
+    blocks = rng.permutation(cfg["requests"] * cfg["tokens"] // cfg["block_size"])
+    metas = [store_metadata(cfg, step, rng_tokens, blocks) for step in range(max(args.warmup, 3) + args.steps)]
+    row_bytes = heads * cfg["head_dim"] * 2
+    step_tokens = cfg["requests"] * cfg["tokens"]
+    offered = step_tokens * cfg["layers"] * 2 * row_bytes
+    for step in range(max(args.warmup, 3)):
+        store_step(connector, caches, metas[step])
+    torch.cuda.synchronize(device)
+    pipeline = connector._pipeline
+    pipeline.kernel_events = []
+    d2h_before = pipeline.d2h_bytes
+    barrier(world)
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for step in range(args.steps):
+            store_step(connector, caches, metas[max(args.warmup, 3) + step])
+        end.record()
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    events = pipeline.kernel_events
+    pipeline.kernel_events = None
+    d2h = (pipeline.d2h_bytes - d2h_before) // args.steps  # chunks rejected under pressure are not copied
+    gather_ms = sum(b.elapsed_time(e) for b, e, _ in events) / len(events)
+    # K+V rows read from the pages and written to the staging
+    launch_bytes = 2 * sum(n for _, _, n in events) / len(events)
+    peaks = measured_peaks()
+    achieved = launch_bytes / (gather_ms / 1e3) / 1e9
+    link = host_link_peak(device)
+    d2h_gbs = d2h / (ms / 1e3) / 1e9
+    traffic = load_traffic().get(f"{cfg['name']}:store_gather:tp{world}")
+    store = connector._store
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        threads = oracle.threads(0)
+        sample = store_cpu_sample(cfg, heads, threads)
+        cpu = {"value": sample["value"], "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": "oracle gather of 4 requests x 1 layer into host memory, extrapolated to 64 x 36"}
+    if rank == 0:
+        value = step_tokens / (ms / 1e3)
+        print(json.dumps({
+            "metric": "stored prompt tokens/s (all layers: gather + D2H + LRU publication)", "value": value,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 pages, new token ids every step)",
+            "config": {"workload": cfg["name"], "requests": cfg["requests"], "tokens_per_request": cfg["tokens"],
+                       "layers": cfg["layers"], "kv_heads_per_rank": heads, "lru_gb": cfg["local_cpu_gb"],
+                       "inflight_batches": cfg["inflight"], "store_workers": cfg["workers"],
+                       "parallelism": f"tp{world}", "l2": "pages 72 GiB, far larger than L2"},
+            "gpu_launches": len(events),
+            "roofline": {"bound": "hbm", "kernel": "store_gather", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                         "avg_launch_us": gather_ms * 1e3, "avg_launch_bytes": launch_bytes,
+                         "peak_source": peaks["source"]},
+            "host_link": {"d2h_bytes_per_step": d2h, "offered_bytes_per_step": offered, "d2h_gbs": d2h_gbs, "peak_d2h_gbs": link["d2h_gbs"], "frac": d2h_gbs / link["d2h_gbs"],
+                          "peak_source": "measured: best single 1 GiB device->pinned copy"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": d2h,
+                    "note": "the Store path starts from vLLM pages in HBM and ends in host memory: value is "
+                            "already measured through the connector API with the D2H inside"},
+            "store": {"committed_entries": store.committed_entries, "bytes": store.current_bytes},
+            "clocks": clocks.summary(), "cpu_baseline": cpu,
+        }), flush=True)
+    connector.close()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--steps", type=int, default=None,
+                        help="timed steps (default 200; 5 for the seconds-long Store step of config 5)")
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--config", type=int, choices=sorted(CONFIGS) + [3], default=2)
+    parser.add_argument("--config", type=int, choices=sorted(CONFIGS) + [3, 5], default=2)
     parser.add_argument("--e2e-steps", type=int, default=5)
     parser.add_argument("--sample-layers", type=int, default=2)
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -653,9 +828,21 @@ def main() -> None:
     parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
                         help="host->device mode of the e2e loader (CACHEBLEND_B200_LOAD)")
     args = parser.parse_args()
+    if args.steps is None:
+        args.steps = 5 if args.config == 5 else 200
     if args.config == 3:
         world, rank, local, group = dist_setup(args)
         sparse_q_bench(args, world, rank, local)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if args.config == 5:
+        world, rank, local, group = dist_setup(args)
+        if args.impl == "reference":
+            if rank == 0:
+                store_reference(args, world)
+        else:
+            store_bench(args, world, rank, local)
         if world > 1:
             torch.distributed.destroy_process_group()
         return

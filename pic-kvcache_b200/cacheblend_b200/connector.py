@@ -160,6 +160,8 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
         verify_runtime(self.config.strict_version_check)
         self._recompute_on_failure = getattr(transfer, "kv_load_failure_policy", None) == "recompute"
         self.engine_id = str(transfer.engine_id)
+        # a producer-only instance saves chunks and never blends: it needs no model
+        self.kv_role = str(getattr(transfer, "kv_role", None) or "kv_both")
         self.block_size = int(vllm_config.cache_config.block_size)
         self.tp_size = int(vllm_config.parallel_config.tensor_parallel_size)
         if int(vllm_config.parallel_config.pipeline_parallel_size) != 1:
@@ -229,7 +231,8 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
             self._store, self.block_size, self.config.chunk_size, self.config.store_workers,
             self.config.max_inflight_store_batches, tracer=self._trace, device=device,
         )
-        self._executor = Qwen3BlendExecutor(registry.get_model(self.engine_id), self.config, self.block_size)
+        if self.kv_role != "kv_producer":
+            self._executor = Qwen3BlendExecutor(registry.get_model(self.engine_id), self.config, self.block_size)
         self._trace.emit("worker_registered", rank=self._rank, layers=len(self._kv_caches),
                          cpu_cache_bytes=self.config.max_local_cpu_bytes)
 
@@ -302,18 +305,23 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
             usable = min(request.save_end, len(request.token_ids), request.slot_mapping.numel())
             usable = usable // chunk * chunk
             pending: list[tuple[Any, int, int]] = []
-            slot_parts: list[torch.Tensor] = []
+            starts: list[int] = []
             for start, segment_id in self._request_save_segments(request, usable):
                 if not self._store.reserve_layer(segment_id, layer_id):
                     continue
                 pending.append((segment_id, layer_id, chunk))
-                slot_parts.append(request.slot_mapping[start : start + chunk])
+                starts.append(start)
             if not pending:
                 continue
+            if starts[-1] - starts[0] == (len(starts) - 1) * chunk:
+                # consecutive chunks (the usual case): one view, no concatenation
+                slots = request.slot_mapping[starts[0] : starts[-1] + chunk]
+            else:
+                slots = torch.cat([request.slot_mapping[s : s + chunk] for s in starts])
             started = time.monotonic_ns() if self._trace.enabled else 0
             try:
                 assert self._pipeline is not None
-                self._pipeline.enqueue(pending, kv_layer, torch.cat(slot_parts), request.request_id,
+                self._pipeline.enqueue(pending, kv_layer, slots, request.request_id,
                                        store_enqueued_ns=started if self._trace.enabled else None)
                 if self._trace.enabled:
                     self._trace.emit("save_store_enqueued", request_id=request.request_id,
@@ -331,12 +339,11 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
         chunk = self.config.chunk_size
         segments = self._save_segments.setdefault(request.request_id, [])
         start = len(segments) * chunk
-        while start < usable:
-            segment_id = self._store.begin_put(
-                self.model_scope, start, request.token_ids[start : start + chunk], len(self._kv_caches)
-            )
-            segments.append((start, segment_id))
-            start += chunk
+        missing = (usable - start) // chunk
+        if missing > 0:
+            ids = self._store.begin_put_chunks(self.model_scope, start, request.token_ids, missing,
+                                               len(self._kv_caches))
+            segments.extend((start + i * chunk, segment_id) for i, segment_id in enumerate(ids))
         return segments[: usable // chunk]
 
     def wait_for_save(self) -> None:
@@ -374,7 +381,7 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
         with self._lookup_state_lock:
             self._cancelled_lookup_ids.discard(request_id)
         self._request_objects[request_id] = request
-        if not self._is_cacheable(request):
+        if not self._is_cacheable(request) or getattr(self, "kv_role", "kv_both") == "kv_producer":
             return 0, False
         plan = self._plans.get(request_id)
         if plan is not None:

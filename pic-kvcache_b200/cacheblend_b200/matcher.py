@@ -68,6 +68,15 @@ def window_hashes(tokens: Sequence[int] | np.ndarray, window: int) -> np.ndarray
         return pows[starts + window] * (prefix[starts + window] - prefix[starts])
 
 
+def chunk_hashes(chunks: np.ndarray) -> np.ndarray:
+    """uint64 fingerprint of each row of ``chunks`` [count, width]: Horner's
+    recurrence unrolled to sum_i (t_i + 1) * B**(width-1-i), wrapping mod 2**64."""
+    values = np.asarray(chunks, dtype=np.int64).astype(np.uint64) + np.uint64(1)
+    with np.errstate(over="ignore"):
+        weights = _powers(POLY_BASE, values.shape[1])[::-1]
+        return (values * weights).sum(axis=1, dtype=np.uint64)
+
+
 @dataclass(frozen=True, slots=True)
 class FingerprintRecord:
     segment_id: SegmentId
@@ -97,6 +106,22 @@ class TokenRangeMatcher:
         return FingerprintRecord(
             SegmentId(model_scope, content_hash(chunk), source_start, len(chunk)), chunk
         )
+
+    def make_records(
+        self, model_scope: str, first_start: int, tokens: Sequence[int] | np.ndarray, count: int
+    ) -> list[FingerprintRecord]:
+        """Records of ``count`` consecutive chunks starting at ``tokens[first_start]``."""
+        width = self.chunk_size
+        rows = np.asarray(tokens[first_start : first_start + count * width], dtype=np.int64)
+        if rows.shape[0] != count * width:
+            raise ValueError(f"fingerprint requires {count * width} tokens, got {rows.shape[0]}")
+        rows = rows.reshape(count, width)
+        hashes = chunk_hashes(rows).tolist()
+        return [
+            FingerprintRecord(SegmentId(model_scope, hashes[i], first_start + i * width, width),
+                              tuple(rows[i].tolist()))
+            for i in range(count)
+        ]
 
     def register(self, record: FingerprintRecord) -> None:
         with self._lock:

@@ -60,6 +60,10 @@ class LocalPinnedCPUStore:
         self.max_bytes = int(max_bytes)
         self.pin_memory = pin_memory
         self._entries: OrderedDict[SegmentId, _Entry] = OrderedDict()
+        # the committed entries in the same least-to-most recent order: the
+        # eviction walk visits only these, so writers under capacity pressure
+        # do not rescan every in-flight entry on each publication
+        self._committed: OrderedDict[SegmentId, _Entry] = OrderedDict()
         self._bytes = 0
         self._request_pins: dict[str, tuple[SegmentId, ...]] = {}
         self._lock = threading.RLock()
@@ -86,18 +90,33 @@ class LocalPinnedCPUStore:
         if num_layers <= 0:
             raise ValueError("num_layers must be positive")
         record = self.matcher.make_record(model_scope, source_start, tokens)
-        sid = record.segment_id
         with self._lock:
-            entry = self._entries.get(sid)
-            if entry is None:
-                self._entries[sid] = _Entry(record=record, num_layers=num_layers)
-                return sid
-            if entry.record.tokens != record.tokens:
-                raise RuntimeError("content-hash collision for an existing segment id")
-            if entry.num_layers != num_layers:
-                raise ValueError("num_layers changed for an existing segment")
-            self._touch(sid, entry)
+            return self._begin(record, num_layers)
+
+    def begin_put_chunks(
+        self, model_scope: str, first_start: int, tokens: Sequence[int], count: int, num_layers: int
+    ) -> list[SegmentId]:
+        """``begin_put`` of ``count`` consecutive chunks of ``tokens`` from ``first_start``,
+        fingerprinted in one vectorised pass; same ids, entries and LRU order as the
+        equivalent sequence of ``begin_put`` calls."""
+        if num_layers <= 0:
+            raise ValueError("num_layers must be positive")
+        records = self.matcher.make_records(model_scope, first_start, tokens, count)
+        with self._lock:
+            return [self._begin(record, num_layers) for record in records]
+
+    def _begin(self, record: FingerprintRecord, num_layers: int) -> SegmentId:
+        sid = record.segment_id
+        entry = self._entries.get(sid)
+        if entry is None:
+            self._entries[sid] = _Entry(record=record, num_layers=num_layers)
             return sid
+        if entry.record.tokens != record.tokens:
+            raise RuntimeError("content-hash collision for an existing segment id")
+        if entry.num_layers != num_layers:
+            raise ValueError("num_layers changed for an existing segment")
+        self._touch(sid, entry)
+        return sid
 
     def put_layer(self, segment_id: SegmentId, layer_id: int, kv: torch.Tensor) -> bool | None:
         """Copy ``kv`` to host memory and publish it (see put_layer_host)."""
@@ -176,6 +195,7 @@ class LocalPinnedCPUStore:
             if newly_committed:
                 entry.committed = True
                 self.matcher.register(entry.record)
+                self._committed[segment_id] = entry
             self._touch(segment_id, entry)
             return newly_committed
 
@@ -247,6 +267,7 @@ class LocalPinnedCPUStore:
             for sid in list(self._entries):
                 self.matcher.unregister(sid)
             self._entries.clear()
+            self._committed.clear()
             self._request_pins.clear()
             self._bytes = 0
 
@@ -259,18 +280,26 @@ class LocalPinnedCPUStore:
     def _touch(self, segment_id: SegmentId, entry: _Entry) -> None:
         entry.last_access = time.monotonic()
         self._entries.move_to_end(segment_id)
+        if entry.committed:
+            self._committed.move_to_end(segment_id)
 
     def _remove(self, segment_id: SegmentId, entry: _Entry) -> None:
         self.matcher.unregister(segment_id)
         self._entries.pop(segment_id, None)
+        self._committed.pop(segment_id, None)
         self._bytes -= entry.size_bytes
 
     def _evict(self, required_bytes: int = 0, exclude: SegmentId | None = None) -> None:
         if self._bytes + required_bytes <= self.max_bytes:
             return
-        for sid, entry in list(self._entries.items()):
-            if self._bytes + required_bytes <= self.max_bytes:
+        freed = 0
+        victims: list[tuple[SegmentId, _Entry]] = []
+        for sid, entry in self._committed.items():
+            if self._bytes - freed + required_bytes <= self.max_bytes:
                 break
-            if sid == exclude or entry.pin_count or not entry.committed:
+            if sid == exclude or entry.pin_count:
                 continue
+            victims.append((sid, entry))
+            freed += entry.size_bytes
+        for sid, entry in victims:
             self._remove(sid, entry)

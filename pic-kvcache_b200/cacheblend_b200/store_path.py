@@ -59,6 +59,13 @@ class StorePipeline:
         self._pending_counts: dict[str, int] = {}
         self._staging: dict[str, torch.Tensor] = {}
         self._retired: list[torch.Tensor] = []
+        # per request: (host slots identity, device slots) -- every layer of a
+        # forward stores the same slots, so they are checked and copied once
+        self._slot_cache: dict[str, tuple[tuple[int, ...], torch.Tensor, torch.Tensor]] = {}
+        self._layouts: dict[tuple, Any] = {}
+        # when a list, (start, end, staging bytes) of every gather launch
+        self.kernel_events: list | None = None
+        self.d2h_bytes = 0  # bytes copied device -> host since construction
         self.stream = torch.cuda.Stream(device=device) if device is not None else torch.cuda.Stream()
 
     # ------------------------------------------------------------- enqueue
@@ -73,7 +80,7 @@ class StorePipeline:
         """Gather + D2H of one request's chunks of one layer on the Store stream."""
         self._slots.acquire()
         try:
-            paged = describe_paged(kv_layer, self.block_size)
+            paged = self._describe(kv_layer)
             _native.require_cuda(paged.key)
             chunks = len(pending)
             if chunks * self.chunk_size != slots.numel():
@@ -91,10 +98,26 @@ class StorePipeline:
                         self._retired.append(staging)
                     staging = torch.empty(shape, dtype=paged.dtype, device=paged.device)
                     self._staging[request_id] = staging
-                device_slots_ = device_slots(slots, paged, self.block_size)
+                identity = (slots.data_ptr(), slots.numel(), slots.stride(0), paged.num_blocks)
+                cached = self._slot_cache.get(request_id)
+                if cached is not None and cached[0] == identity and slots.device.type == "cpu":
+                    device_slots_ = cached[2]
+                else:
+                    device_slots_ = device_slots(slots, paged, self.block_size)
+                    # the host tensor is kept with its copy so that its address
+                    # cannot be reused by other slots while the entry lives
+                    self._slot_cache[request_id] = (identity, slots, device_slots_)
+                if self.kernel_events is not None:
+                    begin = torch.cuda.Event(enable_timing=True)
+                    begin.record(self.stream)
                 gather_chunk_major(paged, device_slots_, staging, stream=self.stream)
+                if self.kernel_events is not None:
+                    finish = torch.cuda.Event(enable_timing=True)
+                    finish.record(self.stream)
+                    self.kernel_events.append((begin, finish, staging.numel() * staging.element_size()))
                 host = torch.empty(shape, dtype=paged.dtype, pin_memory=True)
                 host.copy_(staging, non_blocking=True)
+                self.d2h_bytes += host.numel() * host.element_size()
                 event = torch.cuda.Event()
                 event.record(self.stream)
                 device_slots_.record_stream(self.stream)
@@ -109,6 +132,18 @@ class StorePipeline:
             self._pending_counts[request_id] = self._pending_counts.get(request_id, 0) + 1
         future.add_done_callback(self._done)
 
+    def _describe(self, kv_layer: Any):
+        """``describe_paged`` memoised on the layer tensors' identity and geometry."""
+        tensors = (kv_layer,) if isinstance(kv_layer, torch.Tensor) else tuple(kv_layer)
+        key = tuple((t.data_ptr(), tuple(t.shape), t.stride(), t.dtype, t.device) for t in tensors)
+        paged = self._layouts.get(key)
+        if paged is None:
+            if len(self._layouts) >= 1024:
+                self._layouts.clear()
+            paged = describe_paged(kv_layer, self.block_size)
+            self._layouts[key] = paged
+        return paged
+
     def _done(self, future: Future[bool]) -> None:
         self._slots.release()
 
@@ -116,8 +151,9 @@ class StorePipeline:
     def publish_host_batch(self, pending: list[tuple[Any, int, int]], host: torch.Tensor) -> bool:
         """Publish each chunk of a chunk-major host batch as a view (no host copy)."""
         committed = False
+        views = host.unbind(0)
         for index, (segment_id, layer_id, _length) in enumerate(pending):
-            result = self.store.put_layer_host(segment_id, layer_id, host[index])
+            result = self.store.put_layer_host(segment_id, layer_id, views[index])
             if result is not None:
                 committed |= result
         return committed
@@ -173,6 +209,7 @@ class StorePipeline:
             # staging may only be released after the synchronization above
             self._staging.clear()
             self._retired.clear()
+            self._slot_cache.clear()
         return counts
 
     def drain(self) -> None:
@@ -189,9 +226,11 @@ class StorePipeline:
         finally:
             self._staging.clear()
             self._retired.clear()
+            self._slot_cache.clear()
 
     def close(self) -> None:
         try:
             self.drain()
         finally:
+            self._layouts.clear()
             self._pool.shutdown(wait=True, cancel_futures=False)

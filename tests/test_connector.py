@@ -150,6 +150,10 @@ class CountingStore:
         self.calls.append((model_scope, source_start, token_tuple, num_layers))
         return SegmentId(model_scope, content_hash(token_tuple), source_start, len(token_tuple))
 
+    def begin_put_chunks(self, model_scope, first_start, tokens, count, num_layers):
+        return [self.begin_put(model_scope, first_start + i * 4, tokens[first_start + i * 4 : first_start + (i + 1) * 4],
+                               num_layers) for i in range(count)]
+
 
 def test_save_segment_hashes_are_built_once_per_request():
     connector = make_connector()
@@ -336,6 +340,8 @@ def bare_pipeline(store):
     pipeline._pending_counts = {}
     pipeline._staging = {"r": torch.empty(1)}
     pipeline._retired = [torch.empty(1)]
+    pipeline._slot_cache = {"r": ((0, 0, 0, 0), torch.empty(1), torch.empty(1))}
+    pipeline._layouts = {}
     pipeline._slots = threading.Semaphore(2)
     pipeline._pool = ThreadPoolExecutor(max_workers=1)
     pipeline.stream = RecordingStream()
@@ -346,7 +352,7 @@ def test_wait_for_save_synchronizes_store_stream_and_drops_staging():
     pipeline = bare_pipeline(RecordingStore())
     assert pipeline.wait_for_save() == {}
     assert pipeline.stream.synchronize_calls == 1
-    assert pipeline._staging == {} and pipeline._retired == []
+    assert pipeline._staging == {} and pipeline._retired == [] and pipeline._slot_cache == {}
     pipeline._pool.shutdown()
 
 
