@@ -241,6 +241,7 @@ class DevicePath:
         self.fresh = None
         self.events: dict[str, list] = {"load": [], "scatter": [], "deviation": [], "select": []}
         self.timing = False
+        self.graphs: list = []
 
     def _ev(self, name: str, stream):
         if not self.timing:
@@ -274,6 +275,12 @@ class DevicePath:
         return buf
 
     def score(self, buf: torch.Tensor, stream) -> torch.Tensor:
+        self.deviation(buf, stream)
+        if self.tp_group is not None:
+            torch.distributed.all_reduce(self.scores, group=self.tp_group)
+        return self.select(stream)
+
+    def deviation(self, buf: torch.Tensor, stream) -> None:
         wl, shape, plan = self.wl, self.wl.shape, self.wl.plan
         if self.fresh is None:
             k_plane = buf[0].reshape(plan.allocation_end, -1)
@@ -286,8 +293,9 @@ class DevicePath:
             plan.apc_prefix_tokens, wl.act, width, 0, self.scores.data_ptr(), stream.cuda_stream,
         )
         self._ev_end("deviation", ev, stream)
-        if self.tp_group is not None:
-            torch.distributed.all_reduce(self.scores, group=self.tp_group)
+
+    def select(self, stream) -> torch.Tensor:
+        wl = self.wl
         ev = self._ev("select", stream)
         self.native.call(
             "cb_select_topk", self.scores.data_ptr(), self.base_mask.data_ptr(), wl.act, self.k,
@@ -311,11 +319,82 @@ class DevicePath:
         self._ev_end("scatter", ev, stream)
 
     def step(self, stream) -> None:
+        if self.graphs:
+            self.graphs[0].replay()
+            if len(self.graphs) == 2:
+                torch.distributed.all_reduce(self.scores, group=self.tp_group)
+                self.graphs[1].replay()
+            return
         for layer in range(self.wl.shape.layers):
             buf = self.load_layer(layer, stream)
             if layer == self.wl.shape.check_layer:
                 self.score(buf, stream)
             self.commit(layer, buf, stream)
+
+    def _until_scores(self, stream) -> None:
+        check = self.wl.shape.check_layer
+        for layer in range(check):
+            self.commit(layer, self.load_layer(layer, stream), stream)
+        self.deviation(self.load_layer(check, stream), stream)
+
+    def _after_scores(self, stream) -> None:
+        check = self.wl.shape.check_layer
+        self.select(stream)
+        self.commit(check, self.staging[check % 2], stream)
+        for layer in range(check + 1, self.wl.shape.layers):
+            self.commit(layer, self.load_layer(layer, stream), stream)
+
+    def capture(self, stream) -> None:
+        """CUDA graphs of the step (no per-launch host work while timing): one graph on a
+        single rank; with TP, two graphs around the eager NCCL all-reduce of the scores."""
+        assert self.fresh is not None and not self.timing
+        torch.cuda.synchronize(self.wl.device)
+        parts = [self._until_scores, self._after_scores]
+        graphs = []
+        if self.tp_group is None:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for part in parts:
+                    part(stream)
+            graphs.append(graph)
+        else:
+            for part in parts:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    part(stream)
+                graphs.append(graph)
+        self.graphs = graphs
+
+    def release(self) -> None:
+        self.graphs = []
+
+    def kernel_graph_us(self, stream, reps: int = 20) -> dict[str, float]:
+        """Average launch duration of the per-layer kernels, back to back as in the step:
+        one step's 36 loads (resp. 36 commit scatters) captured in a graph, replayed
+        ``reps`` times between two CUDA events on the launching stream."""
+        layers = self.wl.shape.layers
+        kinds = {
+            "load": lambda: [self.load_layer(layer, stream) for layer in range(layers)],
+            "scatter": lambda: [self.commit(layer, self.staging[layer % 2], stream) for layer in range(layers)],
+        }
+        out = {}
+        for name, launch in kinds.items():
+            torch.cuda.synchronize(self.wl.device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                launch()
+            with torch.cuda.stream(stream):
+                graph.replay()
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                end.record(stream)
+            end.synchronize()
+            out[name] = start.elapsed_time(end) * 1e3 / (reps * layers)
+            del graph
+        return out
 
     def launches_per_step(self) -> int:
         return 2 * self.wl.shape.layers + 2
@@ -440,7 +519,8 @@ def dist_setup(args):
     if world > 1:
         import datetime
 
-        torch.cuda.set_device(local)
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
         torch.distributed.init_process_group(
             "nccl" if args.impl == "ours" else "gloo", timeout=datetime.timedelta(seconds=120),
             device_id=torch.device("cuda", local) if args.impl == "ours" else None,
@@ -823,6 +903,8 @@ def main() -> None:
     parser.add_argument("--sample-layers", type=int, default=2)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-graph", action="store_true",
+                        help="time eager launches instead of CUDA-graph replays of the step")
     parser.add_argument("--layers", type=int, default=0,
                         help="override the layer count (small profiling captures only)")
     parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
@@ -870,10 +952,26 @@ def main() -> None:
             path.step(stream)
     torch.cuda.synchronize(device)
 
-    # ---- value: device-resident inputs, CUDA events on the launching stream
+    # ---- per-kernel CUDA-event durations: an eager pass of the same steps
     barrier(world)
     torch.cuda.synchronize(device)
     path.timing = True
+    with torch.cuda.stream(stream):
+        for _ in range(min(args.steps, 50)):
+            path.step(stream)
+    torch.cuda.synchronize(device)
+    path.timing = False
+    barrier(world)
+
+    # ---- value: device-resident inputs, CUDA events on the launching stream
+    if not args.no_graph:
+        path.capture(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                path.step(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    torch.cuda.synchronize(device)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks, torch.cuda.stream(stream):
@@ -882,16 +980,20 @@ def main() -> None:
             path.step(stream)
         end.record(stream)
         torch.cuda.synchronize(device)
-    path.timing = False
     barrier(world)
+    path.release()
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world, device)
     ms_per_step = elapsed_ms / args.steps
     span = wl.act
     value = span / (ms_per_step / 1e3)
 
-    # ---- per-kernel durations inside the timed region
+    # ---- per-kernel durations: eager CUDA events, then graph replays for the per-layer kernels
     kernel_ms = {name: (sum(s.elapsed_time(e) for s, e in evs) / len(evs)) if evs else None
                  for name, evs in path.events.items()}
+    eager_ms = dict(kernel_ms)
+    if not args.no_graph:
+        for name, us in path.kernel_graph_us(stream).items():
+            kernel_ms[name] = us / 1e3
     totals = {name: (kernel_ms[name] or 0) * len(path.events[name]) for name in kernel_ms}
     dominant = max(totals, key=totals.get)
     alg = algorithmic_bytes(wl)
@@ -903,7 +1005,8 @@ def main() -> None:
                 "peak_source": peaks["source"]}
     per_kernel = {name: {"avg_us": None if ms is None else ms * 1e3,
                          "gbs": None if ms is None else alg[name] / (ms / 1e3) / 1e9,
-                         "launches": len(path.events[name])}
+                         "eager_event_us": None if eager_ms[name] is None else eager_ms[name] * 1e3,
+                         "launches_per_step": len(path.events[name]) // min(args.steps, 50)}
                   for name, ms in kernel_ms.items()}
 
     # ---- e2e: public API with host buffers (H2D of reused chunks inside the step)
@@ -931,6 +1034,10 @@ def main() -> None:
                        "parallelism": f"tp{world}", "l2": "inputs larger than L2 (each layer touches "
                        f"{(alg['load'] + alg['scatter']) / 2**20:.0f} MiB)"},
             "gpu_launches": path.launches_per_step() * args.steps,
+            "launch": "eager" if args.no_graph else ("cuda-graph" if world == 1 else "cuda-graph x2 + NCCL all-reduce"),
+            "kernel_timing": ("CUDA events around each launch in an eager pass of the same steps"
+                              + ("" if args.no_graph else "; load/scatter: one step's launches replayed "
+                                 "as a CUDA graph between two events")),
             "roofline": roofline, "kernels": per_kernel, "e2e": e2e,
             "clocks": clocks.summary(), "cpu_baseline": cpu,
         }

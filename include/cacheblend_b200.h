@@ -96,6 +96,15 @@ CB_API int cb_paged_scatter(const void* src, int64_t src_plane_stride, int64_t s
                      const int64_t* slots, int64_t num_tokens, void* stream);
 
 /*
+ * Failure word of the bulk-copy paged gather/scatter kernels on the stream's
+ * device (0: none; 1: a bounded wait for a bulk copy gave up and the launch
+ * stopped early).  Synchronizes `stream`, stores the word in *value and
+ * clears it when `reset` is non-zero.  Diagnostic entry point with no
+ * counterpart in cacheblend_vllm (torch indexing cannot fail this way).
+ */
+CB_API int cb_paged_copy_error(void* stream, int32_t* value, int reset);
+
+/*
  * RoPE relocation of an already rotated key: out = R(new) R(old)^-1 key,
  * evaluated op by op in the key dtype exactly like
  * `relocate_key(rotary_emb, old_positions, new_positions, key)`

@@ -11,6 +11,7 @@ merged-block ``[blocks, 2, block_size, ...]`` (FlashInfer) and a separate
 
 from __future__ import annotations
 
+import ctypes
 from collections.abc import Sequence
 from dataclasses import dataclass
 
@@ -310,3 +311,15 @@ def scatter_from(
         slots.numel(),
         _native.stream_handle(stream),
     )
+
+
+def paged_copy_error(device: torch.device | int | None = None, reset: bool = True) -> int:
+    """Failure word of the bulk-copy gather/scatter kernels on ``device`` (0: none).
+
+    Synchronizes the device's current stream.  A non-zero word means a bounded
+    wait inside a launch gave up and that launch stopped early.
+    """
+    value = ctypes.c_int32(0)
+    stream = torch.cuda.current_stream(device)
+    _native.call("cb_paged_copy_error", stream.cuda_stream, ctypes.addressof(value), int(reset))
+    return int(value.value)

@@ -19,6 +19,7 @@
 // round-to-nearest-even back to the key dtype:
 //   dc = r(r(nc*oc) + r(ns*os))     ds = r(r(ns*oc) - r(nc*os))
 //   x1' = r(r(x1*dc) - r(x2*ds))    x2' = r(r(x2*dc) + r(x1*ds))
+#include "cb_async.cuh"
 #include "cb_common.cuh"
 
 namespace cb {
@@ -422,7 +423,7 @@ constexpr int kConsumerWarps = 8;
 constexpr int kThreads = 32 * (1 + kConsumerWarps);
 constexpr int kTileBytes = 20480;  // 8 rows of 8 bf16 heads x 128 + their cos|sin rows
 constexpr int kMaxRows = 64;
-constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s: a wait that long is a bug
+using namespace ::cb::async;
 
 enum : int32_t {
   kNone = 0,          // past alloc_end
@@ -448,76 +449,6 @@ constexpr size_t kFixedSmemBytes = kStages * kTileBytes + kStages * kMaxRows * s
 inline size_t smem_bytes(int64_t num_segments) {
   return kFixedSmemBytes +
          (num_segments <= kSmemSegments ? num_segments * sizeof(cb_segment_t) : 0);
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded wait for the phase with the given parity, called by all 32 lanes
-// of a warp; the result is warp-uniform.  Lanes that already observed the
-// phase keep polling it (a completed phase stays observable until the peer
-// side can advance the barrier again, which requires this warp).  Gives up
-// after kTimeoutNs measured by lane 0.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  uint64_t start = 0;
-  const int lane = threadIdx.x & 31;
-  for (uint32_t spin = 0;; ++spin) {
-    const bool mine = mbar_try_wait(bar, parity);
-    if (__all_sync(0xffffffffu, mine)) return true;
-    if ((spin & 255u) == 0) {
-      int expired = 0;
-      if (lane == 0) {
-        const uint64_t now = global_ns();
-        if (start == 0)
-          start = now;
-        else if (now - start > kTimeoutNs)
-          expired = 1;
-      }
-      if (__shfl_sync(0xffffffffu, expired, 0)) return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
 }
 
 __device__ __forceinline__ void report(int32_t* error, int32_t code) {
@@ -803,12 +734,8 @@ int launch_tma_load(const LoadArgs& a, int32_t* error, cudaStream_t s) {
   const int grid = static_cast<int>(tiles < cap ? tiles : cap);
   auto kernel = tma::blend_load_tma_kernel<T, NEOX>;
   const size_t smem = tma::smem_bytes(a.num_segments);
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) {
-    set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-    return CB_ERR_CUDA;
-  }
+  const int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
+  if (rc != CB_OK) return rc;
   kernel<<<grid, tma::kThreads, smem, s>>>(a, rows, tiles, error);
   return launch_status("cb_blend_load_layer");
 }

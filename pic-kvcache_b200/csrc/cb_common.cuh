@@ -24,6 +24,12 @@ int bind_stream(void* stream, const void* device_ptr);
 // Converts the launch status into CB_OK / CB_ERR_CUDA.
 int launch_status(const char* kernel);
 
+// Raises `func`'s dynamic shared memory limit on the current device to at
+// least `bytes`.  The attribute is only changed when a launch needs more than
+// any earlier one, so steady-state calls (and calls inside a stream capture
+// after a warm-up launch) make no attribute change.
+int ensure_dynamic_smem(const void* func, size_t bytes);
+
 constexpr int kSmCount = 148;  // B200: 2 dies x 74 SMs
 
 // Largest power-of-two vector width (<= 16 bytes) that divides every value

@@ -2,6 +2,10 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "cb_common.cuh"
 
 namespace cb {
@@ -24,6 +28,15 @@ int bind_stream(void* stream, const void* device_ptr) {
   int want = -1;
   cudaError_t e = cudaSuccess;
   if (stream != nullptr) {
+    // A capturing stream rejects device queries: the capture is recorded on
+    // the caller's current device, which must own the stream, so keep it.
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(reinterpret_cast<cudaStream_t>(stream), &capture);
+    if (e != cudaSuccess) {
+      set_error("cudaStreamIsCapturing failed: %s", cudaGetErrorString(e));
+      return CB_ERR_CUDA;
+    }
+    if (capture != cudaStreamCaptureStatusNone) return CB_OK;
     e = cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &want);
     if (e != cudaSuccess) {
       set_error("cudaStreamGetDevice failed: %s", cudaGetErrorString(e));
@@ -54,6 +67,27 @@ int bind_stream(void* stream, const void* device_ptr) {
       return CB_ERR_CUDA;
     }
   }
+  return CB_OK;
+}
+
+int ensure_dynamic_smem(const void* func, size_t bytes) {
+  static std::mutex lock;
+  static std::map<std::pair<int, const void*>, size_t> granted;
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) {
+    set_error("cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> guard(lock);
+  size_t& have = granted[std::make_pair(device, func)];
+  if (bytes <= have) return CB_OK;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(%zu bytes) failed: %s", bytes, cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  have = bytes;
   return CB_OK;
 }
 

@@ -457,13 +457,8 @@ extern "C" int cb_select_topk(const float* scores, const uint8_t* base_mask, int
   if (n <= (int64_t)kClusterCtas * kMaxSlice) {
     const int slice = static_cast<int>((n + kClusterCtas - 1) / kClusterCtas);
     const size_t dyn = ((size_t)slice * 5 + 15) / 16 * 16;
-    cudaError_t e = cudaFuncSetAttribute(select_cluster_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(dyn));
-    if (e != cudaSuccess) {
-      set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-      return CB_ERR_CUDA;
-    }
+    const int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(select_cluster_kernel), dyn);
+    if (rc != CB_OK) return rc;
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(kClusterCtas, 1, 1);
     config.blockDim = dim3(kSelThreads, 1, 1);
@@ -476,7 +471,7 @@ extern "C" int cb_select_topk(const float* scores, const uint8_t* base_mask, int
     attr[0].val.clusterDim.z = 1;
     config.attrs = attr;
     config.numAttrs = 1;
-    e = cudaLaunchKernelEx(&config, select_cluster_kernel, scores, base_mask, n, k, out_index,
+    cudaError_t e = cudaLaunchKernelEx(&config, select_cluster_kernel, scores, base_mask, n, k, out_index,
                            out_capacity, slice);
     if (e != cudaSuccess) {
       set_error("cb_select_topk cluster launch failed: %s", cudaGetErrorString(e));

@@ -3,12 +3,26 @@
 //
 // Semantics follow cacheblend_vllm/kv_layout.py:90-161 (gather_paged_kv /
 // scatter_paged_kv): out[plane, t] = cache[plane][slot[t] // bs, slot[t] % bs].
-// Design: one warp per (token, plane) row, 16-byte vector moves whenever
-// every address and stride allows it, four vectors in flight per lane,
-// grid = 8 CTAs x 256 threads per SM with a grid-stride loop.  The op is a
-// pure HBM copy (bytes moved = 2 x rows x row_bytes), so the only goals are
-// full 512-byte warp transactions and enough bytes in flight per SM.
+// The op is a pure HBM copy (bytes moved = 2 x rows x row_bytes), so the
+// goals are few instructions per byte and enough bytes in flight per SM.
+// Two kernels:
+//
+// * paged_run_kernel (rows contiguous on both sides, vLLM's NHD pages): a
+//   vLLM block holds block_size consecutive slots back to back, so the rows
+//   of a block-aligned token group usually form one contiguous run on both
+//   sides.  One warp per CTA reads a group's slots, checks that they are
+//   consecutive inside one block, and lane 0 moves the whole run with one
+//   cp.async.bulk load into a shared-memory ring stage and one bulk store
+//   out of it (one bulk op per row when the slots are not a run).  Loads run
+//   (stages - 2) units ahead of the stores; waits are bounded and report
+//   into a device error word.
+// * paged_copy_kernel (any strides, e.g. head-strided HND pages): one warp
+//   per (token, plane) row, 16-byte vector moves whenever every address and
+//   stride allows it, four vectors in flight per lane, grid = 8 CTAs x 256
+//   threads per SM with a grid-stride loop.
+#include "cb_async.cuh"
 #include "cb_common.cuh"
+
 
 namespace cb {
 namespace {
@@ -103,6 +117,216 @@ __global__ void __launch_bounds__(256) paged_copy_kernel(PagedDesc pg, DenseDesc
   }
 }
 
+// ----------------------------------------------------------- run copy (TMA)
+namespace run {
+using namespace ::cb::async;
+
+constexpr uint32_t kMaxStages = 32;
+constexpr uint32_t kMaxGroup = 32;             // tokens per unit (one warp reads their slots)
+constexpr uint32_t kMaxUnitBytes = 48 * 1024;  // largest run moved by one bulk op pair
+constexpr size_t kMaxSmem = 227 * 1024;        // opt-in shared memory per CTA
+constexpr size_t kSmPool = 228 * 1024;         // shared memory per SM (1 KiB reserved per CTA)
+
+struct Geo {
+  int64_t num_tokens;
+  uint32_t group;        // tokens per unit: a power of two dividing block_size, <= 32
+  uint32_t row_bytes;    // one token row of one plane (heads merged), multiple of 16
+  uint32_t stages;       // ring depth, >= 3
+  uint32_t stage_bytes;  // group * row_bytes rounded up to 128
+  uint32_t ring_offset;  // shared-memory offset of the ring
+};
+
+struct StageMeta {
+  uint32_t rows;        // tokens in the unit
+  uint32_t valid;       // bit r: row r has an in-range slot and is copied
+  uint32_t src_run;     // source rows are one contiguous run
+  uint32_t dst_run;     // destination rows are one contiguous run
+  const char* src[kMaxGroup];
+  char* dst[kMaxGroup];
+};
+
+__device__ int32_t g_error;  // first failure code of any run-copy launch (0: none)
+
+__device__ __forceinline__ void report(int32_t code) { atomicCAS(&g_error, 0, code); }
+
+template <bool GATHER>
+__device__ __forceinline__ bool store_unit(uint32_t u, const Geo& geo, uint64_t* bars,
+                                           StageMeta* meta, unsigned char* ring, int lane) {
+  const uint32_t st = u % geo.stages;
+  if (!mbar_wait(&bars[st], (u / geo.stages) & 1u)) return false;
+  if (lane == 0) {
+    const StageMeta& m = meta[st];
+    const unsigned char* buf = ring + static_cast<size_t>(st) * geo.stage_bytes;
+    const uint32_t all = m.rows == 32 ? 0xffffffffu : ((1u << m.rows) - 1u);
+    fence_async_smem();
+    if (m.dst_run && m.valid == all) {
+      bulk_store(m.dst[0], buf, m.rows * geo.row_bytes);
+    } else {
+      for (uint32_t r = 0; r < m.rows; ++r)
+        if ((m.valid >> r) & 1u) bulk_store(m.dst[r], buf + r * geo.row_bytes, geo.row_bytes);
+    }
+    bulk_commit();
+  }
+  __syncwarp();
+  return true;
+}
+
+template <bool GATHER>
+__global__ void __launch_bounds__(32) paged_run_kernel(PagedDesc pg, DenseDesc dn,
+                                                       const int64_t* __restrict__ slots, Geo geo) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  StageMeta* meta = reinterpret_cast<StageMeta*>(smem + kMaxStages * sizeof(uint64_t));
+  unsigned char* ring = smem + geo.ring_offset;
+  const int lane = threadIdx.x;
+  const uint32_t S = geo.stages;
+  const uint32_t L = S - 2;  // loads issued ahead of the oldest pending store
+  const uint32_t G = geo.group;
+  const uint32_t rb = geo.row_bytes;
+  if (lane == 0) {
+    for (uint32_t i = 0; i < S; ++i) mbar_init(&bars[i], 1);
+    mbar_init_fence();
+  }
+  __syncwarp();
+
+  // Group boundaries follow the slots' block alignment: token 0 sits at
+  // offset (slot % G) of its group.
+  int64_t first = __ldg(slots);
+  if (first < 0) first += pg.num_slots;
+  const uint32_t phase =
+      (first >= 0 && first < pg.num_slots) ? static_cast<uint32_t>(first % G) : 0u;
+  const int64_t groups = (geo.num_tokens + phase + G - 1) / G;
+
+  uint32_t it = 0;
+  bool ok = true;
+  for (int64_t g = blockIdx.x; g < groups && ok; g += gridDim.x) {
+    int64_t t0 = g * G - phase;
+    int64_t t1 = t0 + G;
+    if (t0 < 0) t0 = 0;
+    if (t1 > geo.num_tokens) t1 = geo.num_tokens;
+    const uint32_t n = static_cast<uint32_t>(t1 - t0);
+    int64_t s = -1;
+    bool valid = false;
+    if (static_cast<uint32_t>(lane) < n) {
+      s = __ldg(slots + t0 + lane);
+      if (s < 0) s += pg.num_slots;  // torch advanced-indexing wrap
+      valid = s >= 0 && s < pg.num_slots;  // out-of-range rows are skipped, as in the row kernel
+    }
+    const uint32_t all = n == 32 ? 0xffffffffu : ((1u << n) - 1u);
+    const uint32_t vmask = __ballot_sync(0xffffffffu, valid) & all;
+    const int64_t s0 = __shfl_sync(0xffffffffu, s, 0);
+    const int64_t sl = __shfl_sync(0xffffffffu, s, n - 1);
+    const bool seq = static_cast<uint32_t>(lane) >= n || s == s0 + lane;
+    const bool page_run = __all_sync(0xffffffffu, seq) && vmask == all &&
+                          s0 / pg.block_size == sl / pg.block_size;
+    const bool dense_run = static_cast<uint32_t>(t0) / dn.chunk_tokens ==
+                           static_cast<uint32_t>(t1 - 1) / dn.chunk_tokens;
+    int64_t page_off = 0;
+    if (valid) {
+      const uint32_t blk = static_cast<uint32_t>(s) / pg.block_size;
+      const uint32_t off = static_cast<uint32_t>(s) - blk * pg.block_size;
+      page_off = static_cast<int64_t>(blk) * pg.block_stride + static_cast<int64_t>(off) * pg.slot_stride;
+    }
+    for (int plane = 0; plane < 2; ++plane) {
+      const uint32_t st = it % S;
+      // the store that last read this stage was issued two units ago or earlier
+      if (lane == 0 && it >= S) bulk_wait_read<1>();
+      __syncwarp();
+      StageMeta& m = meta[st];
+      if (static_cast<uint32_t>(lane) < n) {
+        char* prow = (plane ? pg.v : pg.k) + page_off;
+        char* drow = dense_row(dn, plane, t0 + lane);
+        m.src[lane] = GATHER ? prow : drow;
+        m.dst[lane] = GATHER ? drow : prow;
+      }
+      if (lane == 0) {
+        m.rows = n;
+        m.valid = vmask;
+        m.src_run = GATHER ? page_run : dense_run;
+        m.dst_run = GATHER ? dense_run : page_run;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        unsigned char* buf = ring + static_cast<size_t>(st) * geo.stage_bytes;
+        mbar_arrive_expect_tx(&bars[st], __popc(vmask) * rb);
+        if (m.src_run && vmask == all) {
+          bulk_load(buf, m.src[0], n * rb, &bars[st]);
+        } else {
+          for (uint32_t r = 0; r < n; ++r)
+            if ((vmask >> r) & 1u) bulk_load(buf + r * rb, m.src[r], rb, &bars[st]);
+        }
+      }
+      __syncwarp();
+      if (it >= L) ok = ok && store_unit<GATHER>(it - L, geo, bars, meta, ring, lane);
+      ++it;
+    }
+  }
+  const uint32_t drained = it > L ? it - L : 0;
+  for (uint32_t u = drained; u < it; ++u) {
+    if (ok) {
+      ok = store_unit<GATHER>(u, geo, bars, meta, ring, lane);
+    } else {
+      // after a failed wait: give the loads still in flight (bounded) time to land
+      mbar_wait(&bars[u % S], (u / S) & 1u);
+    }
+  }
+  if (lane == 0) {
+    bulk_wait<0>();
+    if (!ok) report(1);
+  }
+}
+
+// Tokens per unit: a power of two <= 32 dividing block_size with a run of at
+// most kMaxUnitBytes.
+uint32_t pick_group(int64_t block_size, int64_t row_bytes) {
+  uint32_t g = 1;
+  while (g < kMaxGroup && block_size % (2 * g) == 0 && 2 * g * row_bytes <= kMaxUnitBytes) g *= 2;
+  return g;
+}
+
+size_t smem_for(uint32_t stages, uint32_t stage_bytes, uint32_t* ring_offset) {
+  size_t off = kMaxStages * sizeof(uint64_t) + stages * sizeof(StageMeta);
+  off = (off + 127) / 128 * 128;
+  *ring_offset = static_cast<uint32_t>(off);
+  return off + static_cast<size_t>(stages) * stage_bytes;
+}
+
+// Launches the run kernel when the layout allows it; returns 1 when the
+// caller must use the row kernel instead.
+template <bool GATHER>
+int try_launch(const PagedDesc& pg, const DenseDesc& dn, const int64_t* slots, int64_t num_tokens,
+               int64_t num_heads, int64_t row_bytes, cudaStream_t s, const char* name) {
+  const uint64_t align = reinterpret_cast<uint64_t>(pg.k) | reinterpret_cast<uint64_t>(pg.v) |
+                         reinterpret_cast<uint64_t>(dn.base) | (uint64_t)pg.block_stride |
+                         (uint64_t)dn.plane_stride | (uint64_t)dn.chunk_stride | (uint64_t)row_bytes;
+  if (num_heads != 1 || (align & 15u) != 0 || pg.slot_stride != row_bytes ||
+      dn.token_stride != row_bytes || row_bytes > kMaxUnitBytes)
+    return 1;
+  Geo geo{};
+  geo.num_tokens = num_tokens;
+  geo.group = pick_group(pg.block_size, row_bytes);
+  geo.row_bytes = static_cast<uint32_t>(row_bytes);
+  geo.stage_bytes = static_cast<uint32_t>((geo.group * row_bytes + 127) / 128 * 128);
+  const int ctas_per_sm = geo.stage_bytes >= 16 * 1024 ? 1 : 2;
+  const size_t budget = ctas_per_sm == 1 ? kMaxSmem : kSmPool / 2 - 1024;
+  uint32_t stages = kMaxStages;
+  uint32_t ring_offset = 0;
+  while (stages >= 3 && smem_for(stages, geo.stage_bytes, &ring_offset) > budget) --stages;
+  if (stages < 3) return 1;
+  geo.stages = stages;
+  const size_t smem = smem_for(stages, geo.stage_bytes, &ring_offset);
+  geo.ring_offset = ring_offset;
+  const int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(paged_run_kernel<GATHER>), smem);
+  if (rc != CB_OK) return rc;
+  const int64_t groups = (num_tokens + 2 * geo.group - 1) / geo.group;
+  const int64_t cap = static_cast<int64_t>(kSmCount) * ctas_per_sm;
+  const int grid = static_cast<int>(groups < cap ? groups : cap);
+  paged_run_kernel<GATHER><<<grid, 32, smem, s>>>(pg, dn, slots, geo);
+  return launch_status(name);
+}
+
+}  // namespace run
+
 template <bool GATHER>
 int launch_paged_copy(PagedDesc pg, DenseDesc dn, const int64_t* slots, int64_t num_tokens,
                       int64_t num_heads, int64_t head_bytes, void* stream, const char* name) {
@@ -110,6 +334,11 @@ int launch_paged_copy(PagedDesc pg, DenseDesc dn, const int64_t* slots, int64_t 
   if (num_heads > 1 && pg.head_stride == head_bytes && dn.head_stride == head_bytes) {
     head_bytes *= num_heads;
     num_heads = 1;
+  }
+  {
+    const int rc = run::try_launch<GATHER>(pg, dn, slots, num_tokens, num_heads, head_bytes,
+                                           reinterpret_cast<cudaStream_t>(stream), name);
+    if (rc != 1) return rc;
   }
   uint64_t acc = reinterpret_cast<uint64_t>(pg.k) | reinterpret_cast<uint64_t>(pg.v) |
                  (uint64_t)pg.block_stride | (uint64_t)pg.slot_stride |
@@ -218,4 +447,21 @@ extern "C" int cb_paged_scatter(const void* src, int64_t src_plane_stride,
                src_chunk_tokens > 0 ? src_chunk_stride : 0};
   return launch_paged_copy<false>(pg, dn, slots, num_tokens, num_heads, head_bytes, stream,
                                   "cb_paged_scatter");
+}
+
+extern "C" int cb_paged_copy_error(void* stream, int32_t* value, int reset) {
+  CB_BIND(stream, nullptr);
+  CB_REQUIRE(value != nullptr, "null pointer argument");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(value, run::g_error, sizeof(int32_t));
+  if (e == cudaSuccess && reset) {
+    const int32_t zero = 0;
+    e = cudaMemcpyToSymbol(run::g_error, &zero, sizeof(int32_t));
+  }
+  if (e != cudaSuccess) {
+    set_error("cb_paged_copy_error: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return CB_OK;
 }

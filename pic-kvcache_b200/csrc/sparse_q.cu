@@ -775,16 +775,10 @@ int launch_passes(const CUtensorMap& q_map, const CUtensorMap& k_map, const Comm
                   cudaStream_t s) {
   const int grid1 = min(c.num_kv_heads * c.q_tiles, kSmCount);
   const int grid2 = min(c.k_tiles, kSmCount);
-  cudaError_t e = cudaFuncSetAttribute(lse_pass_kernel<T>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kDynSmem1));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(mass_pass_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kDynSmem2));
-  if (e != cudaSuccess) {
-    set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-    return CB_ERR_CUDA;
-  }
+  int rc0 = ensure_dynamic_smem(reinterpret_cast<const void*>(lse_pass_kernel<T>), kDynSmem1);
+  if (rc0 == CB_OK)
+    rc0 = ensure_dynamic_smem(reinterpret_cast<const void*>(mass_pass_kernel<T>), kDynSmem2);
+  if (rc0 != CB_OK) return rc0;
   lse_pass_kernel<T><<<grid1, kThreads, kDynSmem1, s>>>(q_map, k_map, c);
   int rc = launch_status("cb_sparse_q_scores (row pass)");
   if (rc != CB_OK) return rc;

@@ -1,0 +1,92 @@
+"""Tensor-parallel host logic on CPU with two gloo ranks: the score all-reduce
+used by ``tp_global_selection`` (torch.distributed group and vLLM-style group
+coordinator), the rank-identical selection that replaces the reference's
+rank-0 broadcast (cacheblend_vllm/ascend.py:764-796), and the reference arm of
+bench.py under torchrun (rank 0 prints one line, the other rank exits 0)."""
+
+from __future__ import annotations
+
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
+
+
+class _Coordinator:
+    """The two attributes of vLLM's GroupCoordinator the selection path uses."""
+
+    def __init__(self, group):
+        self.group = group
+        self.world_size = dist.get_world_size(group)
+
+    def all_reduce(self, tensor):
+        dist.all_reduce(tensor, group=self.group)
+        return tensor
+
+
+def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    sys.path[:0] = [str(REPO), str(REPO / "pic-kvcache_b200")]
+    import oracle
+    from cacheblend_b200.selection import tp_all_reduce, tp_world_size
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(100 + rank)  # each rank's heads give different partial scores
+        partial = rng.standard_normal(4096).astype(np.float32)
+        gaps = np.random.default_rng(7).random(4096) < 0.2
+        total = torch.from_numpy(partial.copy())
+        assert tp_world_size(None) == 1 and tp_world_size(dist.group.WORLD) == world
+        tp_all_reduce(total, dist.group.WORLD)
+        again = tp_all_reduce(torch.from_numpy(partial.copy()), _Coordinator(dist.group.WORLD))
+        parts = [None] * world
+        dist.all_gather_object(parts, partial)
+        expected = np.sum(np.stack(parts), axis=0, dtype=np.float32)
+        selected = oracle.select(total.numpy(), gaps, 0.15)
+        np.savez(Path(out_dir) / f"rank{rank}.npz", total=total.numpy(), again=again.numpy(),
+                 expected=expected, selected=selected)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_score_all_reduce_and_identical_selection(tmp_path):
+    world = 2
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    for data in ranks:
+        # two-operand float sums are order independent: the reduction is exact
+        assert np.array_equal(data["total"], data["expected"])
+        assert np.array_equal(data["again"], data["expected"])
+    assert np.array_equal(ranks[0]["selected"], ranks[1]["selected"])
+    assert ranks[0]["selected"].size > 0
+
+
+def test_bench_reference_arm_under_torchrun():
+    env = dict(os.environ, OMP_NUM_THREADS="2")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(REPO / "bench.py"),
+           "--impl", "reference", "--gpus", "2", "--config", "1", "--steps", "1", "--warmup", "0",
+           "--sample-layers", "1"]
+    proc = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [line for line in proc.stdout.splitlines() if line.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["e2e"]["h2d_bytes_per_step"] == 0
