@@ -903,6 +903,9 @@ def main() -> None:
     parser.add_argument("--sample-layers", type=int, default=2)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--tp-shard", type=int, default=0,
+                        help="run one rank's KV-head shard of an N-way TP step on this GPU alone "
+                             "(no all-reduce; per-rank kernel study)")
     parser.add_argument("--no-graph", action="store_true",
                         help="time eager launches instead of CUDA-graph replays of the step")
     parser.add_argument("--layers", type=int, default=0,
@@ -943,7 +946,8 @@ def main() -> None:
         return
 
     device = torch.device("cuda", local)
-    wl = Workload(shape, world, rank, device, host_store=not args.no_e2e)
+    shard = args.tp_shard if args.tp_shard and world == 1 else world
+    wl = Workload(shape, shard, rank, device, host_store=not args.no_e2e)
     path = DevicePath(wl, tp_group=group)
     stream = torch.cuda.Stream(device)
     # warm-up (also builds the check-layer fresh K)
@@ -1031,7 +1035,8 @@ def main() -> None:
             "config": {"workload": shape.name, "tokens": shape.tokens, "span_tokens": span,
                        "layers": shape.layers, "kv_heads_per_rank": wl.heads, "hit_chunks": shape.hit_chunks,
                        "block_size": shape.block_size, "check_layer": shape.check_layer, "ratio": shape.ratio,
-                       "parallelism": f"tp{world}", "l2": "inputs larger than L2 (each layer touches "
+                       "parallelism": f"tp{world}" if shard == world else f"one rank of tp{shard}",
+                       "l2": "inputs larger than L2 (each layer touches "
                        f"{(alg['load'] + alg['scatter']) / 2**20:.0f} MiB)"},
             "gpu_launches": path.launches_per_step() * args.steps,
             "launch": "eager" if args.no_graph else ("cuda-graph" if world == 1 else "cuda-graph x2 + NCCL all-reduce"),

@@ -8,13 +8,19 @@ handed CPU tensors.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import numpy as np
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libcacheblend_b200.so"
+# CACHEBLEND_B200_LIB points at another build of the same ABI (e.g. a debug
+# or tuning build); by default the library built in-tree next to this file.
+LIB_PATH = Path(
+    os.environ.get("CACHEBLEND_B200_LIB")
+    or Path(__file__).resolve().parent / "_lib" / "libcacheblend_b200.so"
+)
 ABI_VERSION = 1
 
 CB_OK = 0

@@ -123,6 +123,25 @@ __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
+// bulk_wait_read with a run-time bound: exact for 0..15, larger bounds wait
+// as for 15 (stricter than asked, never weaker).
+__device__ __forceinline__ void bulk_wait_read_dyn(uint32_t n) {
+  switch (n) {
+#define CB_WAIT_READ_CASE(k) \
+  case k:                    \
+    bulk_wait_read<k>();     \
+    break;
+    CB_WAIT_READ_CASE(0) CB_WAIT_READ_CASE(1) CB_WAIT_READ_CASE(2) CB_WAIT_READ_CASE(3)
+    CB_WAIT_READ_CASE(4) CB_WAIT_READ_CASE(5) CB_WAIT_READ_CASE(6) CB_WAIT_READ_CASE(7)
+    CB_WAIT_READ_CASE(8) CB_WAIT_READ_CASE(9) CB_WAIT_READ_CASE(10) CB_WAIT_READ_CASE(11)
+    CB_WAIT_READ_CASE(12) CB_WAIT_READ_CASE(13) CB_WAIT_READ_CASE(14) CB_WAIT_READ_CASE(15)
+#undef CB_WAIT_READ_CASE
+    default:
+      bulk_wait_read<15>();  // deeper bounds only wait more than needed
+      break;
+  }
+}
+
 // At most N of this thread's committed bulk groups may still be in flight.
 template <int N>
 __device__ __forceinline__ void bulk_wait() {

@@ -13,9 +13,10 @@
 //   sides.  One warp per CTA reads a group's slots, checks that they are
 //   consecutive inside one block, and lane 0 moves the whole run with one
 //   cp.async.bulk load into a shared-memory ring stage and one bulk store
-//   out of it (one bulk op per row when the slots are not a run).  Loads run
-//   (stages - 2) units ahead of the stores; waits are bounded and report
-//   into a device error word.
+//   out of it (one bulk op per row when the slots are not a run).  The ring
+//   is split between loads issued ahead (half the stages) and stores still
+//   reading their stage, so both directions keep several runs in flight;
+//   waits are bounded and report into a device error word.
 // * paged_copy_kernel (any strides, e.g. head-strided HND pages): one warp
 //   per (token, plane) row, 16-byte vector moves whenever every address and
 //   stride allows it, four vectors in flight per lane, grid = 8 CTAs x 256
@@ -121,11 +122,37 @@ __global__ void __launch_bounds__(256) paged_copy_kernel(PagedDesc pg, DenseDesc
 namespace run {
 using namespace ::cb::async;
 
+// Run size and CTAs per SM follow the row size (measured on B200, paged
+// scatter/gather of 32,768 tokens at block_size 16): one issuing warp per CTA
+// keeps only a few runs in flight, so more CTAs per SM win until the ring of
+// each gets too shallow.  CB_RUN_UNIT_KB / CB_RUN_CTAS override the policy
+// (tuning sweeps only).
+#ifndef CB_RUN_UNIT_KB
+#define CB_RUN_UNIT_KB 0
+#endif
+#ifndef CB_RUN_CTAS
+#define CB_RUN_CTAS 0
+#endif
+
 constexpr uint32_t kMaxStages = 32;
-constexpr uint32_t kMaxGroup = 32;             // tokens per unit (one warp reads their slots)
-constexpr uint32_t kMaxUnitBytes = 48 * 1024;  // largest run moved by one bulk op pair
-constexpr size_t kMaxSmem = 227 * 1024;        // opt-in shared memory per CTA
-constexpr size_t kSmPool = 228 * 1024;         // shared memory per SM (1 KiB reserved per CTA)
+constexpr uint32_t kMaxGroup = 32;  // tokens per unit (one warp reads their slots)
+constexpr uint32_t kMinStages = 3;
+constexpr size_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA
+constexpr size_t kSmPool = 228 * 1024;   // shared memory per SM (1 KiB reserved per CTA)
+
+struct Policy {
+  uint32_t unit_bytes;  // largest run moved by one bulk load/store pair
+  int ctas_per_sm;
+};
+
+inline Policy pick_policy(int64_t row_bytes) {
+  Policy p{8 * 1024, 4};                                  // rows of 2 KiB and more
+  if (row_bytes < 1024) p = Policy{4 * 1024, 8};          // e.g. one 128-dim head
+  else if (row_bytes < 2048) p = Policy{8 * 1024, 6};     // e.g. four heads
+  if (CB_RUN_UNIT_KB > 0) p.unit_bytes = CB_RUN_UNIT_KB * 1024;
+  if (CB_RUN_CTAS > 0) p.ctas_per_sm = CB_RUN_CTAS;
+  return p;
+}
 
 struct Geo {
   int64_t num_tokens;
@@ -180,7 +207,11 @@ __global__ void __launch_bounds__(32) paged_run_kernel(PagedDesc pg, DenseDesc d
   unsigned char* ring = smem + geo.ring_offset;
   const int lane = threadIdx.x;
   const uint32_t S = geo.stages;
-  const uint32_t L = S - 2;  // loads issued ahead of the oldest pending store
+  // loads issued ahead of the oldest pending store (1 <= L <= S - 2)
+  const uint32_t L = S - 2;
+  // a stage is reloaded S units after its previous load, whose store was
+  // issued at unit + L: the S - L - 1 stores issued since may still be reading
+  const uint32_t reading = S - L - 1;
   const uint32_t G = geo.group;
   const uint32_t rb = geo.row_bytes;
   if (lane == 0) {
@@ -229,8 +260,7 @@ __global__ void __launch_bounds__(32) paged_run_kernel(PagedDesc pg, DenseDesc d
     }
     for (int plane = 0; plane < 2; ++plane) {
       const uint32_t st = it % S;
-      // the store that last read this stage was issued two units ago or earlier
-      if (lane == 0 && it >= S) bulk_wait_read<1>();
+      if (lane == 0 && it >= S) bulk_wait_read_dyn(reading);
       __syncwarp();
       StageMeta& m = meta[st];
       if (static_cast<uint32_t>(lane) < n) {
@@ -277,10 +307,10 @@ __global__ void __launch_bounds__(32) paged_run_kernel(PagedDesc pg, DenseDesc d
 }
 
 // Tokens per unit: a power of two <= 32 dividing block_size with a run of at
-// most kMaxUnitBytes.
-uint32_t pick_group(int64_t block_size, int64_t row_bytes) {
+// most `unit_bytes` (one row when a single row is larger).
+uint32_t pick_group(int64_t block_size, int64_t row_bytes, uint32_t unit_bytes) {
   uint32_t g = 1;
-  while (g < kMaxGroup && block_size % (2 * g) == 0 && 2 * g * row_bytes <= kMaxUnitBytes) g *= 2;
+  while (g < kMaxGroup && block_size % (2 * g) == 0 && 2 * g * row_bytes <= unit_bytes) g *= 2;
   return g;
 }
 
@@ -300,26 +330,30 @@ int try_launch(const PagedDesc& pg, const DenseDesc& dn, const int64_t* slots, i
                          reinterpret_cast<uint64_t>(dn.base) | (uint64_t)pg.block_stride |
                          (uint64_t)dn.plane_stride | (uint64_t)dn.chunk_stride | (uint64_t)row_bytes;
   if (num_heads != 1 || (align & 15u) != 0 || pg.slot_stride != row_bytes ||
-      dn.token_stride != row_bytes || row_bytes > kMaxUnitBytes)
+      dn.token_stride != row_bytes || row_bytes > (int64_t(1) << 20))
     return 1;
+  const Policy policy = pick_policy(row_bytes);
   Geo geo{};
   geo.num_tokens = num_tokens;
-  geo.group = pick_group(pg.block_size, row_bytes);
+  geo.group = pick_group(pg.block_size, row_bytes, policy.unit_bytes);
   geo.row_bytes = static_cast<uint32_t>(row_bytes);
   geo.stage_bytes = static_cast<uint32_t>((geo.group * row_bytes + 127) / 128 * 128);
-  const int ctas_per_sm = geo.stage_bytes >= 16 * 1024 ? 1 : 2;
-  const size_t budget = ctas_per_sm == 1 ? kMaxSmem : kSmPool / 2 - 1024;
-  uint32_t stages = kMaxStages;
+  // fewer CTAs per SM when a CTA's share cannot hold kMinStages stages
   uint32_t ring_offset = 0;
-  while (stages >= 3 && smem_for(stages, geo.stage_bytes, &ring_offset) > budget) --stages;
-  if (stages < 3) return 1;
+  int ctas = policy.ctas_per_sm;
+  auto budget = [](int c) { return c == 1 ? kMaxSmem : kSmPool / c - 1024; };
+  while (ctas > 1 && smem_for(kMinStages, geo.stage_bytes, &ring_offset) > budget(ctas)) --ctas;
+  uint32_t stages = kMaxStages;
+  while (stages >= kMinStages && smem_for(stages, geo.stage_bytes, &ring_offset) > budget(ctas))
+    --stages;
+  if (stages < kMinStages) return 1;
   geo.stages = stages;
   const size_t smem = smem_for(stages, geo.stage_bytes, &ring_offset);
   geo.ring_offset = ring_offset;
   const int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(paged_run_kernel<GATHER>), smem);
   if (rc != CB_OK) return rc;
   const int64_t groups = (num_tokens + 2 * geo.group - 1) / geo.group;
-  const int64_t cap = static_cast<int64_t>(kSmCount) * ctas_per_sm;
+  const int64_t cap = static_cast<int64_t>(kSmCount) * ctas;
   const int grid = static_cast<int>(groups < cap ? groups : cap);
   paged_run_kernel<GATHER><<<grid, 32, smem, s>>>(pg, dn, slots, geo);
   return launch_status(name);

@@ -20,7 +20,7 @@ def _bits(t: torch.Tensor) -> np.ndarray:
 
 
 def _case(device, *, hnd: bool, misalign: bool, apc: int, heads=4, hd=128, bs=16, pool=512,
-          tokens=2048, chunk=256, seed=0, neox=True):
+          tokens=2048, chunk=256, seed=0, neox=True, rotary_dim=None):
     rng = np.random.default_rng(seed)
     gen = torch.Generator(device=device).manual_seed(seed)
     if hnd:
@@ -51,19 +51,22 @@ def _case(device, *, hnd: bool, misalign: bool, apc: int, heads=4, hd=128, bs=16
     token_segment = np.full(alloc_end, -1, dtype=np.int32)
     for i, c in enumerate(hit_idx):
         token_segment[int(c) * chunk:(int(c) + 1) * chunk] = i
-    inv = 1.0 / (1e6 ** (np.arange(0, hd, 2, dtype=np.float64) / hd))
+    rd = rotary_dim or hd
+    inv = 1.0 / (1e6 ** (np.arange(0, rd, 2, dtype=np.float64) / rd))
     freqs = np.arange(32768, dtype=np.float64)[:, None] * inv[None, :]
     cos_sin = oracle.f32_to_bf16(np.concatenate((np.cos(freqs), np.sin(freqs)), -1).astype(np.float32))
     return dict(cache=cache, hit=hit, table=table, hosts=hosts, slots=slots, alloc_end=alloc_end,
                 token_segment=token_segment, cos_sin=cos_sin, sources=sources, hit_idx=hit_idx,
-                heads=heads, hd=hd, bs=bs, chunk=chunk, apc=apc, hnd=hnd, neox=neox)
+                heads=heads, hd=hd, bs=bs, chunk=chunk, apc=apc, hnd=hnd, neox=neox, rotary_dim=rd)
 
 
-def _run(case, device, max_ctas: int):
+def _run(case, device, max_ctas: int, token_pad: int = 0):
+    """``token_pad`` > 0 leaves a gap after every staging row (row-by-row kernel)."""
     c = case
     cache = c["cache"]
     heads, hd = c["heads"], c["hd"]
-    out = torch.empty(2, c["alloc_end"], heads, hd, dtype=torch.bfloat16, device=device)
+    rows = torch.empty(2, c["alloc_end"], heads * hd + token_pad, dtype=torch.bfloat16, device=device)
+    out = rows[:, :, : heads * hd].unflatten(2, (heads, hd))
     slots = torch.from_numpy(c["slots"][: c["alloc_end"]]).to(device)
     token_segment = torch.from_numpy(c["token_segment"]).to(device)
     table = torch.from_numpy(c["table"].view(np.uint8)).to(device)
@@ -74,8 +77,8 @@ def _run(case, device, max_ctas: int):
         "cb_blend_load_layer", out.data_ptr(), out.stride(0) * esize, out.stride(1) * esize, hd * esize,
         c["alloc_end"], c["apc"], cache[0].data_ptr(), cache[1].data_ptr(), cache.stride(1) * esize,
         cache.stride(2) * esize, cache.stride(3) * esize, cache.shape[1], c["bs"], slots.data_ptr(), heads,
-        hd, 0, token_segment.data_ptr(), table.data_ptr(), 4, cos_sin.data_ptr(), cos_sin.shape[0], hd,
-        int(c["neox"]), max_ctas, error.data_ptr(), _native.stream_handle(),
+        hd, 0, token_segment.data_ptr(), table.data_ptr(), 4, cos_sin.data_ptr(), cos_sin.shape[0],
+        c["rotary_dim"], int(c["neox"]), max_ctas, error.data_ptr(), _native.stream_handle(),
     )
     torch.cuda.synchronize()
     assert int(error.item()) == 0
@@ -89,8 +92,8 @@ def _expected(case):
     segs = [(int(c["sources"][i]), int(c["hit_idx"][i]) * c["chunk"], c["chunk"], c["hosts"][i])
             for i in range(4)]
     return oracle.blend_load(oracle.BF16, c["alloc_end"], c["apc"], k_np, v_np, c["slots"][: c["alloc_end"]],
-                             c["bs"], segs, np.ones(4, dtype=np.int32), c["cos_sin"], c["hd"], c["hd"],
-                             c["neox"])
+                             c["bs"], segs, np.ones(4, dtype=np.int32), c["cos_sin"], c["hd"],
+                             c["rotary_dim"], c["neox"])
 
 
 @pytest.mark.parametrize("hnd", [False, True])
@@ -106,6 +109,21 @@ def test_blend_load_tma_tile_shapes(cuda, heads):
     # rows per 16 KiB tile from 64 (1 head) down to 4 (16 heads)
     case = _case(cuda, hnd=False, misalign=False, apc=0, heads=heads, seed=10 + heads)
     assert np.array_equal(_run(case, cuda, 0), _expected(case))
+
+
+@pytest.mark.parametrize("heads,neox", [(1, True), (8, True), (8, False)])
+def test_blend_load_strided_staging(cuda, heads, neox):
+    """Staging rows with gaps between them: the row-by-row TMA kernel (no tile store)."""
+    case = _case(cuda, hnd=False, misalign=False, apc=200, heads=heads, seed=30 + heads, neox=neox)
+    assert np.array_equal(_run(case, cuda, 0, token_pad=64), _expected(case))
+
+
+@pytest.mark.parametrize("neox", [True, False])
+@pytest.mark.parametrize("token_pad", [0, 64])
+def test_blend_load_partial_rotary(cuda, neox, token_pad):
+    """rotary_dim 64 of head_size 128: the upper half of each head passes through."""
+    case = _case(cuda, hnd=False, misalign=False, apc=100, heads=4, seed=40, neox=neox, rotary_dim=64)
+    assert np.array_equal(_run(case, cuda, 0, token_pad=token_pad), _expected(case))
 
 
 @pytest.mark.parametrize("max_ctas", [0, 64])
