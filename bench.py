@@ -1003,7 +1003,8 @@ def main() -> None:
     alg = algorithmic_bytes(wl)
     peaks = measured_peaks()
     achieved = alg[dominant] / (kernel_ms[dominant] / 1e3) / 1e9
-    traffic = load_traffic().get(f"{shape.name}:{dominant}:tp{world}")
+    traffic = load_traffic().get(f"{shape.name}:{dominant}:" + (f"tp{world}" if shard == world
+                                                               else f"tp{shard}-shard"))
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                 "peak_source": peaks["source"]}
