@@ -37,9 +37,11 @@ constexpr int kHead = 128;            // head_size handled by the kernels (eleme
 constexpr int kHalfBytes = kTile * 64 * 2;  // one 128x64 16-bit SW128 box
 constexpr int kTileBytes = 2 * kHalfBytes;  // 32 KiB: a full 128x128 operand
 constexpr int kStages = 3;            // streamed-operand ring
-// warps: 0 TMA producer, 1 MMA issuer, 2 TMEM owner, 3 spare, 4-7 and 8-11
-// the two epilogue warpgroups (alternate tiles)
-constexpr int kThreads = 384;
+// warps: 0 TMA producer, 1 MMA issuer, 2 TMEM owner, 3 spare, 4-15 three
+// epilogue warpgroups taking tiles round robin (three warps per SM sub-partition
+// keep the exp2 pipe fed while one of them waits on its TMEM loads)
+constexpr int kEpilogueGroups = 3;
+constexpr int kThreads = 128 + 128 * kEpilogueGroups;
 constexpr int kTmemBufs = 4;          // four 128-column fp32 accumulators
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
@@ -213,9 +215,9 @@ __device__ __forceinline__ void round_pair<__half>(uint32_t lo_bits, uint32_t hi
   hi = __high2float(h2);
 }
 
-// Named barrier over the two epilogue warpgroups (256 threads).
+// Named barrier over the epilogue warpgroups.
 __device__ __forceinline__ void epilogue_sync() {
-  asm volatile("bar.sync 1, 256;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(128 * kEpilogueGroups) : "memory");
 }
 
 // Instruction descriptor: D f32 (bits 4-5 = 1), A and B bf16 (1) or f16 (0)
@@ -236,7 +238,7 @@ struct Shared {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float merge[2][kTile];  // second warpgroup's partial row stats / key sums
+  float merge[kEpilogueGroups - 1][2][kTile];  // other warpgroups' row stats / key sums
 };
 
 struct Common {
@@ -306,6 +308,17 @@ __device__ __forceinline__ void teardown(Shared& sh, int warp) {
   }
 }
 
+// k-th work item of this CTA.  Items are numbered in decreasing cost (pass 1:
+// later query tiles see more keys; pass 2: earlier key tiles are seen by more
+// queries), so a serpentine deal -- each round in the opposite direction --
+// balances the per-CTA totals; plain round robin left SMs idle 18 % of the time.
+// Once an item is out of range every later one is too.
+__device__ __forceinline__ int cta_item(int k) {
+  const int g = static_cast<int>(gridDim.x);
+  const int c = static_cast<int>(blockIdx.x);
+  return k * g + ((k & 1) ? g - 1 - c : c);
+}
+
 // MMA issuer drain: wait until every MMA this thread issued has completed.
 __device__ __forceinline__ void drain_mma(Shared& sh) {
   umma_commit(&sh.drain);
@@ -335,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int armed[kStages];
       for (int s = 0; s < kStages; ++s) armed[s] = -1;
       int a_armed[2] = {-1, -1};
-      for (int item = blockIdx.x; item < items && !aborted(sh); item += gridDim.x, ++it) {
+      for (int k = 0, item = cta_item(0); item < items && !aborted(sh); item = cta_item(++k), ++it) {
         const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
         const int h = item % c.num_kv_heads;
         const int ab = it & 1;
@@ -366,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t a_addr = smem_u32(a_buf);
       const uint32_t b_addr = smem_u32(b_buf);
       int t = 0, it = 0;
-      for (int item = blockIdx.x; item < items && !aborted(sh); item += gridDim.x, ++it) {
+      for (int k = 0, item = cta_item(0); item < items && !aborted(sh); item = cta_item(++k), ++it) {
         const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
         const int ab = it & 1;
         if (!wait1(&sh.a_full[ab], (it >> 1) & 1)) { report(c, sh, 2); break; }
@@ -396,12 +409,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_mma(sh);
     }
   } else if (warp >= 4) {
-    const int wg = (warp - 4) >> 2;       // epilogue warpgroup: takes tiles with t % 2 == wg
+    const int wg = (warp - 4) >> 2;       // epilogue warpgroup: takes tiles with t % 3 == wg
     const int ew = warp & 3;              // TMEM lanes 32*ew .. +31
     const int row_in_tile = ew * 32 + lane;
     int t0 = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    for (int k = 0, item = cta_item(0); item < items; item = cta_item(++k)) {
       const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
       const int h = item % c.num_kv_heads;
       const int r = qt * kTile + row_in_tile;
@@ -410,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m = -INFINITY, l = 0.0f;  // log2-domain running max and sum of this row
       for (int kt = 0; kt <= kt_end && ok; ++kt) {
         const int t = t0 + kt;
-        if ((t & 1) != wg) continue;
+        if (t % kEpilogueGroups != wg) continue;
         const int tb = t & (kTmemBufs - 1);
         if (!wait_warp(&sh.t_full[tb], (t / kTmemBufs) & 1)) { ok = false; break; }
         tc_fence_after();
@@ -422,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(addr + half * 64, v[0]);
           tmem_ld32(addr + half * 64 + 32, v[1]);
           tmem_wait_ld();
-          if (half == 1) {
+          if (half == 1) {  // the accumulator goes back to the MMA
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
@@ -431,42 +444,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lim <= 0) continue;
           float x[64];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], x[2 * j], x[2 * j + 1]);
+          for (int j = 0; j < 32; ++j)
+            round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], x[2 * j], x[2 * j + 1]);
           if (lim < 64) {
 #pragma unroll
             for (int j = 0; j < 64; ++j)
               if (j >= lim) x[j] = -INFINITY;
           }
-          float cmax = x[0];
+          // eight independent chains for the max and the sum
+          float mx[8];
 #pragma unroll
-          for (int j = 1; j < 64; ++j) cmax = fmaxf(cmax, x[j]);
+          for (int i = 0; i < 8; ++i) mx[i] = x[i];
+#pragma unroll
+          for (int j = 8; j < 64; ++j) mx[j & 7] = fmaxf(mx[j & 7], x[j]);
+          const float cmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
           const float m_new = fmaxf(m, cmax * c.scale_log2);  // scale > 0: max commutes
-          float sum0 = 0.0f, sum1 = 0.0f;
+          float sm[8];
 #pragma unroll
-          for (int j = 0; j < 64; j += 2) {
-            sum0 += ex2(fmaf(x[j], c.scale_log2, -m_new));
-            sum1 += ex2(fmaf(x[j + 1], c.scale_log2, -m_new));
-          }
-          l = l * ex2(m - m_new) + (sum0 + sum1);
+          for (int i = 0; i < 8; ++i) sm[i] = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 64; ++j) sm[j & 7] += ex2(fmaf(x[j], c.scale_log2, -m_new));
+          const float part = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+          l = l * ex2(m - m_new) + part;
           m = m_new;
         }
       }
       t0 += kt_end + 1;
-      // merge the two warpgroups' partial statistics of this row.  After an
-      // error both warpgroups still pass every barrier (without waiting on the
-      // pipeline) so neither blocks in bar.sync.
-      if (wg == 1) {
-        sh.merge[0][row_in_tile] = m;
-        sh.merge[1][row_in_tile] = l;
+      // merge the warpgroups' partial statistics of this row.  After an error
+      // every warpgroup still passes both barriers (without waiting on the
+      // pipeline) so none blocks in bar.sync.
+      if (wg > 0) {
+        sh.merge[wg - 1][0][row_in_tile] = m;
+        sh.merge[wg - 1][1][row_in_tile] = l;
       }
       epilogue_sync();
       if (wg == 0) {
-        const float m1 = sh.merge[0][row_in_tile];
-        const float l1 = sh.merge[1][row_in_tile];
-        const float mx = fmaxf(m, m1);
+        float ms[kEpilogueGroups], ls[kEpilogueGroups];
+        ms[0] = m;
+        ls[0] = l;
+        float mx = m;
+#pragma unroll
+        for (int g = 1; g < kEpilogueGroups; ++g) {
+          ms[g] = sh.merge[g - 1][0][row_in_tile];
+          ls[g] = sh.merge[g - 1][1][row_in_tile];
+          mx = fmaxf(mx, ms[g]);
+        }
         float total = 0.0f;
-        if (l > 0.0f) total += l * ex2(m - mx);
-        if (l1 > 0.0f) total += l1 * ex2(m1 - mx);
+#pragma unroll
+        for (int g = 0; g < kEpilogueGroups; ++g)
+          if (ls[g] > 0.0f) total += ls[g] * ex2(ms[g] - mx);
         c.lse[(int64_t)h * c.rows_pad + r] = total > 0.0f ? mx + lg2(total) : INFINITY;
       }
       epilogue_sync();
@@ -501,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int armed[kStages];
       for (int s = 0; s < kStages; ++s) armed[s] = -1;
       int a_armed[2] = {-1, -1};
-      for (int kt = blockIdx.x; kt < items && !aborted(sh); kt += gridDim.x) {
+      for (int k = 0, kt = cta_item(0); kt < items && !aborted(sh); kt = cta_item(++k)) {
         for (int h = 0; h < c.num_kv_heads && !aborted(sh); ++h, ++it) {
           const int ab = it & 1;
           if (!wait1(&sh.a_empty[ab], ((it >> 1) & 1) ^ 1)) { report(c, sh, 1); break; }
@@ -536,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t b_addr = smem_u32(b_buf);
       int t = 0, it = 0;
       bool ok = true;
-      for (int kt = blockIdx.x; kt < items && ok && !aborted(sh); kt += gridDim.x) {
+      for (int k = 0, kt = cta_item(0); kt < items && ok && !aborted(sh); kt = cta_item(++k)) {
         for (int h = 0; h < c.num_kv_heads && ok; ++h, ++it) {
           const int ab = it & 1;
           if (!wait1(&sh.a_full[ab], (it >> 1) & 1)) { report(c, sh, 2); ok = false; break; }
@@ -571,13 +598,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int key_in_tile = ew * 32 + lane;
     int t = 0;
     bool ok = true;
-    for (int kt = blockIdx.x; kt < items; kt += gridDim.x) {
+    for (int k = 0, kt = cta_item(0); kt < items; kt = cta_item(++k)) {
       const int key = kt * kTile + key_in_tile;
-      float acc0 = 0.0f, acc1 = 0.0f;
+      float acc[8];  // eight independent sums of this key's mass
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
       for (int h = 0; h < c.num_kv_heads && ok; ++h) {
         for (int qt = 0; qt < c.q_tiles; ++qt) {
           if (c.tile_max[qt] < kt * kTile) continue;
-          const int mine = (t & 1) == wg;
+          const int mine = t % kEpilogueGroups == wg;
           const int s = t % kStages;
           const int tb = t & (kTmemBufs - 1);
           const uint32_t tp = (t / kTmemBufs) & 1;
@@ -604,28 +633,36 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
             }
-            const float2* lse2 = reinterpret_cast<const float2*>(lse + half * 64);
-            const int2* pos2 = reinterpret_cast<const int2*>(pos + half * 64);
+            const float4* lse4 = reinterpret_cast<const float4*>(lse + half * 64);
+            const int4* pos4 = reinterpret_cast<const int4*>(pos + half * 64);
             if (full) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float a, b;
-                round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], a, b);
-                const float2 l2 = lse2[j];
-                acc0 += ex2(fmaf(a, c.scale_log2, -l2.x));
-                acc1 += ex2(fmaf(b, c.scale_log2, -l2.y));
+              for (int j = 0; j < 16; ++j) {
+                float a0, a1, a2, a3;
+                round_pair<T>(v[j >> 3][(4 * j) & 31], v[j >> 3][(4 * j + 1) & 31], a0, a1);
+                round_pair<T>(v[j >> 3][(4 * j + 2) & 31], v[j >> 3][(4 * j + 3) & 31], a2, a3);
+                const float4 l4 = lse4[j];
+                acc[(4 * j) & 7] += ex2(fmaf(a0, c.scale_log2, -l4.x));
+                acc[(4 * j + 1) & 7] += ex2(fmaf(a1, c.scale_log2, -l4.y));
+                acc[(4 * j + 2) & 7] += ex2(fmaf(a2, c.scale_log2, -l4.z));
+                acc[(4 * j + 3) & 7] += ex2(fmaf(a3, c.scale_log2, -l4.w));
               }
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float a, b;
-                round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], a, b);
-                const float2 l2 = lse2[j];
-                const int2 p2 = pos2[j];
-                const float pa = ex2(fmaf(a, c.scale_log2, -l2.x));
-                const float pb = ex2(fmaf(b, c.scale_log2, -l2.y));
-                acc0 += key <= p2.x ? pa : 0.0f;
-                acc1 += key <= p2.y ? pb : 0.0f;
+              for (int j = 0; j < 16; ++j) {
+                float a0, a1, a2, a3;
+                round_pair<T>(v[j >> 3][(4 * j) & 31], v[j >> 3][(4 * j + 1) & 31], a0, a1);
+                round_pair<T>(v[j >> 3][(4 * j + 2) & 31], v[j >> 3][(4 * j + 3) & 31], a2, a3);
+                const float4 l4 = lse4[j];
+                const int4 p4 = pos4[j];
+                const float p0 = ex2(fmaf(a0, c.scale_log2, -l4.x));
+                const float p1 = ex2(fmaf(a1, c.scale_log2, -l4.y));
+                const float p2 = ex2(fmaf(a2, c.scale_log2, -l4.z));
+                const float p3 = ex2(fmaf(a3, c.scale_log2, -l4.w));
+                acc[(4 * j) & 7] += key <= p4.x ? p0 : 0.0f;
+                acc[(4 * j + 1) & 7] += key <= p4.y ? p1 : 0.0f;
+                acc[(4 * j + 2) & 7] += key <= p4.z ? p2 : 0.0f;
+                acc[(4 * j + 3) & 7] += key <= p4.w ? p3 : 0.0f;
               }
             }
             if (half == 1) {  // lse / positions of this stage read: release it
@@ -635,11 +672,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // merge the two warpgroups' sums for this key tile (reached by both
-      // warpgroups for every item, also after an error)
-      if (wg == 1) sh.merge[0][key_in_tile] = acc0 + acc1;
+      const float mass = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+      // merge the warpgroups' sums for this key tile (reached by every
+      // warpgroup for every item, also after an error)
+      if (wg > 0) sh.merge[wg - 1][0][key_in_tile] = mass;
       epilogue_sync();
-      if (wg == 0 && key < c.num_keys) c.scores[key] = (acc0 + acc1) + sh.merge[0][key_in_tile];
+      if (wg == 0 && key < c.num_keys) {
+        float total = mass;
+#pragma unroll
+        for (int g = 1; g < kEpilogueGroups; ++g) total += sh.merge[g - 1][0][key_in_tile];
+        c.scores[key] = total;
+      }
       epilogue_sync();
     }
     if (!ok && lane == 0) report(c, sh, 3);
