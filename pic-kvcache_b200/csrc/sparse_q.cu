@@ -37,6 +37,8 @@ constexpr int kHead = 128;            // head_size handled by the kernels (eleme
 constexpr int kHalfBytes = kTile * 64 * 2;  // one 128x64 16-bit SW128 box
 constexpr int kTileBytes = 2 * kHalfBytes;  // 32 KiB: a full 128x128 operand
 constexpr int kStages = 3;            // streamed-operand ring
+constexpr int kSmemQTiles = 4096;     // pass 2 keeps query-tile bounds in smem up to this many
+constexpr int kSideSlots = 8;         // pass 2: ring of per-tile lse / position rows (1 KiB each)
 // warps: 0 TMA producer, 1 MMA issuer, 2 TMEM owner, 3 spare, 4-15 three
 // epilogue warpgroups taking tiles round robin (three warps per SM sub-partition
 // keep the exp2 pipe fed while one of them waits on its TMEM loads)
@@ -235,6 +237,7 @@ struct Shared {
   uint64_t a_full[2], a_empty[2];
   uint64_t b_full[kStages], b_empty[kStages];
   uint64_t t_full[kTmemBufs], t_empty[kTmemBufs];
+  uint64_t side_full[kSideSlots], side_empty[kSideSlots];  // pass 2 lse / position ring
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -280,6 +283,10 @@ __device__ __forceinline__ void setup(Shared& sh, int warp, int a_empty_count, i
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sh.b_full[s], 1);
       mbar_init(&sh.b_empty[s], b_empty_count);
+    }
+    for (int q = 0; q < kSideSlots; ++q) {
+      mbar_init(&sh.side_full[q], 1);
+      mbar_init(&sh.side_empty[q], 4);  // the four warps of the warpgroup that read the slot
     }
     mbar_init(&sh.drain, 1);
     sh.abort = 0;
@@ -517,9 +524,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(dyn) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* a_buf = base;                   // 2 x K tiles
   unsigned char* b_buf = base + 2 * kTileBytes;  // kStages x (Q tile)
-  float* side = reinterpret_cast<float*>(b_buf + kStages * kTileBytes);  // per stage: lse[128], pos[128]
-  // b_empty: the MMA commit + the four warps of the warpgroup that read lse/pos
-  setup(sh, warp, 1, 1 + 4);
+  // per side slot: lse[128], pos[128] of one streamed query tile.  Kept apart from the
+  // query tile so that the MMA alone frees a query stage: three epilogue warpgroups
+  // holding the stages until they finish would starve the loads.
+  float* side = reinterpret_cast<float*>(b_buf + kStages * kTileBytes);
+  // Every role scans the query tiles' position bounds for every key tile:
+  // keep them in shared memory when they fit (copied before setup's barrier).
+  const int* tile_max = c.tile_max;
+  const int* tile_min = c.tile_min;
+  if (c.q_tiles <= kSmemQTiles) {
+    int* bounds = reinterpret_cast<int*>(side + kSideSlots * 2 * kTile);
+    for (int i = threadIdx.x; i < c.q_tiles; i += blockDim.x) {
+      bounds[i] = c.tile_max[i];
+      bounds[c.q_tiles + i] = c.tile_min[i];
+    }
+    tile_max = bounds;
+    tile_min = bounds + c.q_tiles;
+  }
+  setup(sh, warp, 1, 1);  // b_empty: the MMA commit
   const int items = c.k_tiles;
 
   if (warp == 0) {
@@ -528,6 +550,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int armed[kStages];
       for (int s = 0; s < kStages; ++s) armed[s] = -1;
       int a_armed[2] = {-1, -1};
+      int side_armed[kSideSlots];
+      for (int q = 0; q < kSideSlots; ++q) side_armed[q] = -1;
       for (int k = 0, kt = cta_item(0); kt < items && !aborted(sh); kt = cta_item(++k)) {
         for (int h = 0; h < c.num_kv_heads && !aborted(sh); ++h, ++it) {
           const int ab = it & 1;
@@ -537,22 +561,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(a_buf + ab * kTileBytes + kHalfBytes, &k_map, &sh.a_full[ab], 64, h, kt * kTile);
           a_armed[ab] = (it >> 1) & 1;
           for (int qt = 0; qt < c.q_tiles; ++qt) {
-            if (c.tile_max[qt] < kt * kTile) continue;  // no row of this tile sees these keys
+            if (tile_max[qt] < kt * kTile) continue;  // no row of this tile sees these keys
             const int s = t % kStages;
-            if (!wait1(&sh.b_empty[s], ((t / kStages) & 1) ^ 1)) { report(c, sh, 1); break; }
-            mbar_expect_tx(&sh.b_full[s], kTileBytes + 2 * kTile * 4);
+            const int q = t % kSideSlots;
+            if (!wait1(&sh.b_empty[s], ((t / kStages) & 1) ^ 1) ||
+                !wait1(&sh.side_empty[q], ((t / kSideSlots) & 1) ^ 1)) {
+              report(c, sh, 1);
+              break;
+            }
+            mbar_expect_tx(&sh.b_full[s], kTileBytes);
             tma_load_3d(b_buf + s * kTileBytes, &q_map, &sh.b_full[s], 0, qt * kTile, h);
             tma_load_3d(b_buf + s * kTileBytes + kHalfBytes, &q_map, &sh.b_full[s], 64, qt * kTile, h);
-            bulk_load(side + s * 2 * kTile, c.lse + (int64_t)h * c.rows_pad + qt * kTile, kTile * 4,
-                      &sh.b_full[s]);
-            bulk_load(side + s * 2 * kTile + kTile, c.row_pos + qt * kTile, kTile * 4, &sh.b_full[s]);
             armed[s] = (t / kStages) & 1;
+            mbar_expect_tx(&sh.side_full[q], 2 * kTile * 4);
+            bulk_load(side + q * 2 * kTile, c.lse + (int64_t)h * c.rows_pad + qt * kTile, kTile * 4,
+                      &sh.side_full[q]);
+            bulk_load(side + q * 2 * kTile + kTile, c.row_pos + qt * kTile, kTile * 4, &sh.side_full[q]);
+            side_armed[q] = (t / kSideSlots) & 1;
             ++t;
           }
         }
       }
       for (int s = 0; s < kStages; ++s)
         if (armed[s] >= 0) wait1(&sh.b_full[s], armed[s]);
+      for (int q = 0; q < kSideSlots; ++q)
+        if (side_armed[q] >= 0) wait1(&sh.side_full[q], side_armed[q]);
       for (int i = 0; i < 2; ++i)
         if (a_armed[i] >= 0) wait1(&sh.a_full[i], a_armed[i]);
     }
@@ -568,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ab = it & 1;
           if (!wait1(&sh.a_full[ab], (it >> 1) & 1)) { report(c, sh, 2); ok = false; break; }
           for (int qt = 0; qt < c.q_tiles; ++qt) {
-            if (c.tile_max[qt] < kt * kTile) continue;
+            if (tile_max[qt] < kt * kTile) continue;
             const int s = t % kStages;
             const int tb = t & (kTmemBufs - 1);
             if (!wait1(&sh.b_full[s], (t / kStages) & 1) ||
@@ -605,42 +638,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
       for (int h = 0; h < c.num_kv_heads && ok; ++h) {
         for (int qt = 0; qt < c.q_tiles; ++qt) {
-          if (c.tile_max[qt] < kt * kTile) continue;
+          if (tile_max[qt] < kt * kTile) continue;
           const int mine = t % kEpilogueGroups == wg;
-          const int s = t % kStages;
+          const int q = t % kSideSlots;
           const int tb = t & (kTmemBufs - 1);
           const uint32_t tp = (t / kTmemBufs) & 1;
-          const uint32_t sp = (t / kStages) & 1;
+          const uint32_t qp = (t / kSideSlots) & 1;
           ++t;
           if (!mine) continue;
-          if (!wait_warp(&sh.b_full[s], sp) || !wait_warp(&sh.t_full[tb], tp)) {
+          if (!wait_warp(&sh.side_full[q], qp) || !wait_warp(&sh.t_full[tb], tp)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t addr = sh.tmem_base + tb * kTile + (static_cast<uint32_t>(ew * 32) << 16);
-          const float* lse = side + s * 2 * kTile;
-          const int* pos = reinterpret_cast<const int*>(side + s * 2 * kTile + kTile);
-          const bool full = key <= c.tile_min[qt];  // every row of the tile sees this key
+          const float* lse = side + q * 2 * kTile;
+          const int* pos = reinterpret_cast<const int*>(side + q * 2 * kTile + kTile);
+          const bool full = key <= tile_min[qt];  // every row of the tile sees this key
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t v[2][32];
-            tmem_ld32(addr + half * 64, v[0]);
-            tmem_ld32(addr + half * 64 + 32, v[1]);
+          for (int quarter = 0; quarter < 4; ++quarter) {
+            uint32_t v[32];  // 32 rows of this key: one TMEM load, few live registers
+            tmem_ld32(addr + quarter * 32, v);
             tmem_wait_ld();
-            if (half == 1) {  // TMEM no longer needed: hand the accumulator back to the MMA
+            if (quarter == 3) {  // TMEM no longer needed: hand the accumulator back to the MMA
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
             }
-            const float4* lse4 = reinterpret_cast<const float4*>(lse + half * 64);
-            const int4* pos4 = reinterpret_cast<const int4*>(pos + half * 64);
+            const float4* lse4 = reinterpret_cast<const float4*>(lse + quarter * 32);
+            const int4* pos4 = reinterpret_cast<const int4*>(pos + quarter * 32);
             if (full) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
+              for (int j = 0; j < 8; ++j) {
                 float a0, a1, a2, a3;
-                round_pair<T>(v[j >> 3][(4 * j) & 31], v[j >> 3][(4 * j + 1) & 31], a0, a1);
-                round_pair<T>(v[j >> 3][(4 * j + 2) & 31], v[j >> 3][(4 * j + 3) & 31], a2, a3);
+                round_pair<T>(v[4 * j], v[4 * j + 1], a0, a1);
+                round_pair<T>(v[4 * j + 2], v[4 * j + 3], a2, a3);
                 const float4 l4 = lse4[j];
                 acc[(4 * j) & 7] += ex2(fmaf(a0, c.scale_log2, -l4.x));
                 acc[(4 * j + 1) & 7] += ex2(fmaf(a1, c.scale_log2, -l4.y));
@@ -649,10 +681,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             } else {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
+              for (int j = 0; j < 8; ++j) {
                 float a0, a1, a2, a3;
-                round_pair<T>(v[j >> 3][(4 * j) & 31], v[j >> 3][(4 * j + 1) & 31], a0, a1);
-                round_pair<T>(v[j >> 3][(4 * j + 2) & 31], v[j >> 3][(4 * j + 3) & 31], a2, a3);
+                round_pair<T>(v[4 * j], v[4 * j + 1], a0, a1);
+                round_pair<T>(v[4 * j + 2], v[4 * j + 3], a2, a3);
                 const float4 l4 = lse4[j];
                 const int4 p4 = pos4[j];
                 const float p0 = ex2(fmaf(a0, c.scale_log2, -l4.x));
@@ -665,9 +697,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc[(4 * j + 3) & 7] += key <= p4.w ? p3 : 0.0f;
               }
             }
-            if (half == 1) {  // lse / positions of this stage read: release it
+            if (quarter == 3) {  // lse / positions of this slot read: release it
               __syncwarp();
-              if (lane == 0) mbar_arrive(&sh.b_empty[s]);
+              if (lane == 0) mbar_arrive(&sh.side_empty[q]);
             }
           }
         }
@@ -811,7 +843,7 @@ int encode_3d(EncodeTiled encode, CUtensorMap* map, int dtype, const void* base,
 }
 
 constexpr size_t kDynSmem1 = 1024 + (2 + kStages) * kTileBytes;
-constexpr size_t kDynSmem2 = 1024 + (2 + kStages) * kTileBytes + kStages * 2 * kTile * 4;
+constexpr size_t kDynSmem2 = 1024 + (2 + kStages) * kTileBytes + kSideSlots * 2 * kTile * 4;
 
 template <typename T>
 int launch_passes(const CUtensorMap& q_map, const CUtensorMap& k_map, const Common& c,
@@ -820,12 +852,14 @@ int launch_passes(const CUtensorMap& q_map, const CUtensorMap& k_map, const Comm
   const int grid2 = min(c.k_tiles, kSmCount);
   int rc0 = ensure_dynamic_smem(reinterpret_cast<const void*>(lse_pass_kernel<T>), kDynSmem1);
   if (rc0 == CB_OK)
-    rc0 = ensure_dynamic_smem(reinterpret_cast<const void*>(mass_pass_kernel<T>), kDynSmem2);
+    rc0 = ensure_dynamic_smem(reinterpret_cast<const void*>(mass_pass_kernel<T>),
+                              kDynSmem2 + 2 * kSmemQTiles * sizeof(int));
   if (rc0 != CB_OK) return rc0;
   lse_pass_kernel<T><<<grid1, kThreads, kDynSmem1, s>>>(q_map, k_map, c);
   int rc = launch_status("cb_sparse_q_scores (row pass)");
   if (rc != CB_OK) return rc;
-  mass_pass_kernel<T><<<grid2, kThreads, kDynSmem2, s>>>(q_map, k_map, c);
+  const size_t smem2 = kDynSmem2 + (c.q_tiles <= kSmemQTiles ? 2 * c.q_tiles * sizeof(int) : 0);
+  mass_pass_kernel<T><<<grid2, kThreads, smem2, s>>>(q_map, k_map, c);
   return launch_status("cb_sparse_q_scores (key pass)");
 }
 
