@@ -708,6 +708,10 @@ def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
     peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
     peak = float(peaks.get("bf16_tflops", 1590.0))
     achieved = flops / (ms / 1e3) / 1e12
+    # co-limit: one exp2 per score element in each of the two passes on the MUFU
+    # pipe (16 per SM per clock on B200)
+    exps = 2.0 * flops / (2 * 128)
+    mufu_peak = 16 * 148 * 1.965e9
     if rank == 0:
         print(json.dumps({
             "metric": "sparse-q scored span tokens/s (boundary layer, TP-sharded)", "value": ctx / (ms / 1e3),
@@ -716,7 +720,10 @@ def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
             "config": {"workload": cfg["name"], "keys": ctx, "queries": int(positions.size),
                        "q_heads_per_rank": hq, "kv_heads_per_rank": hkv},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "flops_note": "one causal QK^T counted once (two passes run)"},
+                         "frac": achieved / peak, "flops_note": "one causal QK^T counted once (two passes run)",
+                         "co_limit": {"pipe": "mufu exp2", "achieved_per_s": exps / (ms / 1e3),
+                                      "peak_per_s": mufu_peak, "frac": exps / (ms / 1e3) / mufu_peak,
+                                      "peak_source": "16 exp2 per SM per clock x 148 SMs x 1965 MHz (nominal)"}},
             "device_error": int(error.item()), "clocks": clocks.summary(),
         }), flush=True)
 

@@ -11,15 +11,17 @@
 // Layout: rows = (query, group) pairs of one KV head, r = qi * groups + g, in
 // 128-row tiles; keys in 128-key tiles.  Two passes over the causal tiles:
 //   pass 1  S  = Q K^T in TMEM (lane = row): per-row online max/sum in the log2
-//           domain -> lse2[h][r] = m + log2(l)   (workspace)
+//           domain -> lse2[h][r] = m + log2(l), stored negated (workspace)
 //   pass 2  S' = K Q^T in TMEM (lane = key): each thread owns one key and sums
 //           exp2(round_T(s') * scale*log2e - lse2[row]) over the rows of every
 //           query tile -> one fp32 store per key, no atomics.
-// Each CTA (persistent, one per SM) is warp-specialized: warp 0 issues TMA
-// tensor loads (128x64 boxes, SWIZZLE_128B, no cluster features), warp 1 lane 0
-// issues tcgen05.mma (M=128, N=128, K=16 x 8) into one of two TMEM
-// accumulators, warp 2 owns the TMEM allocation, warps 4-7 are the softmax /
-// accumulation warpgroup reading TMEM with tcgen05.ld.  Every mbarrier wait is
+// Each CTA (persistent, one per SM, work dealt serpentine) is warp-specialized:
+// warp 0 issues TMA tensor loads (128x64 boxes, SWIZZLE_128B, no cluster
+// features), warp 1 lane 0 issues tcgen05.mma (M=128, N=128, K=16 x 8) into one
+// of four TMEM accumulators, warp 2 owns the TMEM allocation, warps 4-15 are
+// three softmax / accumulation warpgroups taking tiles round robin, reading
+// TMEM with tcgen05.ld and computing in paired fp32 (one exp2 per score on the
+// MUFU pipe, which with the issue slots bounds both passes).  Every mbarrier wait is
 // bounded (2 s); a wait that runs out records a code in *device_error, the CTA
 // drains its MMAs and TMA loads, frees TMEM and returns.
 #include <cuda.h>  // CUtensorMap types; the encoder is fetched through the runtime
@@ -255,7 +257,7 @@ struct Common {
   const int32_t* row_pos;   // [rows_pad]: position of each row, -1 for padding
   const int32_t* tile_max;  // [q_tiles]
   const int32_t* tile_min;  // [q_tiles]
-  float* lse;               // [num_kv_heads][rows_pad] (pass 1 out, pass 2 in)
+  float* lse;               // [num_kv_heads][rows_pad]: -(log2-sum-exp) per row (pass 1 out, pass 2 in)
   float* scores;            // [num_keys] (pass 2 out)
   int32_t* error;
 };
@@ -467,12 +469,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float cmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                    fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
           const float m_new = fmaxf(m, cmax * c.scale_log2);  // scale > 0: max commutes
-          float sm[8];
+          // paired fp32 FMA / add: one instruction per two scores
+          const float2 scale2 = make_float2(c.scale_log2, c.scale_log2);
+          const float2 shift2 = make_float2(-m_new, -m_new);
+          float2 sm[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) sm[i] = 0.0f;
+          for (int i = 0; i < 4; ++i) sm[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int j = 0; j < 64; ++j) sm[j & 7] += ex2(fmaf(x[j], c.scale_log2, -m_new));
-          const float part = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+          for (int j = 0; j < 32; ++j) {
+            const float2 y = __ffma2_rn(make_float2(x[2 * j], x[2 * j + 1]), scale2, shift2);
+            sm[j & 3] = __fadd2_rn(sm[j & 3], make_float2(ex2(y.x), ex2(y.y)));
+          }
+          const float2 s01 = __fadd2_rn(sm[0], sm[1]);
+          const float2 s23 = __fadd2_rn(sm[2], sm[3]);
+          const float2 s03 = __fadd2_rn(s01, s23);
+          const float part = s03.x + s03.y;
           l = l * ex2(m - m_new) + part;
           m = m_new;
         }
@@ -501,7 +512,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int g = 0; g < kEpilogueGroups; ++g)
           if (ls[g] > 0.0f) total += ls[g] * ex2(ms[g] - mx);
-        c.lse[(int64_t)h * c.rows_pad + r] = total > 0.0f ? mx + lg2(total) : INFINITY;
+        // stored negated: pass 2 adds it in a paired FMA
+        c.lse[(int64_t)h * c.rows_pad + r] = total > 0.0f ? -(mx + lg2(total)) : -INFINITY;
       }
       epilogue_sync();
     }
@@ -524,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(dyn) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* a_buf = base;                   // 2 x K tiles
   unsigned char* b_buf = base + 2 * kTileBytes;  // kStages x (Q tile)
-  // per side slot: lse[128], pos[128] of one streamed query tile.  Kept apart from the
+  // per side slot: -lse[128], pos[128] of one streamed query tile.  Kept apart from the
   // query tile so that the MMA alone frees a query stage: three epilogue warpgroups
   // holding the stages until they finish would starve the loads.
   float* side = reinterpret_cast<float*>(b_buf + kStages * kTileBytes);
@@ -633,9 +645,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int k = 0, kt = cta_item(0); kt < items; kt = cta_item(++k)) {
       const int key = kt * kTile + key_in_tile;
-      float acc[8];  // eight independent sums of this key's mass
+      float2 acc[4];  // eight independent sums of this key's mass, in pairs
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
+      const float2 scale2 = make_float2(c.scale_log2, c.scale_log2);
       for (int h = 0; h < c.num_kv_heads && ok; ++h) {
         for (int qt = 0; qt < c.q_tiles; ++qt) {
           if (tile_max[qt] < kt * kTile) continue;
@@ -652,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t addr = sh.tmem_base + tb * kTile + (static_cast<uint32_t>(ew * 32) << 16);
-          const float* lse = side + q * 2 * kTile;
+          const float* nlse = side + q * 2 * kTile;  // -lse of each row
           const int* pos = reinterpret_cast<const int*>(side + q * 2 * kTile + kTile);
           const bool full = key <= tile_min[qt];  // every row of the tile sees this key
 #pragma unroll
@@ -665,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               __syncwarp();
               if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
             }
-            const float4* lse4 = reinterpret_cast<const float4*>(lse + quarter * 32);
+            const float4* nlse4 = reinterpret_cast<const float4*>(nlse + quarter * 32);
             const int4* pos4 = reinterpret_cast<const int4*>(pos + quarter * 32);
             if (full) {
 #pragma unroll
@@ -673,11 +686,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float a0, a1, a2, a3;
                 round_pair<T>(v[4 * j], v[4 * j + 1], a0, a1);
                 round_pair<T>(v[4 * j + 2], v[4 * j + 3], a2, a3);
-                const float4 l4 = lse4[j];
-                acc[(4 * j) & 7] += ex2(fmaf(a0, c.scale_log2, -l4.x));
-                acc[(4 * j + 1) & 7] += ex2(fmaf(a1, c.scale_log2, -l4.y));
-                acc[(4 * j + 2) & 7] += ex2(fmaf(a2, c.scale_log2, -l4.z));
-                acc[(4 * j + 3) & 7] += ex2(fmaf(a3, c.scale_log2, -l4.w));
+                const float4 l4 = nlse4[j];
+                const float2 y0 = __ffma2_rn(make_float2(a0, a1), scale2, make_float2(l4.x, l4.y));
+                const float2 y1 = __ffma2_rn(make_float2(a2, a3), scale2, make_float2(l4.z, l4.w));
+                acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], make_float2(ex2(y0.x), ex2(y0.y)));
+                acc[(2 * j + 1) & 3] = __fadd2_rn(acc[(2 * j + 1) & 3], make_float2(ex2(y1.x), ex2(y1.y)));
               }
             } else {
 #pragma unroll
@@ -685,16 +698,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float a0, a1, a2, a3;
                 round_pair<T>(v[4 * j], v[4 * j + 1], a0, a1);
                 round_pair<T>(v[4 * j + 2], v[4 * j + 3], a2, a3);
-                const float4 l4 = lse4[j];
+                const float4 l4 = nlse4[j];
                 const int4 p4 = pos4[j];
-                const float p0 = ex2(fmaf(a0, c.scale_log2, -l4.x));
-                const float p1 = ex2(fmaf(a1, c.scale_log2, -l4.y));
-                const float p2 = ex2(fmaf(a2, c.scale_log2, -l4.z));
-                const float p3 = ex2(fmaf(a3, c.scale_log2, -l4.w));
-                acc[(4 * j) & 7] += key <= p4.x ? p0 : 0.0f;
-                acc[(4 * j + 1) & 7] += key <= p4.y ? p1 : 0.0f;
-                acc[(4 * j + 2) & 7] += key <= p4.z ? p2 : 0.0f;
-                acc[(4 * j + 3) & 7] += key <= p4.w ? p3 : 0.0f;
+                const float2 y0 = __ffma2_rn(make_float2(a0, a1), scale2, make_float2(l4.x, l4.y));
+                const float2 y1 = __ffma2_rn(make_float2(a2, a3), scale2, make_float2(l4.z, l4.w));
+                const float2 e0 = make_float2(key <= p4.x ? ex2(y0.x) : 0.0f, key <= p4.y ? ex2(y0.y) : 0.0f);
+                const float2 e1 = make_float2(key <= p4.z ? ex2(y1.x) : 0.0f, key <= p4.w ? ex2(y1.y) : 0.0f);
+                acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], e0);
+                acc[(2 * j + 1) & 3] = __fadd2_rn(acc[(2 * j + 1) & 3], e1);
               }
             }
             if (quarter == 3) {  // lse / positions of this slot read: release it
@@ -704,7 +715,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      const float mass = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+      const float2 a03 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+      const float mass = a03.x + a03.y;
       // merge the warpgroups' sums for this key tile (reached by every
       // warpgroup for every item, also after an error)
       if (wg > 0) sh.merge[wg - 1][0][key_in_tile] = mass;
