@@ -944,6 +944,84 @@ __global__ void __launch_bounds__(kThreads, 3) blend_load_bulk_kernel(LoadArgs a
   }
 }
 
+
+// ---- flat variant (rows under 1 KiB: one or a few heads per rank) ----------
+// One thread per 16-byte work item of one row: a rotary item (NEOX: E
+// consecutive pairs, i.e. one vector in each half; GPT-J: one vector of E/2
+// pairs) or a pass-through / V-plane vector.  No tiles, no barriers: with rows
+// this small a tile pipeline does a few latency-bound round trips per CTA,
+// while here every thread has its loads in flight at once.  Rows are
+// classified exactly as by the tile kernels (classify_row).
+template <typename T, bool NEOX>
+__global__ void __launch_bounds__(256) blend_load_flat_kernel(LoadArgs a) {
+  constexpr int E = 16 / sizeof(T);
+  const int D = a.rope.head_size;
+  const int R = a.rope.rotary_dim;
+  const int half = R / 2;
+  const int rot_items = NEOX ? R / 2 / E : R / E;
+  const uint32_t k_items = static_cast<uint32_t>(rot_items + (D - R) / E);  // per head, K plane
+  const uint32_t v_items = static_cast<uint32_t>(D / E);                    // per head, V plane
+  const uint32_t k_row = a.num_heads * k_items;
+  const uint32_t v_row = a.num_heads * v_items;
+  const uint32_t nk = static_cast<uint32_t>(a.alloc_end) * k_row;
+  const uint32_t total = nk + static_cast<uint32_t>(a.alloc_end) * v_row;
+  const int head_bytes = D * static_cast<int>(sizeof(T));
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    int plane;
+    uint32_t t, h, c;
+    if (i < nk) {
+      plane = 0;
+      t = i / k_row;
+      const uint32_t r = i - t * k_row;
+      h = r / k_items;
+      c = r - h * k_items;
+    } else {
+      plane = 1;
+      const uint32_t j = i - nk;
+      t = j / v_row;
+      const uint32_t r = j - t * v_row;
+      h = r / v_items;
+      c = r - h * v_items;
+    }
+    const RowMeta m = classify_row(a, a.segments, plane, t, load_raw(a, t), head_bytes, sizeof(T));
+    T* d = reinterpret_cast<T*>(a.out + plane * a.out_plane_stride + t * a.out_token_stride +
+                                h * a.out_head_stride);
+    // element offsets of this item: one vector, or (NEOX rotary) one in each half
+    const bool pair = plane == 0 && NEOX && static_cast<int>(c) < rot_items;
+    const int off0 = plane == 1 ? static_cast<int>(c) * E
+                     : static_cast<int>(c) < rot_items ? static_cast<int>(c) * E
+                                                       : R + (static_cast<int>(c) - rot_items) * E;
+    if (m.kind == kZero) {
+      Pack<T, E> z;
+#pragma unroll
+      for (int e = 0; e < E; ++e) z.v[e] = Elem<T>::from_f(0.0f);
+      store_pack<T, E, true>(d + off0, z);
+      if (pair) store_pack<T, E, true>(d + half + off0, z);
+      continue;
+    }
+    const T* s = reinterpret_cast<const T*>(m.src + static_cast<int64_t>(h) * m.src_hs);
+    const bool aligned = m.kind == kSmemCopy || m.kind == kSmemRotate;
+    const bool rotate = (m.kind == kSmemRotate || m.kind == kDirectRotate) &&
+                        static_cast<int>(c) < rot_items;
+    if (rotate) {
+      const T* old_cs = rope_row<T>(a.rope, m.old_pos);
+      const T* new_cs = rope_row<T>(a.rope, t);
+      if (aligned)
+        relocate_item<T, E, NEOX, true>(s, d, static_cast<int>(c), R, old_cs, new_cs);
+      else
+        relocate_item<T, E, NEOX, false>(s, d, static_cast<int>(c), R, old_cs, new_cs);
+      continue;
+    }
+    if (aligned) {
+      store_pack<T, E, true>(d + off0, load_pack<T, E, true>(s + off0));
+      if (pair) store_pack<T, E, true>(d + half + off0, load_pack<T, E, true>(s + half + off0));
+    } else {
+      store_pack<T, E, true>(d + off0, load_pack<T, E, false>(s + off0));
+      if (pair) store_pack<T, E, true>(d + half + off0, load_pack<T, E, false>(s + half + off0));
+    }
+  }
+}
+
 }  // namespace tma
 
 struct RelocArgs {
@@ -1060,6 +1138,18 @@ int dispatch_load(const LoadArgs& a, bool vec, bool neox, int64_t max_ctas, int3
                   cudaStream_t s) {
   const int64_t row_bytes = (int64_t)a.num_heads * a.rope.head_size * (int64_t)sizeof(T);
   const int64_t cs_bytes = 2 * (int64_t)a.rope.rotary_dim * (int64_t)sizeof(T);
+  const int64_t flat_items = a.alloc_end * (2 * row_bytes / 16);
+  const bool flat_ok = flat_items < (int64_t(1) << 31);
+  if (vec && max_ctas <= 0 && flat_ok && (row_bytes < 1024 || CB_LOAD_VARIANT == 9)) {
+    // device-memory sources, rows under 1 KiB: one thread per 16-byte item
+    const int64_t blocks = (flat_items + 255) / 256;
+    const int grid = static_cast<int>(blocks < kSmCount * 8 ? blocks : kSmCount * 8);
+    if (neox)
+      tma::blend_load_flat_kernel<T, true><<<grid, 256, 0, s>>>(a);
+    else
+      tma::blend_load_flat_kernel<T, false><<<grid, 256, 0, s>>>(a);
+    return launch_status("cb_blend_load_layer");
+  }
   if (vec && max_ctas <= 0 && row_bytes + cs_bytes <= tma::kTileBytes) {
     // device-memory sources: TMA-staged pipeline
     return neox ? launch_tma_load<T, true>(a, error, s) : launch_tma_load<T, false>(a, error, s);

@@ -126,6 +126,16 @@ def test_blend_load_partial_rotary(cuda, neox, token_pad):
     assert np.array_equal(_run(case, cuda, 0, token_pad=token_pad), _expected(case))
 
 
+@pytest.mark.parametrize("heads", [1, 2])
+@pytest.mark.parametrize("hnd,misalign", [(False, False), (True, False), (False, True)])
+@pytest.mark.parametrize("neox,rotary_dim", [(True, 128), (False, 128), (True, 64)])
+def test_blend_load_small_rows(cuda, heads, hnd, misalign, neox, rotary_dim):
+    """Rows under 1 KiB (one or two heads per rank): the one-thread-per-item kernel."""
+    case = _case(cuda, hnd=hnd, misalign=misalign, apc=300, heads=heads, neox=neox,
+                 rotary_dim=rotary_dim, seed=50 + heads + 2 * hnd + 4 * misalign + 8 * neox)
+    assert np.array_equal(_run(case, cuda, 0), _expected(case))
+
+
 @pytest.mark.parametrize("max_ctas", [0, 64])
 def test_blend_load_gptj_matches_oracle(cuda, max_ctas):
     case = _case(cuda, hnd=False, misalign=False, apc=100, seed=21, neox=False)
