@@ -369,16 +369,21 @@ class DevicePath:
         self.graphs = []
 
     def kernel_graph_us(self, stream, reps: int = 20) -> dict[str, float]:
-        """Average launch duration of the per-layer kernels, back to back as in the step:
-        one step's 36 loads (resp. 36 commit scatters) captured in a graph, replayed
-        ``reps`` times between two CUDA events on the launching stream."""
+        """Average launch duration of each kernel, back to back as in the step: one step's
+        36 loads (resp. 36 commit scatters, or ten deviation / select launches) captured
+        in a graph, replayed ``reps`` times between two CUDA events on the launching stream."""
         layers = self.wl.shape.layers
+        check = self.wl.shape.check_layer
         kinds = {
-            "load": lambda: [self.load_layer(layer, stream) for layer in range(layers)],
-            "scatter": lambda: [self.commit(layer, self.staging[layer % 2], stream) for layer in range(layers)],
+            "load": (layers, lambda: [self.load_layer(layer, stream) for layer in range(layers)]),
+            "scatter": (layers, lambda: [self.commit(layer, self.staging[layer % 2], stream)
+                                         for layer in range(layers)]),
+            # single launches per step: ten back to back (same inputs, same outputs)
+            "deviation": (10, lambda: [self.deviation(self.staging[check % 2], stream) for _ in range(10)]),
+            "select": (10, lambda: [self.select(stream) for _ in range(10)]),
         }
         out = {}
-        for name, launch in kinds.items():
+        for name, (count, launch) in kinds.items():
             torch.cuda.synchronize(self.wl.device)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
@@ -392,7 +397,7 @@ class DevicePath:
                     graph.replay()
                 end.record(stream)
             end.synchronize()
-            out[name] = start.elapsed_time(end) * 1e3 / (reps * layers)
+            out[name] = start.elapsed_time(end) * 1e3 / (reps * count)
             del graph
         return out
 
@@ -1049,8 +1054,8 @@ def main() -> None:
             "gpu_launches": path.launches_per_step() * args.steps,
             "launch": "eager" if args.no_graph else ("cuda-graph" if world == 1 else "cuda-graph x2 + NCCL all-reduce"),
             "kernel_timing": ("CUDA events around each launch in an eager pass of the same steps"
-                              + ("" if args.no_graph else "; load/scatter: one step's launches replayed "
-                                 "as a CUDA graph between two events")),
+                              + ("" if args.no_graph else "; avg_us: each kernel's launches of one step "
+                                 "(ten for deviation/select) replayed as a CUDA graph between two events")),
             "roofline": roofline, "kernels": per_kernel, "e2e": e2e,
             "clocks": clocks.summary(), "cpu_baseline": cpu,
         }

@@ -94,7 +94,59 @@ __global__ void __launch_bounds__(256) deviation_kernel(const char* __restrict__
   }
 }
 
-// Order-preserving key: larger float -> larger key.  NaN (either sign) is
+// Rows of at most 32 16-byte units (up to two 128-dim bf16 heads per rank):
+// 32 / units tokens share a warp, one unit per lane, and each lane keeps four
+// tokens' loads in flight.  Same association order as deviation_kernel: a
+// lane's unit sum with fmaf, then the xor butterfly; the butterfly steps of
+// offset >= units that deviation_kernel also takes only add lanes holding
+// +0.0 to a sum of squares (>= 0), so skipping them changes no bit.
+template <typename T>
+__global__ void __launch_bounds__(256) deviation_small_kernel(const char* __restrict__ fresh,
+                                                              int64_t fresh_stride,
+                                                              const char* __restrict__ cached,
+                                                              int64_t cached_stride,
+                                                              int64_t cached_rows,
+                                                              const int64_t* __restrict__ abs_index,
+                                                              int64_t abs_offset, int64_t n,
+                                                              int units_log2,
+                                                              float* __restrict__ scores) {
+  constexpr int R = 4;  // token groups per warp per iteration
+  const int lane = threadIdx.x & 31;
+  const int units = 1 << units_log2;
+  const int per_warp = 32 >> units_log2;     // tokens per warp instruction
+  const int sub = lane >> units_log2;        // this lane's token within the group
+  const int q = lane & (units - 1);          // this lane's unit
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t step = nwarps * per_warp * R;
+  for (int64_t base = warp * per_warp * R; base < n; base += step) {
+    uint4 fv[R], cv[R];
+    bool ok[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t i = base + r * per_warp + sub;
+      ok[r] = false;
+      if (i < n) {
+        const int64_t ai = abs_index ? __ldg(abs_index + i) : abs_offset + i;
+        ok[r] = ai >= 0 && ai < cached_rows;  // never read outside the cached rows
+        if (ok[r]) {
+          fv[r] = ld_stream(reinterpret_cast<const uint4*>(fresh + i * fresh_stride) + q);
+          cv[r] = ld_stream(reinterpret_cast<const uint4*>(cached + ai * cached_stride) + q);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float v = 0.0f;
+      if (ok[r]) acc_vec16<T>(fv[r], cv[r], v);
+      for (int o = units >> 1; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+      const int64_t i = base + r * per_warp + sub;
+      if (q == 0 && i < n) scores[i] = ok[r] ? v : __int_as_float(0x7fc00000);
+    }
+  }
+}
+
+// Order-preserving key: larger float -> larger key.// Order-preserving key: larger float -> larger key.  NaN (either sign) is
 // the largest, -0.0 equals +0.0.
 __device__ __forceinline__ uint32_t order_key(float f) {
   if (f != f) return 0xffffffffu;
@@ -420,9 +472,24 @@ extern "C" int cb_kv_deviation(const void* fresh, int64_t fresh_row_stride, cons
   const char* f = static_cast<const char*>(fresh);
   const char* c = static_cast<const char*>(cached);
   const int w = static_cast<int>(width);
+  const int64_t units = width * esize / 16;
+  int units_log2 = 0;
+  while ((int64_t(1) << units_log2) < units) ++units_log2;
+  const bool small = vec && units <= 32 && (int64_t(1) << units_log2) == units;
+  int small_grid = 0;
+  if (small) {
+    const int64_t per_block = 8 * (32 >> units_log2) * 4;  // tokens per block per iteration
+    const int64_t small_blocks = (num_tokens + per_block - 1) / per_block;
+    small_grid = static_cast<int>(small_blocks < kSmCount * 8 ? small_blocks : kSmCount * 8);
+  }
 #define CB_DEV_LAUNCH(T)                                                                      \
   do {                                                                                        \
-    if (vec)                                                                                  \
+    if (small)                                                                                \
+      deviation_small_kernel<T><<<small_grid, 256, 0, s>>>(f, fresh_row_stride, c,            \
+                                                           cached_row_stride, cached_rows,    \
+                                                           abs_index, abs_offset, num_tokens, \
+                                                           units_log2, scores);               \
+    else if (vec)                                                                             \
       deviation_kernel<T, true><<<grid, 256, 0, s>>>(f, fresh_row_stride, c,                  \
                                                      cached_row_stride, cached_rows, abs_index,\
                                                      abs_offset, num_tokens, w, scores);      \

@@ -245,7 +245,10 @@ def test_deviation_golden_and_oracle(golden, cuda):
 
 
 @pytest.mark.parametrize("width,dtype", [(1024, torch.bfloat16), (512, torch.float16), (256, torch.float32),
-                                         (100, torch.bfloat16)])
+                                         (100, torch.bfloat16),
+                                         # rows of <= 32 16-byte units: tokens packed per warp
+                                         (256, torch.bfloat16), (128, torch.bfloat16), (64, torch.float16),
+                                         (32, torch.float32), (8, torch.bfloat16)])
 def test_deviation_bit_exact_vs_oracle(cuda, width, dtype):
     gen = torch.Generator(device=cuda).manual_seed(width)
     n, total = 3000, 4000
@@ -257,6 +260,21 @@ def test_deviation_bit_exact_vs_oracle(cuda, width, dtype):
     assert np.array_equal(scores.cpu().numpy(), want)
     ref = ((fresh.float() - cached[500 : 500 + n].float()) ** 2).sum(-1)
     torch.testing.assert_close(scores, ref, rtol=1e-5, atol=0)
+
+
+@pytest.mark.parametrize("width", [128, 1024])
+def test_deviation_out_of_range_rows_are_nan(cuda, width):
+    gen = torch.Generator(device=cuda).manual_seed(7)
+    cached = torch.randn(100, width, generator=gen, device=cuda).to(torch.bfloat16)
+    fresh = torch.randn(37, width, generator=gen, device=cuda).to(torch.bfloat16)
+    index = torch.arange(37, dtype=torch.int64) * 2  # in range except the three set below
+    index[[0, 5, 36]] = torch.tensor([-1, 100, 500])
+    scores = kv_deviation(fresh, cached, index).cpu().numpy()
+    want = oracle.kv_deviation(bits(fresh), bits(cached), oracle.BF16, abs_index=index.numpy().clip(0, 99))
+    bad = np.zeros(37, dtype=bool)
+    bad[[0, 5, 36]] = True
+    assert np.isnan(scores[bad]).all()
+    assert np.array_equal(scores[~bad], want[~bad])
 
 
 @pytest.mark.parametrize("case", range(6))
