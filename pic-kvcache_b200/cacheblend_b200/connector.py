@@ -304,10 +304,12 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
                 continue
             usable = min(request.save_end, len(request.token_ids), request.slot_mapping.numel())
             usable = usable // chunk * chunk
+            segments = self._request_save_segments(request, usable)
+            reserved = self._store.reserve_layers([sid for _, sid in segments], layer_id)
             pending: list[tuple[Any, int, int]] = []
             starts: list[int] = []
-            for start, segment_id in self._request_save_segments(request, usable):
-                if not self._store.reserve_layer(segment_id, layer_id):
+            for (start, segment_id), ok in zip(segments, reserved):
+                if not ok:
                     continue
                 pending.append((segment_id, layer_id, chunk))
                 starts.append(start)

@@ -136,14 +136,22 @@ class LocalPinnedCPUStore:
     def reserve_layer(self, segment_id: SegmentId, layer_id: int) -> bool:
         """Claim one layer for an asynchronous transfer; False if already present/claimed."""
         with self._lock:
-            entry = self._entries.get(segment_id)
-            if entry is None:
-                return False
-            self._check_layer(entry, layer_id)
-            if entry.failed or layer_id in entry.layers or layer_id in entry.reserved_layers:
-                return False
-            entry.reserved_layers.add(layer_id)
-            return True
+            return self._reserve(segment_id, layer_id)
+
+    def reserve_layers(self, segment_ids: Sequence[SegmentId], layer_id: int) -> list[bool]:
+        """``reserve_layer`` for each segment in order, under one lock acquisition."""
+        with self._lock:
+            return [self._reserve(sid, layer_id) for sid in segment_ids]
+
+    def _reserve(self, segment_id: SegmentId, layer_id: int) -> bool:
+        entry = self._entries.get(segment_id)
+        if entry is None:
+            return False
+        self._check_layer(entry, layer_id)
+        if entry.failed or layer_id in entry.layers or layer_id in entry.reserved_layers:
+            return False
+        entry.reserved_layers.add(layer_id)
+        return True
 
     def cancel_layer(self, segment_id: SegmentId, layer_id: int) -> None:
         with self._lock:
@@ -162,42 +170,59 @@ class LocalPinnedCPUStore:
         if cpu_tensor.device.type != "cpu":
             raise ValueError("put_layer_host requires a CPU tensor")
         with self._lock:
-            entry = self._entries.get(segment_id)
-            if entry is None:
-                return None
-            self._check_layer(entry, layer_id)
-            if entry.failed:
-                entry.reserved_layers.discard(layer_id)
-                if entry.idle():
-                    self._remove(segment_id, entry)
-                return None
-            if entry.committed:
-                entry.reserved_layers.discard(layer_id)
-                return False  # content-addressed entries are immutable
-            old = entry.layers.get(layer_id)
-            old_bytes = _nbytes(old) if old is not None else 0
-            growth = _nbytes(cpu_tensor) - old_bytes
-            if growth > 0:
-                self._evict(required_bytes=growth, exclude=segment_id)
-            if self._bytes + growth > self.max_bytes:
-                # fail closed: never expose a partial entry, never exceed the cap
-                entry.reserved_layers.discard(layer_id)
-                entry.failed = True
-                if entry.idle():
-                    self._remove(segment_id, entry)
-                return None
+            return self._put_host(segment_id, layer_id, cpu_tensor, _nbytes(cpu_tensor))
+
+    def put_layers_host(
+        self, segment_ids: Sequence[SegmentId], layer_id: int, cpu_tensors: Sequence[torch.Tensor]
+    ) -> list[bool | None]:
+        """``put_layer_host`` for each (segment, tensor) pair in order, under one lock
+        acquisition (the Store path publishes a whole batch of one layer at once)."""
+        if len(segment_ids) != len(cpu_tensors):
+            raise ValueError("one tensor per segment is required")
+        if any(t.device.type != "cpu" for t in cpu_tensors):
+            raise ValueError("put_layer_host requires a CPU tensor")
+        with self._lock:
+            return [self._put_host(sid, layer_id, t, _nbytes(t)) for sid, t in zip(segment_ids, cpu_tensors)]
+
+    def _put_host(
+        self, segment_id: SegmentId, layer_id: int, cpu_tensor: torch.Tensor, nbytes: int
+    ) -> bool | None:
+        entry = self._entries.get(segment_id)
+        if entry is None:
+            return None
+        self._check_layer(entry, layer_id)
+        if entry.failed:
             entry.reserved_layers.discard(layer_id)
-            entry.layers[layer_id] = cpu_tensor
-            entry.size_bytes += growth
-            self._bytes += growth
-            entry.last_access = time.monotonic()
-            newly_committed = not entry.committed and len(entry.layers) == entry.num_layers
-            if newly_committed:
-                entry.committed = True
-                self.matcher.register(entry.record)
-                self._committed[segment_id] = entry
-            self._touch(segment_id, entry)
-            return newly_committed
+            if entry.idle():
+                self._remove(segment_id, entry)
+            return None
+        if entry.committed:
+            entry.reserved_layers.discard(layer_id)
+            return False  # content-addressed entries are immutable
+        old = entry.layers.get(layer_id)
+        old_bytes = _nbytes(old) if old is not None else 0
+        growth = nbytes - old_bytes
+        if growth > 0:
+            self._evict(required_bytes=growth, exclude=segment_id)
+        if self._bytes + growth > self.max_bytes:
+            # fail closed: never expose a partial entry, never exceed the cap
+            entry.reserved_layers.discard(layer_id)
+            entry.failed = True
+            if entry.idle():
+                self._remove(segment_id, entry)
+            return None
+        entry.reserved_layers.discard(layer_id)
+        entry.layers[layer_id] = cpu_tensor
+        entry.size_bytes += growth
+        self._bytes += growth
+        entry.last_access = time.monotonic()
+        newly_committed = not entry.committed and len(entry.layers) == entry.num_layers
+        if newly_committed:
+            entry.committed = True
+            self.matcher.register(entry.record)
+            self._committed[segment_id] = entry
+        self._touch(segment_id, entry)
+        return newly_committed
 
     def abort_put(self, segment_id: SegmentId) -> None:
         with self._lock:

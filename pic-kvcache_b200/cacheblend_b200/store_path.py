@@ -150,10 +150,16 @@ class StorePipeline:
     # ------------------------------------------------------------- publish
     def publish_host_batch(self, pending: list[tuple[Any, int, int]], host: torch.Tensor) -> bool:
         """Publish each chunk of a chunk-major host batch as a view (no host copy)."""
-        committed = False
         views = host.unbind(0)
-        for index, (segment_id, layer_id, _length) in enumerate(pending):
-            result = self.store.put_layer_host(segment_id, layer_id, views[index])
+        layer_id = pending[0][1] if pending else 0
+        if all(layer == layer_id for _, layer, _ in pending):
+            results = self.store.put_layers_host([sid for sid, _, _ in pending], layer_id,
+                                                 views[: len(pending)])
+        else:
+            results = [self.store.put_layer_host(sid, layer, views[i])
+                       for i, (sid, layer, _) in enumerate(pending)]
+        committed = False
+        for result in results:
             if result is not None:
                 committed |= result
         return committed

@@ -327,6 +327,9 @@ class RecordingStore:
         self.layers.append((segment_id, layer_id, tensor))
         return True
 
+    def put_layers_host(self, segment_ids, layer_id, tensors):
+        return [self.put_layer_host(sid, layer_id, t) for sid, t in zip(segment_ids, tensors)]
+
     def abort_put(self, segment_id):
         self.aborted.append(segment_id)
 

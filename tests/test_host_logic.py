@@ -161,3 +161,27 @@ def test_sparse_q_masks_match_oracle(radius_blocks, tail):
         want = oracle.sparse_q_masks(gaps, 16, radius_blocks, tail)
         assert np.array_equal(got[0], want[0]) and np.array_equal(got[1], want[1])
         assert got[2] == want[2]
+
+
+def test_batched_reserve_and_publish_match_single_calls():
+    """reserve_layers / put_layers_host == the single-chunk calls in order (one lock)."""
+    import torch
+
+    from cacheblend_b200.storage import LocalPinnedCPUStore
+
+    def run(batched: bool):
+        store = LocalPinnedCPUStore(4, 3 * 2 * 2 * 4 * 4, pin_memory=False)  # room for ~3 chunk-layers of 2 layers
+        ids = [store.begin_put("m", 4 * i, [10 * i + j for j in range(4)], 2) for i in range(5)]
+        log = []
+        for layer in range(2):
+            ok = store.reserve_layers(ids, layer) if batched else [store.reserve_layer(s, layer) for s in ids]
+            log.append(ok)
+            views = [torch.full((2, 4, 2), float(layer * 10 + i)) for i in range(5)]
+            picked = [s for s, o in zip(ids, ok) if o]
+            tensors = [v for v, o in zip(views, ok) if o]
+            res = (store.put_layers_host(picked, layer, tensors) if batched
+                   else [store.put_layer_host(s, layer, t) for s, t in zip(picked, tensors)])
+            log.append(res)
+        return log, store.entry_order(), store.current_bytes, store.committed_entries
+
+    assert run(True) == run(False)
