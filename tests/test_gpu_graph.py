@@ -1,6 +1,7 @@
 """The hot-path C-ABI calls can be captured in a CUDA graph: a captured
 blend-request step (fused load, deviation, cluster top-k, commit scatter over
-every layer) replays to exactly the pages and selection of eager launches."""
+every layer; for small rows with the loads on a second stream) replays to
+exactly the pages and selection of eager launches."""
 
 from __future__ import annotations
 
@@ -12,11 +13,13 @@ import bench
 pytestmark = pytest.mark.gpu
 
 
-def test_graph_replay_matches_eager(cuda):
+@pytest.mark.parametrize("shard", [1, 8])
+def test_graph_replay_matches_eager(cuda, shard):
+    """shard 8 (one head per rank) also runs the two-stream pipelined capture."""
     from dataclasses import replace
 
-    shape = replace(bench.CONFIGS[1], layers=4)
-    wl = bench.Workload(shape, 1, 0, cuda, host_store=False)
+    shape = replace(bench.CONFIGS[1], layers=6)
+    wl = bench.Workload(shape, shard, 0, cuda, host_store=False)
     path = bench.DevicePath(wl)
     stream = torch.cuda.Stream(cuda)
     with torch.cuda.stream(stream):
