@@ -96,6 +96,17 @@ CB_API int cb_paged_scatter(const void* src, int64_t src_plane_stride, int64_t s
                      const int64_t* slots, int64_t num_tokens, void* stream);
 
 /*
+ * Number of common entries of two strictly ascending int64 index lists
+ * (device memory), written to *count (device memory) on `stream`.  The
+ * overlap of the two selections that the `compare` strategy reports
+ * (cacheblend_vllm/ascend.py:713-747: overlap_tokens, and with the list
+ * lengths the union and Jaccard index) without building the reference's two
+ * boolean masks.
+ */
+CB_API int cb_sorted_overlap(const int64_t* a, int64_t na, const int64_t* b, int64_t nb,
+                             int64_t* count, void* stream);
+
+/*
  * Failure word of the bulk-copy paged gather/scatter kernels on the stream's
  * device (0: none; 1: a bounded wait for a bulk copy gave up and the launch
  * stopped early).  Synchronizes `stream`, stores the word in *value and

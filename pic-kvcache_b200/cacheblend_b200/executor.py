@@ -20,7 +20,7 @@ import torch
 from .config import CacheBlendConfig
 from .loader import PagedBlendLoader
 from .rope import validate_rope_support
-from .selection import kv_deviation, select_tokens, sparse_q_scores
+from .selection import kv_deviation, select_tokens, selection_overlap, sparse_q_scores
 from .trace import PipelineTracer
 from .types import BlendPlan
 
@@ -143,6 +143,12 @@ class Qwen3BlendExecutor:
                 float(attn.impl.scale),
             )
             sparse_q_selected = self._select(scores, active_gap_mask, layer_id, forced_mask=forced)
+        if check_layer and strategy == "compare" and tracer is not None and tracer.enabled:
+            overlap, union = selection_overlap(deviation_selected, sparse_q_selected)
+            tracer.emit("selection_compared", request_id=request_id, layer_id=layer_id,
+                        deviation_tokens=deviation_selected.numel(),
+                        sparse_q_tokens=sparse_q_selected.numel(), overlap_tokens=overlap,
+                        jaccard=overlap / max(union, 1), **stats)
         if check_layer and strategy in {"kv_deviation", "compare"}:
             selected = deviation_selected
             q, k, v = q[selected], k[selected], v[selected]

@@ -300,3 +300,17 @@ def sparse_q_scores(
     }
     forced_dev = torch.from_numpy(forced).to(query.device, non_blocking=True)
     return scores, forced_dev, stats
+
+
+def selection_overlap(a: torch.Tensor, b: torch.Tensor) -> tuple[int, int]:
+    """(overlap, union) of two ascending selections on the device (cb_sorted_overlap):
+    the ``compare`` strategy's diagnostic (ascend.py:713-747) with one 8-byte read back
+    instead of two boolean masks and three synchronisations."""
+    _native.require_cuda(a, b)
+    a = a.to(torch.long).contiguous()
+    b = b.to(device=a.device, dtype=torch.long).contiguous()
+    count = torch.empty(1, dtype=torch.long, device=a.device)
+    _native.call("cb_sorted_overlap", a.data_ptr(), a.numel(), b.data_ptr(), b.numel(), count.data_ptr(),
+                 _native.stream_handle())
+    overlap = int(count.item())
+    return overlap, a.numel() + b.numel() - overlap

@@ -445,6 +445,33 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
   }
 }
 
+// |A n B| of two strictly ascending index lists (the two selections of the
+// `compare` strategy, ascend.py:713-747): each thread binary-searches its A
+// entries in B; per-warp sums, one atomic per warp.
+__global__ void __launch_bounds__(256) sorted_overlap_kernel(const int64_t* __restrict__ a,
+                                                             int64_t na,
+                                                             const int64_t* __restrict__ b,
+                                                             int64_t nb,
+                                                             unsigned long long* __restrict__ count) {
+  unsigned long long local = 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < na; i += stride) {
+    const int64_t x = __ldg(a + i);
+    int64_t lo = 0, hi = nb;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (__ldg(b + mid) < x)
+        lo = mid + 1;
+      else
+        hi = mid;
+    }
+    local += (lo < nb && __ldg(b + lo) == x) ? 1ull : 0ull;
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+  if ((threadIdx.x & 31) == 0 && local) atomicAdd(count, local);
+}
+
 }  // namespace
 }  // namespace cb
 
@@ -548,4 +575,24 @@ extern "C" int cb_select_topk(const float* scores, const uint8_t* base_mask, int
   }
   select_topk_kernel<<<1, kSelThreads, 0, s>>>(scores, base_mask, n, k, out_index, out_capacity);
   return launch_status("cb_select_topk");
+}
+
+extern "C" int cb_sorted_overlap(const int64_t* a, int64_t na, const int64_t* b, int64_t nb,
+                                 int64_t* count, void* stream) {
+  CB_BIND(stream, count);
+  CB_REQUIRE(na >= 0 && nb >= 0, "negative list length");
+  CB_REQUIRE(count != nullptr, "null count");
+  CB_REQUIRE((na == 0 || a != nullptr) && (nb == 0 || b != nullptr), "null pointer argument");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(count, 0, sizeof(int64_t), s);
+  if (e != cudaSuccess) {
+    set_error("cb_sorted_overlap: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  if (na == 0 || nb == 0) return CB_OK;
+  const int64_t blocks = (na + 255) / 256;
+  const int grid = static_cast<int>(blocks < kSmCount * 4 ? blocks : kSmCount * 4);
+  sorted_overlap_kernel<<<grid, 256, 0, s>>>(a, na, b, nb,
+                                             reinterpret_cast<unsigned long long*>(count));
+  return launch_status("cb_sorted_overlap");
 }

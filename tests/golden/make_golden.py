@@ -16,6 +16,7 @@ Covered reference functions (file:line in the reference):
   ascend.Qwen3BlendExecutor._select                   ascend.py:757-796
   ascend.Qwen3BlendExecutor._sparse_q_scores          ascend.py:638-711
   storage.LocalPinnedCPUStore (op sequence)           storage.py:56-294
+  hashing.content_hash / rolling_hash_values          hashing.py:18-53  (hashes.npz)
 """
 
 from __future__ import annotations
@@ -32,6 +33,22 @@ import torch
 
 OUT = Path(__file__).resolve().parent / "golden.npz"
 STORE_OUT = Path(__file__).resolve().parent / "store_sequence.json"
+HASH_OUT = Path(__file__).resolve().parent / "hashes.npz"
+
+
+def make_hash_golden() -> None:
+    """Reference fingerprints (hashing.py:18-53): every 256-token window of a seeded prompt
+    (token ids up to 2**31 and a negative one) and the content hash of each chunk."""
+    from cacheblend_vllm.hashing import content_hash, rolling_hash_values
+
+    rng = np.random.default_rng(31)
+    tokens = rng.integers(0, 151_936, size=4096).astype(np.int64)
+    tokens[[5, 700, 3000]] = [2**31 - 1, 0, 123_456_789]
+    windows = rolling_hash_values(tokens.tolist(), 256)
+    chunks = np.array([content_hash(tokens[i : i + 256].tolist()) for i in range(0, 4096, 256)],
+                      dtype=np.uint64)
+    small = np.array([content_hash([7]), content_hash([-1, 0, 1]), content_hash([])], dtype=np.uint64)
+    np.savez_compressed(HASH_OUT, tokens=tokens, windows=windows, chunks=chunks, small=small)
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -269,6 +286,7 @@ def main() -> None:
         )
 
     np.savez_compressed(OUT, **gold)
+    make_hash_golden()
 
     # ---- 7. store op sequence: every call, its result, bytes and LRU order
     rng = np.random.default_rng(7)

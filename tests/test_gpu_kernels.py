@@ -334,3 +334,15 @@ def test_deviation_select_full_cfg4_size(cuda):
     got = select_tokens(scores, gaps, 0.15).cpu().numpy()
     assert np.array_equal(got, oracle.select(want, gaps, 0.15))
     assert np.all(np.diff(got) > 0)
+
+
+@pytest.mark.parametrize("na,nb", [(0, 5), (5, 0), (1, 1), (1000, 3000), (70000, 90000)])
+def test_selection_overlap_vs_numpy(cuda, na, nb):
+    from cacheblend_b200.selection import selection_overlap
+
+    rng = np.random.default_rng(na + nb)
+    universe = max(na, nb) * 2 + 1
+    a = np.sort(rng.choice(universe, size=na, replace=False))
+    b = np.sort(rng.choice(universe, size=nb, replace=False))
+    overlap, union = selection_overlap(torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda))
+    assert overlap == len(np.intersect1d(a, b)) and union == len(np.union1d(a, b))

@@ -4,6 +4,8 @@ fingerprints, the recompute budget and the Sparse-Q masks."""
 
 from __future__ import annotations
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -185,3 +187,17 @@ def test_batched_reserve_and_publish_match_single_calls():
         return log, store.entry_order(), store.current_bytes, store.committed_entries
 
     assert run(True) == run(False)
+
+
+def test_fingerprints_match_reference_vectors():
+    """The reference's own hashing.rolling_hash_values / content_hash outputs (hashes.npz):
+    the O(N) window hashes, the per-chunk vectorised hashes and the scalar form agree."""
+    from cacheblend_b200.matcher import TokenRangeMatcher, chunk_hashes
+
+    gold = np.load(Path(__file__).resolve().parent / "golden" / "hashes.npz")
+    tokens = gold["tokens"]
+    assert np.array_equal(window_hashes(tokens, 256), gold["windows"])
+    assert np.array_equal(chunk_hashes(tokens.reshape(16, 256)), gold["chunks"])
+    assert [content_hash([7]), content_hash([-1, 0, 1]), content_hash([])] == gold["small"].tolist()
+    records = TokenRangeMatcher(256).make_records("m", 0, tokens.tolist(), 16)
+    assert [r.segment_id.content_hash for r in records] == gold["chunks"].tolist()
