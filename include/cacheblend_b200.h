@@ -208,6 +208,37 @@ CB_API int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t
                    int64_t* out_index, int64_t out_capacity, void* stream);
 
 /*
+ * Workspace bytes cb_blend_attention needs (dense per-KV-head query rows, the
+ * transposed values, row positions and tile bounds).  Same shape limits as
+ * Sparse-Q: head_size 128, bf16 or fp16, (q heads / KV heads) dividing 128.
+ */
+CB_API int cb_blend_attention_workspace_size(int64_t num_queries, int64_t num_keys,
+                                             int64_t num_q_heads, int64_t num_kv_heads,
+                                             int64_t head_size, int dtype, int64_t* bytes);
+
+/*
+ * Causal attention of the computed queries over the whole staging context
+ * (Qwen3BlendExecutor._attention, cacheblend_vllm/ascend.py:798-846, its
+ * einsum path): query [num_queries][num_q_heads][head_size] at absolute
+ * positions query_positions[i] (device int64, each in [0, num_keys)), key and
+ * value [num_keys][num_kv_heads][head_size] (staging rows = positions),
+ * query head h attends KV head h / (num_q_heads / num_kv_heads):
+ *   w = T(T(q . k) * scale), p = softmax over keys k <= pos of w (fp32),
+ *   out = T(sum_k p v).
+ * Strides in bytes, rows and heads 16-byte aligned, heads contiguous within a
+ * row.  On the tensor cores: QK^T and PV with tcgen05.mma, accumulators in
+ * TMEM, operands staged by TMA; device_error (optional) receives a code if a
+ * bounded wait gives up.
+ */
+CB_API int cb_blend_attention(const void* query, int64_t query_token_stride, const void* key,
+                              int64_t key_token_stride, const void* value,
+                              int64_t value_token_stride, int64_t num_keys, int64_t num_q_heads,
+                              int64_t num_kv_heads, int64_t head_size, int dtype,
+                              const int64_t* query_positions, int64_t num_queries, float scale,
+                              void* out, int64_t out_token_stride, void* workspace,
+                              int64_t workspace_bytes, int32_t* device_error, void* stream);
+
+/*
  * Workspace bytes cb_sparse_q_scores needs for `num_queries` sparse queries
  * (dense per-KV-head query rows, per-row log-sum-exp, row positions, tile
  * position bounds).  head_size must be 128, dtype bf16 or fp16, and the query

@@ -97,6 +97,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_ptr, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i32, _ptr, _ptr],
     ),
     "cb_select_topk": (_i32, [_ptr, _ptr, _i64, _i64, _ptr, _i64, _ptr]),
+    "cb_blend_attention_workspace_size": (_i32, [_i64, _i64, _i64, _i64, _i64, _i32, _ptr]),
+    "cb_blend_attention": (
+        _i32,
+        [_ptr, _i64, _ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _i64,
+         ctypes.c_float, _ptr, _i64, _ptr, _i64, _ptr, _ptr],
+    ),
     "cb_sparse_q_workspace_size": (_i32, [_i64, _i64, _i64, _i64, _i32, _ptr]),
     "cb_sparse_q_scores": (
         _i32,

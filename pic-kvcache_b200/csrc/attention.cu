@@ -1,0 +1,599 @@
+// Blend attention: the side executor's attention of the computed (possibly
+// pruned) queries over the whole staging context, on the 5th-generation
+// tensor cores.
+//
+// Semantics: Qwen3BlendExecutor._attention (cacheblend_vllm/ascend.py:798-846,
+// its einsum path).  For query q at absolute position pos_q, query head
+// hq = hk * groups + g, and staging key k (position k):
+//   w   = round_T(round_T(q . k) * scale)        (bf16/fp16 einsum output, scaled in T)
+//   p   = softmax over k <= pos_q of w           (fp32; keys k > pos_q get 0)
+//   out = round_T(sum_k p * v)                   (fp32 accumulation)
+// The reference rounds the normalized probabilities to T before the second
+// product; here the unnormalized exp2 values are rounded to T and the sum is
+// divided at the end (flash-attention order), a difference within one T ulp
+// per probability.
+//
+// Layout: rows = (query, group) pairs of one KV head, r = qi * groups + g, in
+// 128-row tiles (dense copy Qd[h][r][:] made by prep_kernel), so every K / V
+// tile is shared by all groups of the head.  V is transposed per head (Vt[h][d][k],
+// transpose_kernel) so that both products use K-major SWIZZLE_128B operands:
+//   S = Q K^T   A = Q tile [rows][dims],  B = K tile [keys][dims]   -> TMEM (two buffers)
+//   O += P V    A = P tile [rows][keys],  B = Vt tile [dims][keys]  -> TMEM (one accumulator)
+// Per CTA (persistent, items (head, query tile) dealt serpentine, latest
+// queries first): warp 0 issues the TMA loads (Q per item; K and Vt per key
+// tile, two stages), warp 1 lane 0 issues tcgen05.mma (S of tile t, then P V of
+// tile t-1, so the tensor core computes ahead of the softmax), warp 2 owns the
+// TMEM allocation, warps 4-7 (one row per thread) read S with tcgen05.ld, apply
+// the reference's roundings and the causal mask, keep an online max / sum in
+// the log2 domain, write P (rounded to T) into shared memory in the SW128
+// layout the MMA reads, and at the end of an item read O, divide by the sum and
+// store the output rows.  O is rescaled (tcgen05.ld / st) only when a row's max
+// grows by more than 2^8: until then the stale max keeps every exp2 <= 256, and
+// the final division uses the same max, so the result is unchanged.
+// Every mbarrier wait is bounded (2 s): a wait that runs out records a code in
+// *device_error, the CTA drains its MMAs and loads, frees TMEM and returns.
+#include <algorithm>
+#include <type_traits>
+
+#include "cb_common.cuh"
+#include "cb_tcgen05.cuh"
+
+namespace cb {
+namespace att {
+using namespace ::cb::tc;
+
+constexpr int kHead = 128;
+constexpr int kKvStages = 2;
+constexpr int kThreads = 256;      // warps 0-3 roles above, 4-7 softmax / epilogue
+constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
+constexpr uint32_t kTmemO = 256;
+constexpr float kRescaleLog2 = 8.0f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Shared {
+  uint64_t q_full, q_empty;
+  uint64_t kv_full[kKvStages], kv_empty[kKvStages];
+  uint64_t s_full[2], s_empty[2];
+  uint64_t p_full, pv_done, o_empty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct Params {
+  int num_kv_heads;
+  int groups;
+  int rows_pad;
+  int q_tiles;
+  int64_t num_queries;
+  float scale;
+  const int32_t* row_pos;   // [rows_pad]: position of each row, -1 for padding
+  const int32_t* tile_max;  // [q_tiles]
+  char* out;
+  int64_t out_token_stride;  // bytes
+  int32_t* error;
+};
+
+template <typename T>
+__host__ __device__ constexpr uint32_t instr_desc() {
+  constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(kTile >> 3) << 17) |
+         ((uint32_t)(kTile >> 4) << 24);
+}
+
+__device__ __forceinline__ void report(const Params& c, Shared& sh, int code) {
+  if (c.error != nullptr) atomicCAS(c.error, 0, code);
+  *reinterpret_cast<volatile int*>(&sh.abort) = 1;
+}
+__device__ __forceinline__ bool aborted(Shared& sh) {
+  return *reinterpret_cast<volatile int*>(&sh.abort) != 0;
+}
+
+__device__ __forceinline__ int cta_item(int k) {
+  const int g = static_cast<int>(gridDim.x);
+  const int c = static_cast<int>(blockIdx.x);
+  return k * g + ((k & 1) ? g - 1 - c : c);
+}
+
+// Value rounded to T (round to nearest even) and widened back to fp32.
+template <typename T>
+__device__ __forceinline__ float round_t(float x) {
+  return Elem<T>::to_f(Elem<T>::from_f(x));
+}
+// Two fp32 values rounded to T and packed (low half = a).
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap q_map,
+                     const __grid_constant__ CUtensorMap k_map,
+                     const __grid_constant__ CUtensorMap vt_map, Params c) {
+  extern __shared__ __align__(1024) unsigned char dyn[];
+  __shared__ Shared sh;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dyn) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* q_buf = base;                                // Q tile
+  unsigned char* kv_buf = base + kTileBytes;                  // stages x (K tile, Vt tile)
+  unsigned char* p_buf = base + (1 + 2 * kKvStages) * kTileBytes;  // P tile
+  const int items = c.num_kv_heads * c.q_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sh.q_full, 1);
+    mbar_init(&sh.q_empty, 1);
+    for (int s = 0; s < kKvStages; ++s) {
+      mbar_init(&sh.kv_full[s], 1);
+      mbar_init(&sh.kv_empty[s], 2);  // after S (reads K) and after P V (reads Vt)
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.s_full[i], 1);
+      mbar_init(&sh.s_empty[i], 4);
+    }
+    mbar_init(&sh.p_full, 4);
+    mbar_init(&sh.pv_done, 1);
+    mbar_init(&sh.o_empty, 4);
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&sh.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int t = 0, it = 0;
+      int kv_armed[kKvStages];
+      for (int s = 0; s < kKvStages; ++s) kv_armed[s] = -1;
+      int q_armed = -1;
+      for (int k = 0, item = cta_item(0); item < items && !aborted(sh); item = cta_item(++k), ++it) {
+        const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+        const int h = item % c.num_kv_heads;
+        if (!wait1(&sh.q_empty, (it & 1) ^ 1)) { report(c, sh, 1); break; }
+        mbar_expect_tx(&sh.q_full, kTileBytes);
+        tma_load_3d(q_buf, &q_map, &sh.q_full, 0, qt * kTile, h);
+        tma_load_3d(q_buf + kHalfBytes, &q_map, &sh.q_full, 64, qt * kTile, h);
+        q_armed = it & 1;
+        const int kt_end = max(c.tile_max[qt], 0) / kTile;  // the last tile holds a real row
+        bool ok = true;
+        for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+          const int s = t % kKvStages;
+          if (!wait1(&sh.kv_empty[s], ((t / kKvStages) & 1) ^ 1)) { ok = false; break; }
+          mbar_expect_tx(&sh.kv_full[s], 2 * kTileBytes);
+          unsigned char* kb = kv_buf + s * 2 * kTileBytes;
+          tma_load_3d(kb, &k_map, &sh.kv_full[s], 0, h, kt * kTile);
+          tma_load_3d(kb + kHalfBytes, &k_map, &sh.kv_full[s], 64, h, kt * kTile);
+          tma_load_3d(kb + kTileBytes, &vt_map, &sh.kv_full[s], kt * kTile, 0, h);
+          tma_load_3d(kb + kTileBytes + kHalfBytes, &vt_map, &sh.kv_full[s], kt * kTile + 64, 0, h);
+          kv_armed[s] = (t / kKvStages) & 1;
+        }
+        if (!ok) { report(c, sh, 1); break; }
+      }
+      // every armed load has landed before the CTA may exit
+      for (int s = 0; s < kKvStages; ++s)
+        if (kv_armed[s] >= 0) wait1(&sh.kv_full[s], kv_armed[s]);
+      if (q_armed >= 0) wait1(&sh.q_full, q_armed);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc<T>();
+      const uint32_t q_addr = smem_u32(q_buf);
+      const uint32_t kv_addr = smem_u32(kv_buf);
+      const uint32_t p_addr = smem_u32(p_buf);
+      const uint32_t o_tmem = sh.tmem_base + kTmemO;
+      int t = 0, it = 0;
+      bool ok = true;
+      // P V of tile u (its P is in shared memory once p_full completes)
+      auto issue_pv = [&](int u, bool first_of_item) -> bool {
+        if (!wait1(&sh.p_full, u & 1)) return false;
+        if (first_of_item && !wait1(&sh.o_empty, (it & 1) ^ 1)) return false;
+        tc_fence_after();
+        const uint32_t vt = kv_addr + (u % kKvStages) * 2 * kTileBytes + kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          umma(o_tmem, operand_desc(p_addr, kk), operand_desc(vt, kk), idesc,
+               (first_of_item && kk == 0) ? 0u : 1u);
+        umma_commit(&sh.pv_done);
+        umma_commit(&sh.kv_empty[u % kKvStages]);
+        return true;
+      };
+      for (int k = 0, item = cta_item(0); item < items && ok && !aborted(sh); item = cta_item(++k), ++it) {
+        const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+        if (!wait1(&sh.q_full, it & 1)) { ok = false; break; }
+        const int kt_end = max(c.tile_max[qt], 0) / kTile;
+        for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+          const int s = t % kKvStages;
+          const int sb = t & 1;
+          if (!wait1(&sh.kv_full[s], (t / kKvStages) & 1) ||
+              !wait1(&sh.s_empty[sb], ((t >> 1) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t kb = kv_addr + s * 2 * kTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kHead / 16; ++kk)
+            umma(sh.tmem_base + sb * kTile, operand_desc(q_addr, kk), operand_desc(kb, kk), idesc,
+                 kk > 0 ? 1u : 0u);
+          umma_commit(&sh.s_full[sb]);
+          umma_commit(&sh.kv_empty[s]);
+          if (kt > 0 && !issue_pv(t - 1, kt == 1)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&sh.q_empty);  // every S of this item issued: Q may be replaced
+        if (!issue_pv(t - 1, kt_end == 0)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) report(c, sh, 2);
+      umma_commit(&sh.drain);
+      wait1(&sh.drain, 0);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------- softmax / epilogue
+    const int ew = warp & 3;                 // TMEM lanes 32*ew .. +31
+    const int row_in_tile = ew * 32 + lane;  // this thread's row
+    const uint32_t lane_off = static_cast<uint32_t>(ew * 32) << 16;
+    int t = 0;
+    bool ok = true;
+    for (int k = 0, item = cta_item(0); item < items && ok; item = cta_item(++k)) {
+      const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+      const int h = item % c.num_kv_heads;
+      const int r = qt * kTile + row_in_tile;
+      const int pos = c.row_pos[r];
+      const int kt_end = max(c.tile_max[qt], 0) / kTile;
+      float m_used = -INFINITY;  // log2-domain max the exponentials are taken against
+      float l = 0.0f;
+      for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+        const int sb = t & 1;
+        if (!wait_warp(&sh.s_full[sb], (t >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t v[4][32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld32(sh.tmem_base + sb * kTile + lane_off + q * 32, v[q]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.s_empty[sb]);
+        // the reference's roundings: bf16 logits, bf16 (logit * scale); keys > pos masked
+        const int valid = min(max(pos - kt * kTile + 1, 0), kTile);
+        float x[128];
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 128; ++j) {
+          const float w = round_t<T>(round_t<T>(__uint_as_float(v[j >> 5][j & 31])) * c.scale);
+          x[j] = j < valid ? w * kLog2e : -INFINITY;
+          mx[j & 7] = fmaxf(mx[j & 7], x[j]);
+        }
+        const float tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        const bool grow = tile_max > m_used + kRescaleLog2 || (m_used == -INFINITY && tile_max > -INFINITY);
+        // the P buffer is free and O settled once the previous tile's P V is done
+        if (kt > 0 && !wait_warp(&sh.pv_done, (t - 1) & 1)) { ok = false; break; }
+        if (__any_sync(0xffffffffu, grow)) {
+          const float m_new = grow ? tile_max : m_used;
+          const float corr = grow ? (m_used == -INFINITY ? 0.0f : ex2(m_used - m_new)) : 1.0f;
+          if (kt > 0) {  // O holds earlier tiles of this item: rescale its rows
+            tc_fence_after();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t o[32];
+              tmem_ld32(sh.tmem_base + kTmemO + lane_off + q * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * corr);
+              tmem_st32(sh.tmem_base + kTmemO + lane_off + q * 32, o);
+            }
+            tmem_wait_st();
+          }
+          l *= corr;
+          m_used = m_new;
+        }
+        // p = 2^(x - m_used) rounded to T into the SW128 P tile; the sum in fp32
+        // (a padding row keeps m_used = -inf: its p are exact zeros)
+        const float base_m = m_used == -INFINITY ? 0.0f : m_used;
+        float sm[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sm[i] = 0.0f;
+#pragma unroll
+        for (int c16 = 0; c16 < 16; ++c16) {  // 16-byte chunk of 8 keys
+          uint32_t packed[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = c16 * 8 + 2 * e;
+            const float p0 = ex2(x[j] - base_m);
+            const float p1 = ex2(x[j + 1] - base_m);
+            sm[(2 * e) & 7] += p0;
+            sm[(2 * e + 1) & 7] += p1;
+            packed[e] = pack2<T>(p0, p1);
+          }
+          const int half = c16 >> 3;
+          const int chunk = c16 & 7;
+          unsigned char* dst = p_buf + half * kHalfBytes + row_in_tile * 128 +
+                               ((chunk ^ (row_in_tile & 7)) * 16);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        }
+        l += ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+        fence_async_smem();  // generic-proxy P writes -> the MMA's async-proxy reads
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.p_full);
+      }
+      if (!ok) break;
+      // O of this item complete once the last P V is done
+      if (!wait_warp(&sh.pv_done, (t - 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      const int64_t qi = static_cast<int64_t>(r) / c.groups;
+      const int g = r - static_cast<int>(qi) * c.groups;
+      const bool store = qi < c.num_queries && pos >= 0;
+      const float inv = store && l > 0.0f ? 1.0f / l : 0.0f;
+      T* dst = reinterpret_cast<T*>(c.out + qi * c.out_token_stride) +
+               static_cast<int64_t>(h * c.groups + g) * kHead;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t o[32];
+        tmem_ld32(sh.tmem_base + kTmemO + lane_off + q * 32, o);
+        tmem_wait_ld();
+        if (store) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            const uint4 w = make_uint4(pack2<T>(__uint_as_float(o[j]) * inv, __uint_as_float(o[j + 1]) * inv),
+                                       pack2<T>(__uint_as_float(o[j + 2]) * inv, __uint_as_float(o[j + 3]) * inv),
+                                       pack2<T>(__uint_as_float(o[j + 4]) * inv, __uint_as_float(o[j + 5]) * inv),
+                                       pack2<T>(__uint_as_float(o[j + 6]) * inv, __uint_as_float(o[j + 7]) * inv));
+            *reinterpret_cast<uint4*>(dst + q * 32 + j) = w;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.o_empty);
+    }
+    if (!ok && lane == 0) report(c, sh, 3);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(sh.tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// Qd[h][r][:] = query[r / groups][h * groups + r % groups][:], zero rows up to
+// rows_pad; row positions; per-tile max position.
+__global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ query,
+                                                   int64_t query_token_stride,
+                                                   const int64_t* __restrict__ positions,
+                                                   int64_t num_queries, int num_kv_heads, int groups,
+                                                   int rows_pad, char* __restrict__ qd,
+                                                   int32_t* __restrict__ row_pos,
+                                                   int32_t* __restrict__ tile_max) {
+  constexpr int kRowBytes = kHead * 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int64_t total = static_cast<int64_t>(num_kv_heads) * rows_pad;
+  for (int64_t task = warp; task < total; task += nwarps) {
+    const int h = static_cast<int>(task / rows_pad);
+    const int r = static_cast<int>(task - (int64_t)h * rows_pad);
+    const int64_t qi = r / groups;
+    const int g = r - static_cast<int>(qi) * groups;
+    uint4* dst = reinterpret_cast<uint4*>(qd + task * kRowBytes);
+    if (lane < kRowBytes / 16) {
+      if (qi < num_queries)
+        dst[lane] = reinterpret_cast<const uint4*>(query + qi * query_token_stride +
+                                                   (int64_t)(h * groups + g) * kRowBytes)[lane];
+      else
+        dst[lane] = make_uint4(0, 0, 0, 0);
+    }
+    if (h == 0 && lane == 0) row_pos[r] = qi < num_queries ? static_cast<int32_t>(positions[qi]) : -1;
+  }
+  const int q_tiles = rows_pad / kTile;
+  for (int64_t qt = warp; qt < q_tiles; qt += nwarps) {
+    int mx = -1;
+    for (int r = lane; r < kTile; r += 32) {
+      const int64_t qi = (qt * kTile + r) / groups;
+      if (qi < num_queries) mx = max(mx, static_cast<int>(positions[qi]));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) tile_max[qt] = mx;
+  }
+}
+
+// Vt[h][d][k] = value[k][h][d] for k < num_keys, zero up to keys_pad: 64 keys x
+// 128 dims per block through shared memory (both sides coalesced).
+__global__ void __launch_bounds__(256) transpose_kernel(const char* __restrict__ value,
+                                                        int64_t value_token_stride,
+                                                        int64_t num_keys, int64_t keys_pad,
+                                                        int num_kv_heads, char* __restrict__ vt) {
+  __shared__ uint16_t tile[kHead][64 + 2];
+  const int64_t blocks_per_head = keys_pad / 64;
+  for (int64_t b = blockIdx.x; b < blocks_per_head * num_kv_heads; b += gridDim.x) {
+    const int h = static_cast<int>(b / blocks_per_head);
+    const int64_t k0 = (b - (int64_t)h * blocks_per_head) * 64;
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * kHead; i += blockDim.x) {
+      const int kk = i / kHead;
+      const int d = i - kk * kHead;
+      const int64_t key = k0 + kk;
+      tile[d][kk] = key < num_keys
+                        ? reinterpret_cast<const uint16_t*>(value + key * value_token_stride)[h * kHead + d]
+                        : uint16_t(0);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * kHead; i += blockDim.x) {
+      const int d = i / 64;
+      const int kk = i - d * 64;
+      reinterpret_cast<uint16_t*>(vt)[((int64_t)h * kHead + d) * keys_pad + k0 + kk] = tile[d][kk];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+struct Workspace {
+  size_t qd, vt, row_pos, tile_max, total;
+  int64_t rows_pad, keys_pad;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+Workspace layout(int64_t num_queries, int64_t num_keys, int64_t num_q_heads, int64_t num_kv_heads) {
+  const int64_t groups = num_q_heads / num_kv_heads;
+  Workspace w{};
+  w.rows_pad = (num_queries * groups + kTile - 1) / kTile * kTile;
+  w.keys_pad = (num_keys + kTile - 1) / kTile * kTile;
+  size_t off = 0;
+  w.qd = off;
+  off = align_up(off + (size_t)num_kv_heads * w.rows_pad * kHead * 2, 1024);
+  w.vt = off;
+  off = align_up(off + (size_t)num_kv_heads * kHead * w.keys_pad * 2, 1024);
+  w.row_pos = off;
+  off = align_up(off + (size_t)w.rows_pad * 4, 256);
+  w.tile_max = off;
+  off = align_up(off + (size_t)(w.rows_pad / kTile) * 4, 256);
+  w.total = off;
+  return w;
+}
+
+constexpr size_t kDynSmem = 1024 + (1 + 2 * kKvStages + 1) * kTileBytes;
+
+int check_shape(int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int dtype) {
+  CB_SUPPORTED(dtype == CB_DTYPE_BF16 || dtype == CB_DTYPE_FP16,
+               "blend attention needs bf16 or fp16 query / key / value");
+  CB_SUPPORTED(head_size == kHead, "blend attention supports head_size 128 (got %lld)",
+               (long long)head_size);
+  CB_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
+             "query heads must be a multiple of KV heads");
+  const int64_t groups = num_q_heads / num_kv_heads;
+  CB_SUPPORTED(groups <= kTile && kTile % groups == 0, "query groups must divide 128");
+  return CB_OK;
+}
+
+}  // namespace att
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" int cb_blend_attention_workspace_size(int64_t num_queries, int64_t num_keys,
+                                                 int64_t num_q_heads, int64_t num_kv_heads,
+                                                 int64_t head_size, int dtype, int64_t* bytes) {
+  clear_error();
+  CB_REQUIRE(bytes != nullptr, "null output");
+  int rc = att::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
+  if (rc != CB_OK) return rc;
+  CB_REQUIRE(num_queries >= 0 && num_keys >= 0, "negative size");
+  *bytes = static_cast<int64_t>(att::layout(num_queries, num_keys, num_q_heads, num_kv_heads).total);
+  return CB_OK;
+}
+
+extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride, const void* key,
+                                  int64_t key_token_stride, const void* value,
+                                  int64_t value_token_stride, int64_t num_keys, int64_t num_q_heads,
+                                  int64_t num_kv_heads, int64_t head_size, int dtype,
+                                  const int64_t* query_positions, int64_t num_queries, float scale,
+                                  void* out, int64_t out_token_stride, void* workspace,
+                                  int64_t workspace_bytes, int32_t* device_error, void* stream) {
+  CB_BIND(stream, out);
+  int rc = att::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
+  if (rc != CB_OK) return rc;
+  CB_REQUIRE(num_queries >= 0 && num_keys >= 0, "negative size");
+  if (num_queries == 0) return CB_OK;
+  CB_REQUIRE(num_keys > 0, "attention needs at least one key");
+  CB_REQUIRE(query && key && value && query_positions && out && workspace, "null pointer argument");
+  CB_REQUIRE(num_keys < (int64_t(1) << 31) && num_queries * (num_q_heads / num_kv_heads) < (int64_t(1) << 30),
+             "size out of range");
+  const uint64_t acc = reinterpret_cast<uint64_t>(query) | reinterpret_cast<uint64_t>(key) |
+                       reinterpret_cast<uint64_t>(value) | reinterpret_cast<uint64_t>(out) |
+                       (uint64_t)query_token_stride | (uint64_t)key_token_stride |
+                       (uint64_t)value_token_stride | (uint64_t)out_token_stride |
+                       reinterpret_cast<uint64_t>(workspace);
+  CB_SUPPORTED((acc & 15u) == 0, "blend attention needs 16-byte aligned rows and strides");
+  const att::Workspace w = att::layout(num_queries, num_keys, num_q_heads, num_kv_heads);
+  CB_REQUIRE(workspace_bytes >= static_cast<int64_t>(w.total), "workspace too small (%lld < %zu)",
+             (long long)workspace_bytes, w.total);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const int groups = static_cast<int>(num_q_heads / num_kv_heads);
+  {
+    const int64_t warps = num_kv_heads * w.rows_pad;
+    const int grid = static_cast<int>(std::min<int64_t>((warps + 7) / 8, kSmCount * 8));
+    att::prep_kernel<<<grid, 256, 0, s>>>(static_cast<const char*>(query), query_token_stride,
+                                           query_positions, num_queries, static_cast<int>(num_kv_heads),
+                                           groups, static_cast<int>(w.rows_pad), ws + w.qd,
+                                           reinterpret_cast<int32_t*>(ws + w.row_pos),
+                                           reinterpret_cast<int32_t*>(ws + w.tile_max));
+    rc = launch_status("cb_blend_attention (prep)");
+    if (rc != CB_OK) return rc;
+    const int64_t blocks = num_kv_heads * (w.keys_pad / 64);
+    const int tgrid = static_cast<int>(std::min<int64_t>(blocks, kSmCount * 8));
+    att::transpose_kernel<<<tgrid, 256, 0, s>>>(static_cast<const char*>(value), value_token_stride,
+                                                 num_keys, w.keys_pad, static_cast<int>(num_kv_heads),
+                                                 ws + w.vt);
+    rc = launch_status("cb_blend_attention (transpose)");
+    if (rc != CB_OK) return rc;
+  }
+  tc::EncodeTiled encode = nullptr;
+  rc = tc::get_encoder(&encode);
+  if (rc != CB_OK) return rc;
+  CUtensorMap q_map, k_map, vt_map;
+  rc = tc::encode_3d(encode, &q_map, dtype, ws + w.qd, head_size, w.rows_pad, num_kv_heads,
+                     head_size * 2, w.rows_pad * head_size * 2, tc::kTile, 1);
+  if (rc == CB_OK)
+    rc = tc::encode_3d(encode, &k_map, dtype, key, head_size, num_kv_heads, num_keys, head_size * 2,
+                       key_token_stride, 1, tc::kTile);
+  if (rc == CB_OK)
+    rc = tc::encode_3d(encode, &vt_map, dtype, ws + w.vt, w.keys_pad, head_size, num_kv_heads,
+                       w.keys_pad * 2, head_size * w.keys_pad * 2, tc::kTile, 1);
+  if (rc != CB_OK) return rc;
+  att::Params c{};
+  c.num_kv_heads = static_cast<int>(num_kv_heads);
+  c.groups = groups;
+  c.rows_pad = static_cast<int>(w.rows_pad);
+  c.q_tiles = static_cast<int>(w.rows_pad / tc::kTile);
+  c.num_queries = num_queries;
+  c.scale = scale;
+  c.row_pos = reinterpret_cast<const int32_t*>(ws + w.row_pos);
+  c.tile_max = reinterpret_cast<const int32_t*>(ws + w.tile_max);
+  c.out = static_cast<char*>(out);
+  c.out_token_stride = out_token_stride;
+  c.error = device_error;
+  const int grid = static_cast<int>(std::min<int64_t>(num_kv_heads * c.q_tiles, kSmCount));
+  auto kernel = dtype == CB_DTYPE_BF16 ? att::attention_kernel<__nv_bfloat16>
+                                       : att::attention_kernel<__half>;
+  rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), att::kDynSmem);
+  if (rc != CB_OK) return rc;
+  kernel<<<grid, att::kThreads, att::kDynSmem, s>>>(q_map, k_map, vt_map, c);
+  return launch_status("cb_blend_attention");
+}

@@ -1,0 +1,144 @@
+"""Blend attention on the tcgen05 tensor cores vs the reference's einsum path
+(Qwen3BlendExecutor._attention, cacheblend_vllm/ascend.py:798-846) evaluated in
+torch on the same device and dtype.
+
+Tolerance: the kernel rounds the unnormalized exp2 values to the element type
+and divides by the fp32 sum at the end, where the reference rounds the
+normalized probabilities; each output element therefore differs by at most a
+few ulps of the element type: |got - want| <= 2e-2 + 2e-2 * |want|, and the
+mean absolute difference stays below 2e-3.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from cacheblend_b200.attention import attention_workspace_bytes, blend_attention
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+RTOL = 2e-2
+MEAN_TOL = 2e-3
+
+
+def reference_attention(query, key, value, positions, scale):
+    """The reference formula, one KV head at a time (same roundings: the
+    einsum output in the element type, scaled in the element type, masked with
+    the type's minimum, softmax in fp32, probabilities cast back)."""
+    nq, hq, d = query.shape
+    nk, hkv, _ = key.shape
+    groups = hq // hkv
+    masked = positions[:, None] < torch.arange(nk, device=query.device)[None, :]
+    out = torch.empty_like(query)
+    for h in range(hkv):
+        q = query[:, h * groups:(h + 1) * groups]              # [nq, g, d]
+        weights = torch.einsum("qgd,kd->gqk", q, key[:, h]) * scale
+        weights = weights.masked_fill(masked[None], torch.finfo(weights.dtype).min)
+        probs = torch.softmax(weights.float(), dim=-1).to(query.dtype)
+        out[:, h * groups:(h + 1) * groups] = torch.einsum("gqk,kd->qgd", probs, value[:, h])
+    return out
+
+
+def _check(got, want, max_bad_fraction=0.0):
+    diff = (got.float() - want.float()).abs()
+    bound = ATOL + RTOL * want.float().abs()
+    bad = int((diff > bound).sum())
+    assert bad <= max_bad_fraction * diff.numel(), (
+        f"{bad} elements out of tolerance, max diff {float(diff.max()):.4g}")
+    assert float(diff.mean()) < MEAN_TOL
+
+
+def _inputs(cuda, nq, nk, hq, hkv, dtype, seed, pruned=True):
+    gen = torch.Generator(device=cuda).manual_seed(seed)
+    if pruned:
+        # computed rows: a sorted random subset of positions that always
+        # includes the last one (the suffix of a blend request)
+        pick = torch.randperm(nk - 1, generator=gen, device=cuda)[: nq - 1]
+        positions = torch.cat([pick.sort().values, torch.tensor([nk - 1], device=cuda)])
+    else:
+        positions = torch.arange(nk - nq, nk, device=cuda)
+    query = torch.randn(nq, hq, 128, generator=gen, device=cuda).to(dtype)
+    key = torch.randn(nk, hkv, 128, generator=gen, device=cuda).to(dtype)
+    value = torch.randn(nk, hkv, 128, generator=gen, device=cuda).to(dtype)
+    return query, key, value, positions
+
+
+@pytest.mark.parametrize(
+    "nq,nk,hq,hkv,dtype,pruned",
+    [
+        (300, 300, 32, 8, torch.bfloat16, False),   # prefill: every position computed
+        (160, 1000, 16, 2, torch.bfloat16, True),   # pruned rows, ragged key count
+        (77, 77, 8, 8, torch.float16, False),       # one query per head (groups 1), fp16
+        (250, 2100, 64, 4, torch.bfloat16, True),   # groups 16
+        (1, 129, 32, 8, torch.bfloat16, True),      # single query, keys one past a tile
+        (1229, 8192, 32, 8, torch.bfloat16, True),  # Qwen3-8B heads, 15% of 8k rows
+    ],
+)
+def test_attention_vs_reference(cuda, nq, nk, hq, hkv, dtype, pruned):
+    query, key, value, positions = _inputs(cuda, nq, nk, hq, hkv, dtype, nq * 7 + nk, pruned)
+    scale = 128 ** -0.5
+    error = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = blend_attention(query, key, value, positions, scale, device_error=error)
+    torch.cuda.synchronize()
+    assert int(error.item()) == 0
+    _check(got, reference_attention(query, key, value, positions, scale))
+
+
+def test_attention_peaked_logits(cuda):
+    """Large logits: row maxima grow across key tiles by more than the lazy
+    rescale threshold, so the output accumulator is rescaled in TMEM.  Here a
+    logit's element-type rounding is a large step (1/8 at 30), and the two
+    fp32 accumulation orders can round a logit near a midpoint differently;
+    when that logit dominates its row the output moves by more than the
+    tolerance, so up to 1e-3 of the elements may differ by more."""
+    query, key, value, positions = _inputs(cuda, 200, 1500, 16, 4, torch.bfloat16, 11)
+    # keys grow in magnitude with position so later tiles raise each row's max
+    key = (key.float() * torch.linspace(0.5, 3.0, key.shape[0], device=cuda)[:, None, None]).to(key.dtype)
+    scale = 0.5
+    error = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = blend_attention(query, key, value, positions, scale, device_error=error)
+    torch.cuda.synchronize()
+    assert int(error.item()) == 0
+    _check(got, reference_attention(query, key, value, positions, scale), max_bad_fraction=1e-3)
+
+
+def test_attention_strided_views(cuda):
+    """Query / key / value as column slices of one packed QKV projection (the
+    executor's layout), output into a wider buffer through a view."""
+    nq, nk, hq, hkv = 180, 640, 32, 8
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    width = (hq + 2 * hkv) * 128
+    qkv = torch.randn(nk, width, generator=gen, device=cuda).to(torch.bfloat16)
+    key = qkv[:, hq * 128:(hq + hkv) * 128].view(nk, hkv, 128)
+    value = qkv[:, (hq + hkv) * 128:].view(nk, hkv, 128)
+    positions = torch.randperm(nk, generator=gen, device=cuda)[:nq].sort().values
+    query = qkv[positions, : hq * 128].view(nq, hq, 128)
+    query = torch.empty(nq, width, dtype=torch.bfloat16, device=cuda)[:, : hq * 128].copy_(
+        query.reshape(nq, -1)).view(nq, hq, 128)
+    assert query.stride(0) == width
+    got = blend_attention(query, key, value, positions, 128 ** -0.5)
+    _check(got, reference_attention(query, key, value, positions, 128 ** -0.5))
+
+
+def test_attention_workspace_reuse(cuda):
+    """A caller-owned workspace sized for the largest shape serves smaller calls."""
+    query, key, value, positions = _inputs(cuda, 400, 3000, 32, 8, torch.bfloat16, 3)
+    need = attention_workspace_bytes(400, 3000, 32, 8, 128, torch.bfloat16)
+    workspace = torch.empty(need, dtype=torch.uint8, device=cuda)
+    for nq, nk in ((400, 3000), (90, 700)):
+        q = query[:nq]
+        pos = torch.clamp(positions[:nq], max=nk - 1)
+        got = blend_attention(q, key[:nk], value[:nk], pos, 0.1, workspace=workspace)
+        _check(got, reference_attention(q, key[:nk], value[:nk], pos, 0.1))
+
+
+def test_attention_rejects_unsupported(cuda):
+    q = torch.zeros(4, 8, 64, dtype=torch.bfloat16, device=cuda)
+    k = torch.zeros(4, 8, 64, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(NotImplementedError):
+        blend_attention(q, k, k, torch.arange(4, device=cuda), 1.0)
+    q = torch.zeros(4, 8, 128, dtype=torch.float32, device=cuda)
+    with pytest.raises(NotImplementedError):
+        blend_attention(q, q, q, torch.arange(4, device=cuda), 1.0)
