@@ -76,6 +76,11 @@ class Shape:
 SPARSE_Q_CONFIG = {"name": "qwen3-30b-a3b-98k-sparse_q", "layers": 48, "q_heads": 32, "kv_heads": 4,
                    "head_dim": 128, "tokens": 98304, "query_chunks": 16, "check_layer": 6}
 
+ATTENTION_CONFIG = {"name": "qwen3-8b-32k-blend_attention", "q_heads": 32, "kv_heads": 8, "head_dim": 128,
+                    "tokens": 32768, "ratio": 0.15}
+
+ATTENTION_KEYS = 0  # --attention-tokens: a smaller context for profiling captures
+
 STORE_CONFIG = {"name": "qwen3-8b-store-64x8k", "layers": 36, "kv_heads": 8, "head_dim": 128, "requests": 64,
                 "tokens": 8192, "chunk": 256, "block_size": 16, "local_cpu_gb": 16.0, "inflight": 8,
                 "workers": 1}
@@ -514,8 +519,9 @@ def measured_peaks() -> dict:
     path = REPO / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 def load_traffic() -> dict:
@@ -758,6 +764,153 @@ def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
         }), flush=True)
 
 
+def attention_inputs(world: int, rank: int, device):
+    """Config 6 inputs: the staging context of one layer (K / V rows = positions)
+    and the queries of the rows kept after the check layer (15% of the span,
+    the last prompt token among them), TP-sharded over heads."""
+    cfg = ATTENTION_CONFIG
+    ctx = (ATTENTION_KEYS or cfg["tokens"]) - 1
+    rng = np.random.default_rng(6)
+    count = int(round(cfg["ratio"] * ctx))
+    positions = np.sort(np.concatenate([rng.choice(ctx - 1, size=count - 1, replace=False), [ctx - 1]]))
+    hq, hkv = cfg["q_heads"] // world, cfg["kv_heads"] // world
+    gen = torch.Generator(device=device).manual_seed(60 + rank)
+    query = torch.randn(positions.size, hq, 128, generator=gen, device=device).to(torch.bfloat16)
+    key = torch.randn(ctx, hkv, 128, generator=gen, device=device).to(torch.bfloat16)
+    value = torch.randn(ctx, hkv, 128, generator=gen, device=device).to(torch.bfloat16)
+    return positions, query, key, value
+
+
+def attention_flops(positions: np.ndarray, q_heads: int) -> float:
+    """Causal QK^T plus PV over keys <= position: 4 * head_dim per (query head, key)."""
+    return 4.0 * 128 * q_heads * float((positions.astype(np.float64) + 1).sum())
+
+
+def attention_bench(args, world: int, rank: int, local: int) -> None:
+    """Config 6: the executor's attention of the kept rows over the staging
+    context (one layer), on the tensor cores."""
+    from cacheblend_b200.attention import attention_workspace_bytes, blend_attention
+
+    cfg = ATTENTION_CONFIG
+    device = torch.device("cuda", local)
+    positions, query, key, value = attention_inputs(world, rank, device)
+    pos = torch.from_numpy(positions).to(device)
+    nq, hq = query.shape[0], query.shape[1]
+    workspace = torch.empty(attention_workspace_bytes(nq, key.shape[0], hq, key.shape[1], 128, torch.bfloat16),
+                            dtype=torch.uint8, device=device)
+    error = torch.zeros(1, dtype=torch.int32, device=device)
+    scale = 128 ** -0.5
+    stream = torch.cuda.Stream(device)
+
+    def step():
+        return blend_attention(query, key, value, pos, scale, workspace=workspace, device_error=error,
+                               stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks, torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    flops = attention_flops(positions, hq)
+    # context: torch SDPA with the boolean causal-by-position mask (the generic path)
+    allowed = pos[:, None] >= torch.arange(key.shape[0], device=device)[None, :]
+    sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(
+        query.transpose(0, 1)[None], key.transpose(0, 1)[None], value.transpose(0, 1)[None],
+        attn_mask=allowed[None, None], scale=scale, enable_gqa=hq != key.shape[1])
+    sdpa()
+    torch.cuda.synchronize(device)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(3):
+        sdpa()
+    s1.record()
+    torch.cuda.synchronize(device)
+    sdpa_ms = s0.elapsed_time(s1) / 3
+    peaks = measured_peaks()
+    peak = peaks["bf16_tflops"]
+    achieved = flops / (ms / 1e3) / 1e12
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = attention_cpu_sample(positions, query, key, value, scale)
+        print(json.dumps({
+            "metric": "blend-attention query tokens/s (one layer, TP-sharded heads)",
+            "value": positions.size / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
+            "config": {"workload": cfg["name"] + (f"-{ATTENTION_KEYS}tok" if ATTENTION_KEYS else ""),
+                       "keys": int(key.shape[0]), "queries": int(positions.size),
+                       "q_heads_per_rank": hq, "kv_heads_per_rank": int(key.shape[1]),
+                       "l2": "inputs larger than L2 (K, V and Q: %d MiB)"
+                             % ((key.numel() * 2 + query.numel()) * 2 >> 20)},
+            "gpu_launches": 3 * args.steps, "launch": "eager (prep, value transpose, attention per step)",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": peaks["source"],
+                         "flops_note": "causal algorithmic: 4 x 128 x q_heads x sum(position + 1)"},
+            "context": {"torch_sdpa_masked_ms": sdpa_ms},
+            "device_error": int(error.item()), "clocks": clocks.summary(), "cpu_baseline": cpu,
+        }), flush=True)
+
+
+def attention_cpu_sample(positions, query, key, value, scale, budget_s: float = 15.0) -> dict:
+    """The oracle's restatement of the reference einsum path on the host, over
+    the last query rows until about ``budget_s`` of CPU work."""
+    import oracle
+
+    q = query.float().cpu().numpy()
+    k = key.float().cpu().numpy()
+    v = value.float().cpu().numpy()
+    done, t0 = 0, time.perf_counter()
+    step = 8
+    while time.perf_counter() - t0 < budget_s and done < positions.size:
+        rows = slice(positions.size - done - step, positions.size - done)
+        limit = int(positions[rows].max()) + 1
+        oracle.blend_attention(q[rows], k[:limit], v[:limit], positions[rows], scale, oracle.BF16)
+        done += step
+    elapsed = time.perf_counter() - t0
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max([int(info.get("num_threads", 1)) for info in threadpool_info()] + [1])
+    except ImportError:
+        cores = 1
+    return {"value": done / elapsed, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"the last {done} query rows, keys up to their positions (numpy oracle; "
+                      f"BLAS products on {cores} threads)"}
+
+
+def attention_reference(args) -> None:
+    """--impl reference for config 6: the reference's einsum attention restated
+    by the oracle, timed on the host; each step a bounded sample of rows."""
+    positions, query, key, value = attention_inputs(1, 0, torch.device("cpu"))
+    times = []
+    sample = None
+    for i in range(args.warmup + args.steps):
+        s = attention_cpu_sample(positions, query, key, value, 128 ** -0.5, budget_s=2.0)
+        if i >= args.warmup:
+            times.append(s["value"])
+            sample = s
+    value_ = float(np.median(times))
+    print(json.dumps({
+        "impl": "reference", "metric": "blend-attention query tokens/s (one layer, TP-sharded heads)",
+        "value": value_, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
+        "config": {"workload": ATTENTION_CONFIG["name"]},
+        "cpu_baseline": {**sample, "value": value_},
+        "e2e": {"value": value_, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def store_connector(cfg: dict, world: int, rank: int, device):
     """A producer-only ``CacheBlendConnectorV1`` worker built the way vLLM builds it."""
     from types import SimpleNamespace
@@ -935,7 +1088,7 @@ def main() -> None:
                         help="timed steps (default 200; 5 for the seconds-long Store step of config 5)")
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--config", type=int, choices=sorted(CONFIGS) + [3, 5], default=2)
+    parser.add_argument("--config", type=int, choices=sorted(CONFIGS) + [3, 5, 6], default=2)
     parser.add_argument("--e2e-steps", type=int, default=5)
     parser.add_argument("--sample-layers", type=int, default=2)
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -947,6 +1100,8 @@ def main() -> None:
                         help="time eager launches instead of CUDA-graph replays of the step")
     parser.add_argument("--layers", type=int, default=0,
                         help="override the layer count (small profiling captures only)")
+    parser.add_argument("--attention-tokens", type=int, default=0,
+                        help="config 6 context length override (small profiling captures only)")
     parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
                         help="host->device mode of the e2e loader (CACHEBLEND_B200_LOAD)")
     args = parser.parse_args()
@@ -955,6 +1110,18 @@ def main() -> None:
     if args.config == 3:
         world, rank, local, group = dist_setup(args)
         sparse_q_bench(args, world, rank, local)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if args.config == 6:
+        global ATTENTION_KEYS
+        ATTENTION_KEYS = args.attention_tokens
+        world, rank, local, group = dist_setup(args)
+        if args.impl == "reference":
+            if rank == 0:
+                attention_reference(args)
+        else:
+            attention_bench(args, world, rank, local)
         if world > 1:
             torch.distributed.destroy_process_group()
         return

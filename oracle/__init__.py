@@ -346,3 +346,50 @@ def sparse_q_scores(query: np.ndarray, key: np.ndarray, absolute: np.ndarray,
     if full:
         return scores, forced, stats
     return scores[np.asarray(absolute, dtype=np.int64)], forced, stats
+
+
+def _round_to(values: np.ndarray, dtype: int) -> np.ndarray:
+    """fp32 values rounded to the element type (nearest even), returned as fp32."""
+    if dtype == BF16:
+        return round_bf16(values)
+    if dtype == FP16:
+        return values.astype(np.float16).astype(np.float32)
+    return values.astype(np.float32)
+
+
+def blend_attention(query: np.ndarray, key: np.ndarray, value: np.ndarray, positions: np.ndarray,
+                    scale: float, dtype: int = BF16) -> np.ndarray:
+    """Attention of the computed queries over the staging context
+    (Qwen3BlendExecutor._attention, ascend.py:798-846, einsum path), numpy fp32.
+
+    query [Nq, Hq, D], key / value [Nk, Hkv, D] as fp32 arrays holding values
+    of the element type; query head h uses KV head h // (Hq // Hkv).  Each
+    step rounds where the reference's tensors do: the Q.K^T product to the
+    element type, the scaled logits to the element type, softmax in fp32 over
+    keys k <= position (masked logits contribute exp(finfo.min - max) == 0),
+    probabilities to the element type, the P.V product to the element type.
+    Returns fp32 values of the element type.
+    """
+    nq, hq, _ = query.shape
+    nk, hkv, _ = key.shape
+    if hq % hkv:
+        raise ValueError("query heads must be divisible by KV heads")
+    groups = hq // hkv
+    pos = np.asarray(positions, dtype=np.int64)
+    scale32 = np.float32(scale)
+    out = np.zeros(query.shape, dtype=np.float32)
+    for start in range(0, nq, 128):
+        rows = slice(start, min(start + 128, nq))
+        limit = int(pos[rows].max()) + 1
+        masked = pos[rows, None] < np.arange(limit)[None, :]
+        for h in range(hkv):
+            k_h = key[:limit, h, :].astype(np.float32)
+            v_h = value[:limit, h, :].astype(np.float32)
+            for g in range(groups):
+                q = query[rows, h * groups + g, :].astype(np.float32)
+                logits = _round_to(_round_to(q @ k_h.T, dtype) * scale32, dtype)
+                logits[masked] = -np.inf
+                e = np.exp(logits - logits.max(axis=1, keepdims=True), dtype=np.float32)
+                probs = _round_to(e / e.sum(axis=1, keepdims=True, dtype=np.float32), dtype)
+                out[rows, h * groups + g, :] = probs @ v_h
+    return _round_to(out, dtype)

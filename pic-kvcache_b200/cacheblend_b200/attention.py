@@ -16,6 +16,17 @@ import torch
 from . import _native
 
 
+def attention_supported(query: torch.Tensor, key: torch.Tensor) -> bool:
+    """Shapes cb_blend_attention takes: head size 128, bf16 / fp16, query heads
+    a multiple of KV heads with the group count dividing 128."""
+    if query.ndim != 3 or key.ndim != 3 or query.shape[2] != 128 or key.shape[2] != 128:
+        return False
+    if query.dtype not in (torch.bfloat16, torch.float16) or key.dtype != query.dtype:
+        return False
+    hq, hkv = query.shape[1], key.shape[1]
+    return hkv > 0 and hq % hkv == 0 and 128 % (hq // hkv) == 0
+
+
 def attention_workspace_bytes(num_queries: int, num_keys: int, num_q_heads: int, num_kv_heads: int,
                               head_size: int, dtype: torch.dtype) -> int:
     out = ctypes.c_int64(0)

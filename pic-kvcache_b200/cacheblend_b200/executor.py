@@ -17,6 +17,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from .attention import attention_supported, attention_workspace_bytes, blend_attention
 from .config import CacheBlendConfig
 from .loader import PagedBlendLoader
 from .rope import validate_rope_support
@@ -213,7 +214,18 @@ class Qwen3BlendExecutor:
         return attn_layer.rotary_emb(positions, q, k)
 
     def _attention(self, query, key, value, q_positions, scale, state: BlendExecutionState):
-        """Causal attention of the computed queries over the whole staging context."""
+        """Causal attention of the computed queries over the whole staging context
+        (ascend.py:798-846).  Head size 128 in bf16 / fp16 with query groups
+        dividing 128 (every Qwen3 configuration) runs the tcgen05 kernel; other
+        shapes use torch's SDPA with the same mask."""
+        if query.device.type == "cuda" and attention_supported(query, key):
+            need = attention_workspace_bytes(query.shape[0], key.shape[0], query.shape[1],
+                                             key.shape[1], query.shape[2], query.dtype)
+            workspace = getattr(self, "_attention_workspace", None)
+            if workspace is None or workspace.numel() < need or workspace.device != query.device:
+                workspace = torch.empty(need, dtype=torch.uint8, device=query.device)
+                self._attention_workspace = workspace
+            return blend_attention(query, key, value, q_positions, scale, workspace=workspace)
         k_positions = torch.arange(key.shape[0], device=query.device)
         cache = self.config.cache_attention_mask and state.important_indices is not None
         allowed = state.attention_mask if cache else None

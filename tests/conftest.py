@@ -27,6 +27,18 @@ def golden():
 
 
 @pytest.fixture(scope="session")
+def attention_golden():
+    return np.load(GOLDEN / "attention.npz")
+
+
+def element_values(bits: np.ndarray, dtype_code: int) -> np.ndarray:
+    """uint16 bit patterns of bf16 (code 0) or fp16 (code 1) as fp32 values."""
+    if dtype_code == 0:
+        return (bits.astype(np.uint32) << np.uint32(16)).view(np.float32)
+    return bits.view(np.float16).astype(np.float32)
+
+
+@pytest.fixture(scope="session")
 def store_sequence():
     return json.loads((GOLDEN / "store_sequence.json").read_text())
 

@@ -17,6 +17,7 @@ Covered reference functions (file:line in the reference):
   ascend.Qwen3BlendExecutor._sparse_q_scores          ascend.py:638-711
   storage.LocalPinnedCPUStore (op sequence)           storage.py:56-294
   hashing.content_hash / rolling_hash_values          hashing.py:18-53  (hashes.npz)
+  ascend.Qwen3BlendExecutor._attention (einsum path)  ascend.py:798-846 (attention.npz)
 """
 
 from __future__ import annotations
@@ -34,6 +35,7 @@ import torch
 OUT = Path(__file__).resolve().parent / "golden.npz"
 STORE_OUT = Path(__file__).resolve().parent / "store_sequence.json"
 HASH_OUT = Path(__file__).resolve().parent / "hashes.npz"
+ATTENTION_OUT = Path(__file__).resolve().parent / "attention.npz"
 
 
 def make_hash_golden() -> None:
@@ -49,6 +51,46 @@ def make_hash_golden() -> None:
                       dtype=np.uint64)
     small = np.array([content_hash([7]), content_hash([-1, 0, 1]), content_hash([])], dtype=np.uint64)
     np.savez_compressed(HASH_OUT, tokens=tokens, windows=windows, chunks=chunks, small=small)
+
+
+def make_attention_golden() -> None:
+    """The reference's attention of computed queries over the staging context
+    (ascend.py:798-846), CPU einsum path, head size 128: pruned and prefill
+    positions, query groups 4 / 1 / 8, bf16 and fp16."""
+    from types import SimpleNamespace
+
+    from cacheblend_vllm.ascend import Qwen3BlendExecutor
+    from cacheblend_vllm.config import CacheBlendConfig
+
+    gen = torch.Generator().manual_seed(41)
+    gold = {}
+    for case, (nq, nk, hq, hkv, dtype, pruned) in enumerate(
+        [(64, 300, 8, 2, torch.bfloat16, True), (130, 130, 4, 4, torch.bfloat16, False),
+         (33, 200, 8, 1, torch.float16, True)]
+    ):
+        executor = object.__new__(Qwen3BlendExecutor)
+        executor.config = CacheBlendConfig.from_extra_config({"strict_version_check": False})
+        if pruned:
+            pick = torch.randperm(nk - 1, generator=gen)[: nq - 1].sort().values
+            positions = torch.cat([pick, torch.tensor([nk - 1])])
+        else:
+            positions = torch.arange(nk - nq, nk)
+        query = torch.randn(nq, hq, 128, generator=gen).to(dtype)
+        key = torch.randn(nk, hkv, 128, generator=gen).to(dtype)
+        value = torch.randn(nk, hkv, 128, generator=gen).to(dtype)
+        scale = 1.0 / math.sqrt(128)
+        state = SimpleNamespace(important_indices=None, attention_mask=None)
+        out = executor._attention(query, key, value, positions, scale, state)
+        as_bits = bits if dtype == torch.bfloat16 else (lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16).copy())
+        tag = f"att_{case}"
+        gold[f"{tag}_query"] = as_bits(query)
+        gold[f"{tag}_key"] = as_bits(key)
+        gold[f"{tag}_value"] = as_bits(value)
+        gold[f"{tag}_positions"] = positions.numpy()
+        gold[f"{tag}_meta"] = np.array([0 if dtype == torch.bfloat16 else 1], dtype=np.int64)
+        gold[f"{tag}_scale"] = np.array([scale])
+        gold[f"{tag}_out"] = as_bits(out)
+    np.savez_compressed(ATTENTION_OUT, **gold)
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -287,6 +329,7 @@ def main() -> None:
 
     np.savez_compressed(OUT, **gold)
     make_hash_golden()
+    make_attention_golden()
 
     # ---- 7. store op sequence: every call, its result, bytes and LRU order
     rng = np.random.default_rng(7)

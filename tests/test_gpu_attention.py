@@ -11,9 +11,11 @@ mean absolute difference stays below 2e-3.
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
+import oracle
 from cacheblend_b200.attention import attention_workspace_bytes, blend_attention
 
 pytestmark = pytest.mark.gpu
@@ -63,6 +65,35 @@ def _inputs(cuda, nq, nk, hq, hkv, dtype, seed, pruned=True):
     key = torch.randn(nk, hkv, 128, generator=gen, device=cuda).to(dtype)
     value = torch.randn(nk, hkv, 128, generator=gen, device=cuda).to(dtype)
     return query, key, value, positions
+
+
+def _to_device(bits, code, device):
+    dtype = torch.bfloat16 if code == 0 else torch.float16
+    return torch.from_numpy(bits.view(np.int16)).view(dtype).to(device)
+
+
+@pytest.mark.parametrize("case", range(3))
+def test_attention_golden(attention_golden, cuda, case):
+    """Against the reference's own outputs (tests/golden/attention.npz)."""
+    tag = f"att_{case}"
+    code = int(attention_golden[f"{tag}_meta"][0])
+    q, k, v = (_to_device(attention_golden[f"{tag}_{n}"], code, cuda) for n in ("query", "key", "value"))
+    positions = torch.from_numpy(attention_golden[f"{tag}_positions"]).to(cuda)
+    error = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = blend_attention(q, k, v, positions, float(attention_golden[f"{tag}_scale"][0]), device_error=error)
+    torch.cuda.synchronize()
+    assert int(error.item()) == 0
+    _check(got, _to_device(attention_golden[f"{tag}_out"], code, cuda))
+
+
+def test_attention_vs_oracle(cuda):
+    """Against the CPU oracle on a seeded case with ragged tiles."""
+    query, key, value, positions = _inputs(cuda, 150, 420, 8, 2, torch.bfloat16, 17)
+    got = blend_attention(query, key, value, positions, 0.09)
+    as_np = lambda t: t.float().cpu().numpy()
+    want = oracle.blend_attention(as_np(query), as_np(key), as_np(value), positions.cpu().numpy(), 0.09,
+                                  oracle.BF16)
+    _check(got, torch.from_numpy(want).to(cuda))
 
 
 @pytest.mark.parametrize(

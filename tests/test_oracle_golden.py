@@ -172,3 +172,21 @@ def test_sparse_q_head128_matches_reference(golden, case):
     assert np.array_equal(forced, golden[f"{tag}_forced"])
     assert stats["sparse_query_tokens"] == golden[f"{tag}_stats"][0]
     assert np.array_equal(oracle.select(scores, golden[f"{tag}_gaps"], 0.15, forced), golden[f"{tag}_selected"])
+
+
+@pytest.mark.parametrize("case", range(3))
+def test_attention_matches_reference(attention_golden, case):
+    """Oracle attention vs the reference's einsum path (ascend.py:798-846):
+    bit-equal except where the fp32 accumulation order flips one rounding of a
+    logit or a probability (under 0.5% of the elements, each within 2e-3: one
+    probability ulp times a value)."""
+    from conftest import element_values
+
+    tag = f"att_{case}"
+    code = int(attention_golden[f"{tag}_meta"][0])
+    q, k, v = (element_values(attention_golden[f"{tag}_{n}"], code) for n in ("query", "key", "value"))
+    got = oracle.blend_attention(q, k, v, attention_golden[f"{tag}_positions"],
+                                 float(attention_golden[f"{tag}_scale"][0]), code)
+    want = element_values(attention_golden[f"{tag}_out"], code)
+    assert (got != want).mean() < 5e-3
+    assert float(np.abs(got - want).max()) <= 2e-3
