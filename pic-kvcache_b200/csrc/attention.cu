@@ -116,6 +116,37 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return r;
 }
 
+// Pairs of fp32 values rounded to T and widened back, on the FMA pipe instead
+// of the conversion unit (which shares its issue rate with exp2).
+// bf16: Veltkamp splitting at 16 bits, c = y (2^16 + 1), hi = c - (c - y),
+// leaves the upper 8 significant bits of y rounded to nearest even: equal to
+// the conversion for every fp32 value with 2^-126 <= |y| < 2^110 (checked
+// exhaustively); below that only subnormals differ, by less than 2^-126.
+// fp16 keeps the conversion instructions (its narrower exponent range makes
+// the rounding point depend on the magnitude).
+template <typename T>
+struct RoundPair;
+template <>
+struct RoundPair<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 apply(float2 y) {
+    const float2 c = __fmul2_rn(y, make_float2(65537.0f, 65537.0f));
+    const float2 d = __ffma2_rn(y, make_float2(-1.0f, -1.0f), c);
+    return __ffma2_rn(d, make_float2(-1.0f, -1.0f), c);
+  }
+};
+template <>
+struct RoundPair<__half> {
+  static __device__ __forceinline__ float2 apply(float2 y) {
+    return make_float2(round_t<__half>(y.x), round_t<__half>(y.y));
+  }
+};
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap q_map,
@@ -282,20 +313,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.s_empty[sb]);
-        // the reference's roundings: bf16 logits, bf16 (logit * scale); keys > pos masked
+        // the reference's roundings: T logits, T (logit * scale); keys > pos masked
         const int valid = min(max(pos - kt * kTile + 1, 0), kTile);
-        float x[128];
-        float mx[8];
+        float2 w[64];
+        const float2 sc2 = make_float2(c.scale, c.scale);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          const float w = round_t<T>(round_t<T>(__uint_as_float(v[j >> 5][j & 31])) * c.scale);
-          x[j] = j < valid ? w * kLog2e : -INFINITY;
-          mx[j & 7] = fmaxf(mx[j & 7], x[j]);
+        for (int j = 0; j < 64; ++j) {
+          const float2 sv = make_float2(__uint_as_float(v[j >> 4][(2 * j) & 31]),
+                                        __uint_as_float(v[j >> 4][(2 * j + 1) & 31]));
+          w[j] = RoundPair<T>::apply(__fmul2_rn(RoundPair<T>::apply(sv), sc2));
         }
-        const float tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        if (valid < kTile) {  // this row's position ends inside the tile
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            if (2 * j >= valid) w[j].x = -INFINITY;
+            if (2 * j + 1 >= valid) w[j].y = -INFINITY;
+          }
+        }
+        float mx[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) mx[j & 3] = max3(mx[j & 3], w[j].x, w[j].y);
+        // log2-domain tile max (rounding is monotonic: max(w) * log2e = max(w * log2e))
+        const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * kLog2e;
         const bool grow = tile_max > m_used + kRescaleLog2 || (m_used == -INFINITY && tile_max > -INFINITY);
         // the P buffer is free and O settled once the previous tile's P V is done
         if (kt > 0 && !wait_warp(&sh.pv_done, (t - 1) & 1)) { ok = false; break; }
@@ -318,23 +359,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= corr;
           m_used = m_new;
         }
-        // p = 2^(x - m_used) rounded to T into the SW128 P tile; the sum in fp32
+        // p = 2^(w log2e - m_used) rounded to T into the SW128 P tile; the sum in fp32
         // (a padding row keeps m_used = -inf: its p are exact zeros)
         const float base_m = m_used == -INFINITY ? 0.0f : m_used;
-        float sm[8];
+        const float2 l2e = make_float2(kLog2e, kLog2e);
+        const float2 nm = make_float2(-base_m, -base_m);
+        float2 sm[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sm[i] = 0.0f;
+        for (int i = 0; i < 4; ++i) sm[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int c16 = 0; c16 < 16; ++c16) {  // 16-byte chunk of 8 keys
           uint32_t packed[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = c16 * 8 + 2 * e;
-            const float p0 = ex2(x[j] - base_m);
-            const float p1 = ex2(x[j + 1] - base_m);
-            sm[(2 * e) & 7] += p0;
-            sm[(2 * e + 1) & 7] += p1;
-            packed[e] = pack2<T>(p0, p1);
+            const float2 x = __ffma2_rn(w[c16 * 4 + e], l2e, nm);
+            const float2 p = make_float2(ex2(x.x), ex2(x.y));
+            sm[e] = __fadd2_rn(sm[e], p);
+            packed[e] = pack2<T>(p.x, p.y);
           }
           const int half = c16 >> 3;
           const int chunk = c16 & 7;
@@ -342,7 +383,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                ((chunk ^ (row_in_tile & 7)) * 16);
           *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
-        l += ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
+        const float2 s01 = __fadd2_rn(sm[0], sm[1]);
+        const float2 s23 = __fadd2_rn(sm[2], sm[3]);
+        const float2 st = __fadd2_rn(s01, s23);
+        l += st.x + st.y;
         fence_async_smem();  // generic-proxy P writes -> the MMA's async-proxy reads
         tc_fence_before();
         __syncwarp();
