@@ -17,19 +17,25 @@
 // 128-row tiles (dense copy Qd[h][r][:] made by prep_kernel), so every K / V
 // tile is shared by all groups of the head.  V is transposed per head (Vt[h][d][k],
 // transpose_kernel) so that both products use K-major SWIZZLE_128B operands:
-//   S = Q K^T   A = Q tile [rows][dims],  B = K tile [keys][dims]   -> TMEM (two buffers)
-//   O += P V    A = P tile [rows][keys],  B = Vt tile [dims][keys]  -> TMEM (one accumulator)
-// Per CTA (persistent, items (head, query tile) dealt serpentine, latest
-// queries first): warp 0 issues the TMA loads (Q per item; K and Vt per key
-// tile, two stages), warp 1 lane 0 issues tcgen05.mma (S of tile t, then P V of
-// tile t-1, so the tensor core computes ahead of the softmax), warp 2 owns the
-// TMEM allocation, warps 4-7 (one row per thread) read S with tcgen05.ld, apply
-// the reference's roundings and the causal mask, keep an online max / sum in
-// the log2 domain, write P (rounded to T) into shared memory in the SW128
-// layout the MMA reads, and at the end of an item read O, divide by the sum and
-// store the output rows.  O is rescaled (tcgen05.ld / st) only when a row's max
-// grows by more than 2^8: until then the stale max keeps every exp2 <= 256, and
-// the final division uses the same max, so the result is unchanged.
+//   S = Q K^T   A = Q tile [rows][dims],  B = K tile [keys][dims]   -> TMEM
+//   O += P V    A = P tile [rows][keys],  B = Vt tile [dims][keys]  -> TMEM
+// An item is (KV head, pair of query tiles = 256 rows); CTAs are persistent and
+// take items dealt serpentine, latest queries first.  Per CTA, 12 warps:
+//   warp 0   Q loads per item, K tiles through a two-stage ring (TMA)
+//   warp 3   Vt tiles through one slot, loaded once the previous P V has read it
+//   warp 1   tcgen05.mma issue: S_A, S_B of key tile t, then P V of tile t-1 for
+//            both query tiles, so the tensor core computes ahead of the softmax
+//   warp 2   TMEM owner (S_A, S_B, O_A, O_B: 512 columns)
+//   warps 4-7 / 8-11  one softmax warpgroup per query tile, a row per thread:
+//            read S with tcgen05.ld, apply the reference's roundings and the
+//            causal mask, keep an online max / sum in the log2 domain, write P
+//            (rounded to T) into shared memory in the SW128 layout the MMA
+//            reads, and at the end of an item divide O by the sum and store it.
+// While one warpgroup runs its softmax the tensor core works on the other
+// tile's products, and each K / Vt tile serves 256 rows.  O is rescaled
+// (tcgen05.ld / st) only when a row's max grows by more than 2^8: until then
+// the stale max keeps every exp2 <= 256, and the final division uses the same
+// max, so the result is unchanged.
 // Every mbarrier wait is bounded (2 s): a wait that runs out records a code in
 // *device_error, the CTA drains its MMAs and loads, frees TMEM and returns.
 #include <algorithm>
@@ -43,18 +49,27 @@ namespace att {
 using namespace ::cb::tc;
 
 constexpr int kHead = 128;
-constexpr int kKvStages = 2;
-constexpr int kThreads = 256;      // warps 0-3 roles above, 4-7 softmax / epilogue
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
+constexpr int kPair = 2;                    // query tiles per item, one softmax warpgroup each
+constexpr int kPairRows = kPair * kTile;    // 256 rows per item
+constexpr int kKStages = 2;                 // K tiles in flight (V: one, see the producer)
+constexpr int kThreads = 384;  // warp 0 Q/K loads, 1 MMA, 2 TMEM owner, 3 V loads; 4-7 / 8-11 softmax
+constexpr uint32_t kTmemCols = 512;  // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
 constexpr uint32_t kTmemO = 256;
+// Register split: 128 control threads x 40 + 256 softmax threads x 232 =
+// 64512 = 384 threads x 168, the launch's allocation (__launch_bounds__(384, 1)).
+// MMA issue is a few adds per product (split descriptors), so the control roles fit in 40.
+constexpr int kRegsControl = 40;
+constexpr int kRegsSoftmax = 232;
+static_assert(4 * 32 * kRegsControl + 8 * 32 * kRegsSoftmax <= kThreads * 168, "register split");
 constexpr float kRescaleLog2 = 8.0f;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Shared {
   uint64_t q_full, q_empty;
-  uint64_t kv_full[kKvStages], kv_empty[kKvStages];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, pv_done, o_empty;
+  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t v_full, v_empty;
+  uint64_t s_full[kPair], s_empty[kPair];
+  uint64_t p_full[kPair], pv_done[kPair], o_empty[kPair];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -63,12 +78,12 @@ struct Shared {
 struct Params {
   int num_kv_heads;
   int groups;
-  int rows_pad;
-  int q_tiles;
+  int rows_pad;   // multiple of kPairRows
+  int q_pairs;    // rows_pad / kPairRows
   int64_t num_queries;
   float scale;
   const int32_t* row_pos;   // [rows_pad]: position of each row, -1 for padding
-  const int32_t* tile_max;  // [q_tiles]
+  const int32_t* pair_max;  // [q_pairs]: largest position among a pair's rows
   char* out;
   int64_t out_token_stride;  // bytes
   int32_t* error;
@@ -158,25 +173,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(dyn) + 1023) & ~static_cast<uintptr_t>(1023));
-  unsigned char* q_buf = base;                                // Q tile
-  unsigned char* kv_buf = base + kTileBytes;                  // stages x (K tile, Vt tile)
-  unsigned char* p_buf = base + (1 + 2 * kKvStages) * kTileBytes;  // P tile
-  const int items = c.num_kv_heads * c.q_tiles;
+  unsigned char* q_buf = base;                                  // kPair Q tiles
+  unsigned char* k_buf = base + kPair * kTileBytes;             // kKStages K tiles
+  unsigned char* v_buf = k_buf + kKStages * kTileBytes;         // one Vt tile
+  unsigned char* p_buf = v_buf + kTileBytes;                    // kPair P tiles
+  const int items = c.num_kv_heads * c.q_pairs;
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.q_full, 1);
     mbar_init(&sh.q_empty, 1);
-    for (int s = 0; s < kKvStages; ++s) {
-      mbar_init(&sh.kv_full[s], 1);
-      mbar_init(&sh.kv_empty[s], 2);  // after S (reads K) and after P V (reads Vt)
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&sh.k_full[s], 1);
+      mbar_init(&sh.k_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sh.s_full[i], 1);
-      mbar_init(&sh.s_empty[i], 4);
+    mbar_init(&sh.v_full, 1);
+    mbar_init(&sh.v_empty, 1);
+    for (int x = 0; x < kPair; ++x) {
+      mbar_init(&sh.s_full[x], 1);
+      mbar_init(&sh.s_empty[x], 4);
+      mbar_init(&sh.p_full[x], 4);
+      mbar_init(&sh.pv_done[x], 1);
+      mbar_init(&sh.o_empty[x], 4);
     }
-    mbar_init(&sh.p_full, 4);
-    mbar_init(&sh.pv_done, 1);
-    mbar_init(&sh.o_empty, 4);
     mbar_init(&sh.drain, 1);
     sh.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -192,85 +210,109 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
 
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
   if (warp == 0) {
-    // ---------------------------------------------------------- TMA producer
+    // ------------------------------------------------------ Q and K loads
     if (lane == 0) {
       int t = 0, it = 0;
-      int kv_armed[kKvStages];
-      for (int s = 0; s < kKvStages; ++s) kv_armed[s] = -1;
+      uint32_t k_armed = 0, k_parity = 0;  // per stage: a load is in flight / its phase parity
       int q_armed = -1;
-      for (int k = 0, item = cta_item(0); item < items && !aborted(sh); item = cta_item(++k), ++it) {
-        const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+      bool ok = true;
+      for (int k = 0, item = cta_item(0); item < items && ok && !aborted(sh);
+           item = cta_item(++k), ++it) {
+        const int qp = c.q_pairs - 1 - item / c.num_kv_heads;
         const int h = item % c.num_kv_heads;
-        if (!wait1(&sh.q_empty, (it & 1) ^ 1)) { report(c, sh, 1); break; }
-        mbar_expect_tx(&sh.q_full, kTileBytes);
-        tma_load_3d(q_buf, &q_map, &sh.q_full, 0, qt * kTile, h);
-        tma_load_3d(q_buf + kHalfBytes, &q_map, &sh.q_full, 64, qt * kTile, h);
-        q_armed = it & 1;
-        const int kt_end = max(c.tile_max[qt], 0) / kTile;  // the last tile holds a real row
-        bool ok = true;
-        for (int kt = 0; kt <= kt_end; ++kt, ++t) {
-          const int s = t % kKvStages;
-          if (!wait1(&sh.kv_empty[s], ((t / kKvStages) & 1) ^ 1)) { ok = false; break; }
-          mbar_expect_tx(&sh.kv_full[s], 2 * kTileBytes);
-          unsigned char* kb = kv_buf + s * 2 * kTileBytes;
-          tma_load_3d(kb, &k_map, &sh.kv_full[s], 0, h, kt * kTile);
-          tma_load_3d(kb + kHalfBytes, &k_map, &sh.kv_full[s], 64, h, kt * kTile);
-          tma_load_3d(kb + kTileBytes, &vt_map, &sh.kv_full[s], kt * kTile, 0, h);
-          tma_load_3d(kb + kTileBytes + kHalfBytes, &vt_map, &sh.kv_full[s], kt * kTile + 64, 0, h);
-          kv_armed[s] = (t / kKvStages) & 1;
+        if (!wait1(&sh.q_empty, (it & 1) ^ 1)) { ok = false; break; }
+        mbar_expect_tx(&sh.q_full, kPair * kTileBytes);
+        for (int x = 0; x < kPair; ++x) {
+          unsigned char* qb = q_buf + x * kTileBytes;
+          tma_load_3d(qb, &q_map, &sh.q_full, 0, qp * kPairRows + x * kTile, h);
+          tma_load_3d(qb + kHalfBytes, &q_map, &sh.q_full, 64, qp * kPairRows + x * kTile, h);
         }
-        if (!ok) { report(c, sh, 1); break; }
+        q_armed = it & 1;
+        const int kt_end = max(c.pair_max[qp], 0) / kTile;
+        for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+          const int s = t % kKStages;
+          if (!wait1(&sh.k_empty[s], ((t / kKStages) & 1) ^ 1)) { ok = false; break; }
+          mbar_expect_tx(&sh.k_full[s], kTileBytes);
+          unsigned char* kb = k_buf + s * kTileBytes;
+          tma_load_3d(kb, &k_map, &sh.k_full[s], 0, h, kt * kTile);
+          tma_load_3d(kb + kHalfBytes, &k_map, &sh.k_full[s], 64, h, kt * kTile);
+          k_armed |= 1u << s;
+          k_parity = (k_parity & ~(1u << s)) | (static_cast<uint32_t>((t / kKStages) & 1) << s);
+        }
       }
+      if (!ok) report(c, sh, 1);
       // every armed load has landed before the CTA may exit
-      for (int s = 0; s < kKvStages; ++s)
-        if (kv_armed[s] >= 0) wait1(&sh.kv_full[s], kv_armed[s]);
+      for (int s = 0; s < kKStages; ++s)
+        if ((k_armed >> s) & 1u) wait1(&sh.k_full[s], (k_parity >> s) & 1u);
       if (q_armed >= 0) wait1(&sh.q_full, q_armed);
     }
+  } else if (warp == 3) {
+    // ------------------------------------------------------ V loads
+    // Vt(t) may land only after P V of tile t-1 has read the previous one;
+    // it is needed after S(t+1), so its latency hides behind those products.
+    if (lane == 0) {
+      int t = 0;
+      int v_armed = -1;
+      bool ok = true;
+      for (int k = 0, item = cta_item(0); item < items && ok && !aborted(sh); item = cta_item(++k)) {
+        const int qp = c.q_pairs - 1 - item / c.num_kv_heads;
+        const int h = item % c.num_kv_heads;
+        const int kt_end = max(c.pair_max[qp], 0) / kTile;
+        for (int kt = 0; kt <= kt_end; ++kt, ++t) {
+          if (!wait1(&sh.v_empty, (t & 1) ^ 1)) { ok = false; break; }
+          mbar_expect_tx(&sh.v_full, kTileBytes);
+          tma_load_3d(v_buf, &vt_map, &sh.v_full, kt * kTile, 0, h);
+          tma_load_3d(v_buf + kHalfBytes, &vt_map, &sh.v_full, kt * kTile + 64, 0, h);
+          v_armed = t & 1;
+        }
+      }
+      if (!ok) report(c, sh, 1);
+      if (v_armed >= 0) wait1(&sh.v_full, v_armed);
+    }
   } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
+    // ------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = instr_desc<T>();
       const uint32_t q_addr = smem_u32(q_buf);
-      const uint32_t kv_addr = smem_u32(kv_buf);
+      const uint32_t k_addr = smem_u32(k_buf);
+      const uint32_t v_addr = smem_u32(v_buf);
       const uint32_t p_addr = smem_u32(p_buf);
-      const uint32_t o_tmem = sh.tmem_base + kTmemO;
       int t = 0, it = 0;
       bool ok = true;
-      // P V of tile u (its P is in shared memory once p_full completes)
+      // O_x += P_x Vt for tile u of the current item, both query tiles
       auto issue_pv = [&](int u, bool first_of_item) -> bool {
-        if (!wait1(&sh.p_full, u & 1)) return false;
-        if (first_of_item && !wait1(&sh.o_empty, (it & 1) ^ 1)) return false;
-        tc_fence_after();
-        const uint32_t vt = kv_addr + (u % kKvStages) * 2 * kTileBytes + kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)
-          umma(o_tmem, operand_desc(p_addr, kk), operand_desc(vt, kk), idesc,
-               (first_of_item && kk == 0) ? 0u : 1u);
-        umma_commit(&sh.pv_done);
-        umma_commit(&sh.kv_empty[u % kKvStages]);
+        if (!wait1(&sh.v_full, u & 1)) return false;
+        for (int x = 0; x < kPair; ++x) {
+          if (!wait1(&sh.p_full[x], u & 1)) return false;
+          if (first_of_item && !wait1(&sh.o_empty[x], (it & 1) ^ 1)) return false;
+          tc_fence_after();
+          umma_k128(sh.tmem_base + kTmemO + x * kTile, p_addr + x * kTileBytes, v_addr, idesc,
+                    !first_of_item);
+          umma_commit(&sh.pv_done[x]);
+        }
+        umma_commit(&sh.v_empty);
         return true;
       };
-      for (int k = 0, item = cta_item(0); item < items && ok && !aborted(sh); item = cta_item(++k), ++it) {
-        const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+      for (int k = 0, item = cta_item(0); item < items && ok && !aborted(sh);
+           item = cta_item(++k), ++it) {
+        const int qp = c.q_pairs - 1 - item / c.num_kv_heads;
         if (!wait1(&sh.q_full, it & 1)) { ok = false; break; }
-        const int kt_end = max(c.tile_max[qt], 0) / kTile;
+        const int kt_end = max(c.pair_max[qp], 0) / kTile;
         for (int kt = 0; kt <= kt_end; ++kt, ++t) {
-          const int s = t % kKvStages;
-          const int sb = t & 1;
-          if (!wait1(&sh.kv_full[s], (t / kKvStages) & 1) ||
-              !wait1(&sh.s_empty[sb], ((t >> 1) & 1) ^ 1)) {
-            ok = false;
-            break;
+          const int s = t % kKStages;
+          if (!wait1(&sh.k_full[s], (t / kKStages) & 1)) { ok = false; break; }
+          const uint32_t kb = k_addr + s * kTileBytes;
+          for (int x = 0; x < kPair; ++x) {
+            if (!wait1(&sh.s_empty[x], (t & 1) ^ 1)) { ok = false; break; }
+            tc_fence_after();
+            umma_k128(sh.tmem_base + x * kTile, q_addr + x * kTileBytes, kb, idesc, false);
+            umma_commit(&sh.s_full[x]);
           }
-          tc_fence_after();
-          const uint32_t kb = kv_addr + s * 2 * kTileBytes;
-#pragma unroll
-          for (int kk = 0; kk < kHead / 16; ++kk)
-            umma(sh.tmem_base + sb * kTile, operand_desc(q_addr, kk), operand_desc(kb, kk), idesc,
-                 kk > 0 ? 1u : 0u);
-          umma_commit(&sh.s_full[sb]);
-          umma_commit(&sh.kv_empty[s]);
+          if (!ok) break;
+          umma_commit(&sh.k_empty[s]);
           if (kt > 0 && !issue_pv(t - 1, kt == 1)) {
             ok = false;
             break;
@@ -287,32 +329,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(&sh.drain);
       wait1(&sh.drain, 0);
     }
-  } else if (warp >= 4) {
-    // ---------------------------------------------------------- softmax / epilogue
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+    // ------------------------------------------------------ softmax / epilogue
+    const int x = (warp - 4) >> 2;           // query tile of the pair
     const int ew = warp & 3;                 // TMEM lanes 32*ew .. +31
     const int row_in_tile = ew * 32 + lane;  // this thread's row
     const uint32_t lane_off = static_cast<uint32_t>(ew * 32) << 16;
+    const uint32_t s_tmem = sh.tmem_base + x * kTile + lane_off;
+    const uint32_t o_tmem = sh.tmem_base + kTmemO + x * kTile + lane_off;
+    unsigned char* my_p = p_buf + x * kTileBytes;
     int t = 0;
     bool ok = true;
     for (int k = 0, item = cta_item(0); item < items && ok; item = cta_item(++k)) {
-      const int qt = c.q_tiles - 1 - item / c.num_kv_heads;
+      const int qp = c.q_pairs - 1 - item / c.num_kv_heads;
       const int h = item % c.num_kv_heads;
-      const int r = qt * kTile + row_in_tile;
+      const int r = qp * kPairRows + x * kTile + row_in_tile;
       const int pos = c.row_pos[r];
-      const int kt_end = max(c.tile_max[qt], 0) / kTile;
+      const int kt_end = max(c.pair_max[qp], 0) / kTile;
       float m_used = -INFINITY;  // log2-domain max the exponentials are taken against
       float l = 0.0f;
       for (int kt = 0; kt <= kt_end; ++kt, ++t) {
-        const int sb = t & 1;
-        if (!wait_warp(&sh.s_full[sb], (t >> 1) & 1)) { ok = false; break; }
+        if (!wait_warp(&sh.s_full[x], t & 1)) { ok = false; break; }
         tc_fence_after();
         uint32_t v[4][32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld32(sh.tmem_base + sb * kTile + lane_off + q * 32, v[q]);
+        for (int q = 0; q < 4; ++q) tmem_ld32(s_tmem + q * 32, v[q]);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.s_empty[sb]);
+        if (lane == 0) mbar_arrive(&sh.s_empty[x]);
         // the reference's roundings: T logits, T (logit * scale); keys > pos masked
         const int valid = min(max(pos - kt * kTile + 1, 0), kTile);
         float2 w[64];
@@ -339,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * kLog2e;
         const bool grow = tile_max > m_used + kRescaleLog2 || (m_used == -INFINITY && tile_max > -INFINITY);
         // the P buffer is free and O settled once the previous tile's P V is done
-        if (kt > 0 && !wait_warp(&sh.pv_done, (t - 1) & 1)) { ok = false; break; }
+        if (kt > 0 && !wait_warp(&sh.pv_done[x], (t - 1) & 1)) { ok = false; break; }
         if (__any_sync(0xffffffffu, grow)) {
           const float m_new = grow ? tile_max : m_used;
           const float corr = grow ? (m_used == -INFINITY ? 0.0f : ex2(m_used - m_new)) : 1.0f;
@@ -348,11 +395,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               uint32_t o[32];
-              tmem_ld32(sh.tmem_base + kTmemO + lane_off + q * 32, o);
+              tmem_ld32(o_tmem + q * 32, o);
               tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * corr);
-              tmem_st32(sh.tmem_base + kTmemO + lane_off + q * 32, o);
+              tmem_st32(o_tmem + q * 32, o);
             }
             tmem_wait_st();
           }
@@ -372,14 +419,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t packed[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 x = __ffma2_rn(w[c16 * 4 + e], l2e, nm);
-            const float2 p = make_float2(ex2(x.x), ex2(x.y));
-            sm[e] = __fadd2_rn(sm[e], p);
-            packed[e] = pack2<T>(p.x, p.y);
+            const float2 xe = __ffma2_rn(w[c16 * 4 + e], l2e, nm);
+            const float2 pe = make_float2(ex2(xe.x), ex2(xe.y));
+            sm[e] = __fadd2_rn(sm[e], pe);
+            packed[e] = pack2<T>(pe.x, pe.y);
           }
           const int half = c16 >> 3;
           const int chunk = c16 & 7;
-          unsigned char* dst = p_buf + half * kHalfBytes + row_in_tile * 128 +
+          unsigned char* dst = my_p + half * kHalfBytes + row_in_tile * 128 +
                                ((chunk ^ (row_in_tile & 7)) * 16);
           *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
@@ -390,11 +437,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_async_smem();  // generic-proxy P writes -> the MMA's async-proxy reads
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.p_full);
+        if (lane == 0) mbar_arrive(&sh.p_full[x]);
       }
       if (!ok) break;
       // O of this item complete once the last P V is done
-      if (!wait_warp(&sh.pv_done, (t - 1) & 1)) { ok = false; break; }
+      if (!wait_warp(&sh.pv_done[x], (t - 1) & 1)) { ok = false; break; }
       tc_fence_after();
       const int64_t qi = static_cast<int64_t>(r) / c.groups;
       const int g = r - static_cast<int>(qi) * c.groups;
@@ -405,22 +452,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint32_t o[32];
-        tmem_ld32(sh.tmem_base + kTmemO + lane_off + q * 32, o);
+        tmem_ld32(o_tmem + q * 32, o);
         tmem_wait_ld();
         if (store) {
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
-            const uint4 w = make_uint4(pack2<T>(__uint_as_float(o[j]) * inv, __uint_as_float(o[j + 1]) * inv),
-                                       pack2<T>(__uint_as_float(o[j + 2]) * inv, __uint_as_float(o[j + 3]) * inv),
-                                       pack2<T>(__uint_as_float(o[j + 4]) * inv, __uint_as_float(o[j + 5]) * inv),
-                                       pack2<T>(__uint_as_float(o[j + 6]) * inv, __uint_as_float(o[j + 7]) * inv));
-            *reinterpret_cast<uint4*>(dst + q * 32 + j) = w;
+            const uint4 wv = make_uint4(pack2<T>(__uint_as_float(o[j]) * inv, __uint_as_float(o[j + 1]) * inv),
+                                        pack2<T>(__uint_as_float(o[j + 2]) * inv, __uint_as_float(o[j + 3]) * inv),
+                                        pack2<T>(__uint_as_float(o[j + 4]) * inv, __uint_as_float(o[j + 5]) * inv),
+                                        pack2<T>(__uint_as_float(o[j + 6]) * inv, __uint_as_float(o[j + 7]) * inv));
+            *reinterpret_cast<uint4*>(dst + q * 32 + j) = wv;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh.o_empty);
+      if (lane == 0) mbar_arrive(&sh.o_empty[x]);
     }
     if (!ok && lane == 0) report(c, sh, 3);
   }
@@ -435,14 +482,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Qd[h][r][:] = query[r / groups][h * groups + r % groups][:], zero rows up to
-// rows_pad; row positions; per-tile max position.
+// rows_pad; row positions; the largest position of each pair of query tiles.
 __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ query,
                                                    int64_t query_token_stride,
                                                    const int64_t* __restrict__ positions,
                                                    int64_t num_queries, int num_kv_heads, int groups,
                                                    int rows_pad, char* __restrict__ qd,
                                                    int32_t* __restrict__ row_pos,
-                                                   int32_t* __restrict__ tile_max) {
+                                                   int32_t* __restrict__ pair_max) {
   constexpr int kRowBytes = kHead * 2;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -463,16 +510,16 @@ __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ quer
     }
     if (h == 0 && lane == 0) row_pos[r] = qi < num_queries ? static_cast<int32_t>(positions[qi]) : -1;
   }
-  const int q_tiles = rows_pad / kTile;
-  for (int64_t qt = warp; qt < q_tiles; qt += nwarps) {
+  const int q_pairs = rows_pad / kPairRows;
+  for (int64_t qt = warp; qt < q_pairs; qt += nwarps) {
     int mx = -1;
-    for (int r = lane; r < kTile; r += 32) {
-      const int64_t qi = (qt * kTile + r) / groups;
+    for (int r = lane; r < kPairRows; r += 32) {
+      const int64_t qi = (qt * kPairRows + r) / groups;
       if (qi < num_queries) mx = max(mx, static_cast<int>(positions[qi]));
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) tile_max[qt] = mx;
+    if (lane == 0) pair_max[qt] = mx;
   }
 }
 
@@ -507,7 +554,7 @@ __global__ void __launch_bounds__(256) transpose_kernel(const char* __restrict__
 
 // ---------------------------------------------------------------- host side
 struct Workspace {
-  size_t qd, vt, row_pos, tile_max, total;
+  size_t qd, vt, row_pos, pair_max, total;
   int64_t rows_pad, keys_pad;
 };
 
@@ -516,7 +563,7 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 Workspace layout(int64_t num_queries, int64_t num_keys, int64_t num_q_heads, int64_t num_kv_heads) {
   const int64_t groups = num_q_heads / num_kv_heads;
   Workspace w{};
-  w.rows_pad = (num_queries * groups + kTile - 1) / kTile * kTile;
+  w.rows_pad = (num_queries * groups + kPairRows - 1) / kPairRows * kPairRows;
   w.keys_pad = (num_keys + kTile - 1) / kTile * kTile;
   size_t off = 0;
   w.qd = off;
@@ -525,13 +572,15 @@ Workspace layout(int64_t num_queries, int64_t num_keys, int64_t num_q_heads, int
   off = align_up(off + (size_t)num_kv_heads * kHead * w.keys_pad * 2, 1024);
   w.row_pos = off;
   off = align_up(off + (size_t)w.rows_pad * 4, 256);
-  w.tile_max = off;
-  off = align_up(off + (size_t)(w.rows_pad / kTile) * 4, 256);
+  w.pair_max = off;
+  off = align_up(off + (size_t)(w.rows_pad / kPairRows) * 4, 256);
   w.total = off;
   return w;
 }
 
-constexpr size_t kDynSmem = 1024 + (1 + 2 * kKvStages + 1) * kTileBytes;
+// kPair Q tiles, kKStages K tiles, one Vt tile, kPair P tiles (+ 1 KiB alignment slack)
+constexpr size_t kDynSmem = 1024 + (2 * kPair + kKStages + 1) * kTileBytes;
+static_assert(kDynSmem + 1024 <= 232448, "shared memory per CTA (static part padded to 1 KiB)");
 
 int check_shape(int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int dtype) {
   CB_SUPPORTED(dtype == CB_DTYPE_BF16 || dtype == CB_DTYPE_FP16,
@@ -597,7 +646,7 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
                                            query_positions, num_queries, static_cast<int>(num_kv_heads),
                                            groups, static_cast<int>(w.rows_pad), ws + w.qd,
                                            reinterpret_cast<int32_t*>(ws + w.row_pos),
-                                           reinterpret_cast<int32_t*>(ws + w.tile_max));
+                                           reinterpret_cast<int32_t*>(ws + w.pair_max));
     rc = launch_status("cb_blend_attention (prep)");
     if (rc != CB_OK) return rc;
     const int64_t blocks = num_kv_heads * (w.keys_pad / 64);
@@ -625,15 +674,15 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
   c.num_kv_heads = static_cast<int>(num_kv_heads);
   c.groups = groups;
   c.rows_pad = static_cast<int>(w.rows_pad);
-  c.q_tiles = static_cast<int>(w.rows_pad / tc::kTile);
+  c.q_pairs = static_cast<int>(w.rows_pad / att::kPairRows);
   c.num_queries = num_queries;
   c.scale = scale;
   c.row_pos = reinterpret_cast<const int32_t*>(ws + w.row_pos);
-  c.tile_max = reinterpret_cast<const int32_t*>(ws + w.tile_max);
+  c.pair_max = reinterpret_cast<const int32_t*>(ws + w.pair_max);
   c.out = static_cast<char*>(out);
   c.out_token_stride = out_token_stride;
   c.error = device_error;
-  const int grid = static_cast<int>(std::min<int64_t>(num_kv_heads * c.q_tiles, kSmCount));
+  const int grid = static_cast<int>(std::min<int64_t>(num_kv_heads * c.q_pairs, kSmCount));
   auto kernel = dtype == CB_DTYPE_BF16 ? att::attention_kernel<__nv_bfloat16>
                                        : att::attention_kernel<__half>;
   rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), att::kDynSmem);

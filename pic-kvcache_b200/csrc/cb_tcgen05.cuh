@@ -47,38 +47,41 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// try_wait with a suspend-time hint: while the phase is incomplete the thread
+// sleeps (up to hint_ns) until it completes instead of re-polling the barrier
+// word.  Polling warps would otherwise compete for shared-memory bandwidth,
+// which tcgen05.mma needs in full for its operands (a 128x128x16 product
+// reads 8 KiB in 64 cycles).
+constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms per try; the 2 s bound still applies
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
 // Single-thread bounded wait (producer / MMA lanes).
 __device__ __forceinline__ bool wait1(uint64_t* bar, uint32_t parity) {
-  uint64_t start = 0;
-  for (uint32_t spin = 0;; ++spin) {
-    if (mbar_try(bar, parity)) return true;
-    if ((spin & 255u) == 0) {
-      const uint64_t now = global_ns();
-      if (start == 0)
-        start = now;
-      else if (now - start > kTimeoutNs)
-        return false;
-    }
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  for (;;) {
+    if (mbar_try_sleep(bar, parity)) return true;
+    if (global_ns() - start > kTimeoutNs) return false;
   }
 }
-// Warp-uniform bounded wait (epilogue warps).
+// Warp-uniform bounded wait (epilogue warps).  A lane that already observed
+// the phase keeps observing it: the barrier cannot advance again before this
+// warp arrives on its peer barrier.
 __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity) {
-  uint64_t start = 0;
-  const int lane = threadIdx.x & 31;
-  for (uint32_t spin = 0;; ++spin) {
-    const bool mine = mbar_try(bar, parity);
-    if (__all_sync(0xffffffffu, mine)) return true;
-    if ((spin & 255u) == 0) {
-      int expired = 0;
-      if (lane == 0) {
-        const uint64_t now = global_ns();
-        if (start == 0)
-          start = now;
-        else if (now - start > kTimeoutNs)
-          expired = 1;
-      }
-      if (__shfl_sync(0xffffffffu, expired, 0)) return false;
-    }
+  if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
+  const uint64_t start = global_ns();
+  for (;;) {
+    if (__all_sync(0xffffffffu, mbar_try_sleep(bar, parity))) return true;
+    if (__shfl_sync(0xffffffffu, static_cast<int>(global_ns() - start > kTimeoutNs), 0)) return false;
   }
 }
 __device__ __forceinline__ void tma_load_3d(void* smem, const CUtensorMap* map, uint64_t* bar,
@@ -108,6 +111,65 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
 // SW128 halves 16 KiB apart.
 __device__ __forceinline__ uint64_t operand_desc(uint32_t tile_addr, int kk) {
   return sw128_desc(tile_addr + (kk >> 2) * kHalfBytes + (kk & 3) * 32);
+}
+// The same descriptor split in words: the high word is the same for every
+// operand here (SBO 1024 B, version 1, SWIZZLE_128B), the low word holds the
+// start address >> 4 (14 bits: shared memory stays below 256 KiB, so adding a
+// K-step offset never carries into the LBO field).  Issuing an MMA then costs
+// one add per operand instead of a 64-bit build.
+constexpr uint32_t kDescHi = 64u | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t desc_lo(uint32_t smem_addr) {
+  return ((smem_addr >> 4) & 0x3FFFu) | (1u << 16);
+}
+// Low-word offset of K step kk (16 elements) within a 128x128 operand stored as
+// two 128x64 SW128 halves 16 KiB apart.
+__host__ __device__ constexpr uint32_t kstep_lo(int kk) {
+  return static_cast<uint32_t>((kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2);
+}
+__device__ __forceinline__ void umma_lo(uint32_t tmem_d, uint32_t a_lo, uint32_t b_lo,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %5};\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHi));
+}
+// Eight K steps (K = 128) of a 128x128 product with both operands in shared
+// memory, issued from one asm block: per step two adds and the MMA, nothing
+// the issuing thread has to wait on, and only a few registers.
+__device__ __forceinline__ void umma_k128(uint32_t tmem_d, uint32_t a_tile, uint32_t b_tile,
+                                          uint32_t idesc, bool accumulate_first) {
+  static_assert(kstep_lo(1) == 2 && kstep_lo(4) == 1024, "K-step offsets baked into umma_k128");
+  asm volatile(
+      "{\n\t.reg .b64 da, db;\n\t.reg .b32 a, b;\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 da, {%1, %5};\n\tmov.b64 db, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t"
+      "add.u32 a, %1, 2;\n\tadd.u32 b, %2, 2;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 4;\n\tadd.u32 b, %2, 4;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 6;\n\tadd.u32 b, %2, 6;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1024;\n\tadd.u32 b, %2, 1024;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1026;\n\tadd.u32 b, %2, 1026;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1028;\n\tadd.u32 b, %2, 1028;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1030;\n\tadd.u32 b, %2, 1030;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t}" ::"r"(tmem_d),
+      "r"(desc_lo(a_tile)), "r"(desc_lo(b_tile)), "r"(idesc), "r"(accumulate_first ? 1u : 0u),
+      "n"(kDescHi));
 }
 __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
                                      uint32_t accumulate) {

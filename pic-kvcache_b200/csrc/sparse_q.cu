@@ -259,11 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d = sh.tmem_base + tb * kTile;
-#pragma unroll
-          for (int kk = 0; kk < kHead / 16; ++kk)
-            umma(d, operand_desc(a_addr + ab * kTileBytes, kk),
-                 operand_desc(b_addr + s * kTileBytes, kk), idesc, kk > 0);
+          umma_k128(sh.tmem_base + tb * kTile, a_addr + ab * kTileBytes, b_addr + s * kTileBytes,
+                    idesc, false);
           umma_commit(&sh.b_empty[s]);
           umma_commit(&sh.t_full[tb]);
         }
@@ -478,11 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t d = sh.tmem_base + tb * kTile;
-#pragma unroll
-            for (int kk = 0; kk < kHead / 16; ++kk)
-              umma(d, operand_desc(a_addr + ab * kTileBytes, kk),
-                   operand_desc(b_addr + s * kTileBytes, kk), idesc, kk > 0);
+            umma_k128(sh.tmem_base + tb * kTile, a_addr + ab * kTileBytes, b_addr + s * kTileBytes,
+                      idesc, false);
             umma_commit(&sh.b_empty[s]);
             umma_commit(&sh.t_full[tb]);
             ++t;
