@@ -856,7 +856,10 @@ def attention_bench(args, world: int, rank: int, local: int) -> None:
             "gpu_launches": 3 * args.steps, "launch": "eager (prep, value transpose, attention per step)",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": peaks["source"],
-                         "flops_note": "causal algorithmic: 4 x 128 x q_heads x sum(position + 1)"},
+                         "traffic": load_traffic().get(f"{cfg['name']}:attention:tp{world}")
+                         if not ATTENTION_KEYS else None,
+                         "flops_note": "causal algorithmic: 4 x 128 x q_heads x sum(position + 1); "
+                                       "timed over the whole step (prep, value transpose, attention)"},
             "context": {"torch_sdpa_masked_ms": sdpa_ms},
             "device_error": int(error.item()), "clocks": clocks.summary(), "cpu_baseline": cpu,
         }), flush=True)
