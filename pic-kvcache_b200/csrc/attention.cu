@@ -15,14 +15,14 @@
 //
 // Layout: rows = (query, group) pairs of one KV head, r = qi * groups + g, in
 // 128-row tiles (dense copy Qd[h][r][:] made by prep_kernel), so every K / V
-// tile is shared by all groups of the head.  V is transposed per head (Vt[h][d][k],
-// transpose_kernel) so that both products use K-major SWIZZLE_128B operands:
-//   S = Q K^T   A = Q tile [rows][dims],  B = K tile [keys][dims]   -> TMEM
-//   O += P V    A = P tile [rows][keys],  B = Vt tile [dims][keys]  -> TMEM
+// tile is shared by all groups of the head.  K and V tiles are TMA boxes of the
+// staging rows as they lie ([keys][dims], SWIZZLE_128B):
+//   S = Q K^T   A = Q tile [rows][dims] (K-major),  B = K tile [keys][dims] (K-major) -> TMEM
+//   O += P V    A = P tile [rows][keys] (K-major),  B = V tile [keys][dims] (MN-major) -> TMEM
 // An item is (KV head, pair of query tiles = 256 rows); CTAs are persistent and
 // take items dealt serpentine, latest queries first.  Per CTA, 12 warps:
 //   warp 0   Q loads per item, K tiles through a two-stage ring (TMA)
-//   warp 3   Vt tiles through one slot, loaded once the previous P V has read it
+//   warp 3   V tiles through one slot, loaded once the previous P V has read it
 //   warp 1   tcgen05.mma issue: S_A, S_B of key tile t, then P V of tile t-1 for
 //            both query tiles, so the tensor core computes ahead of the softmax
 //   warp 2   TMEM owner (S_A, S_B, O_A, O_B: 512 columns)
@@ -32,7 +32,7 @@
 //            (rounded to T) into shared memory in the SW128 layout the MMA
 //            reads, and at the end of an item divide O by the sum and store it.
 // While one warpgroup runs its softmax the tensor core works on the other
-// tile's products, and each K / Vt tile serves 256 rows.  O is rescaled
+// tile's products, and each K / V tile serves 256 rows.  O is rescaled
 // (tcgen05.ld / st) only when a row's max grows by more than 2^8: until then
 // the stale max keeps every exp2 <= 256, and the final division uses the same
 // max, so the result is unchanged.
@@ -166,7 +166,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap q_map,
                      const __grid_constant__ CUtensorMap k_map,
-                     const __grid_constant__ CUtensorMap vt_map, Params c) {
+                     const __grid_constant__ CUtensorMap v_map, Params c) {
   extern __shared__ __align__(1024) unsigned char dyn[];
   __shared__ Shared sh;
   const int warp = threadIdx.x >> 5;
@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(dyn) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* q_buf = base;                                  // kPair Q tiles
   unsigned char* k_buf = base + kPair * kTileBytes;             // kKStages K tiles
-  unsigned char* v_buf = k_buf + kKStages * kTileBytes;         // one Vt tile
+  unsigned char* v_buf = k_buf + kKStages * kTileBytes;         // one V tile
   unsigned char* p_buf = v_buf + kTileBytes;                    // kPair P tiles
   const int items = c.num_kv_heads * c.q_pairs;
 
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 3) {
     // ------------------------------------------------------ V loads
-    // Vt(t) may land only after P V of tile t-1 has read the previous one;
+    // V(t) may land only after P V of tile t-1 has read the previous one;
     // it is needed after S(t+1), so its latency hides behind those products.
     if (lane == 0) {
       int t = 0;
@@ -264,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kt = 0; kt <= kt_end; ++kt, ++t) {
           if (!wait1(&sh.v_empty, (t & 1) ^ 1)) { ok = false; break; }
           mbar_expect_tx(&sh.v_full, kTileBytes);
-          tma_load_3d(v_buf, &vt_map, &sh.v_full, kt * kTile, 0, h);
-          tma_load_3d(v_buf + kHalfBytes, &vt_map, &sh.v_full, kt * kTile + 64, 0, h);
+          tma_load_3d(v_buf, &v_map, &sh.v_full, 0, h, kt * kTile);
+          tma_load_3d(v_buf + kHalfBytes, &v_map, &sh.v_full, 64, h, kt * kTile);
           v_armed = t & 1;
         }
       }
@@ -276,21 +276,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = instr_desc<T>();
+      const uint32_t idesc_bmn = idesc | (1u << 16);  // B (V) MN-major
       const uint32_t q_addr = smem_u32(q_buf);
       const uint32_t k_addr = smem_u32(k_buf);
       const uint32_t v_addr = smem_u32(v_buf);
       const uint32_t p_addr = smem_u32(p_buf);
       int t = 0, it = 0;
       bool ok = true;
-      // O_x += P_x Vt for tile u of the current item, both query tiles
+      // O_x += P_x V for tile u of the current item, both query tiles
       auto issue_pv = [&](int u, bool first_of_item) -> bool {
         if (!wait1(&sh.v_full, u & 1)) return false;
         for (int x = 0; x < kPair; ++x) {
           if (!wait1(&sh.p_full[x], u & 1)) return false;
           if (first_of_item && !wait1(&sh.o_empty[x], (it & 1) ^ 1)) return false;
           tc_fence_after();
-          umma_k128(sh.tmem_base + kTmemO + x * kTile, p_addr + x * kTileBytes, v_addr, idesc,
-                    !first_of_item);
+          umma_k128_bmn(sh.tmem_base + kTmemO + x * kTile, p_addr + x * kTileBytes, v_addr,
+                        idesc_bmn, !first_of_item);
           umma_commit(&sh.pv_done[x]);
         }
         umma_commit(&sh.v_empty);
@@ -523,39 +524,10 @@ __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ quer
   }
 }
 
-// Vt[h][d][k] = value[k][h][d] for k < num_keys, zero up to keys_pad: 64 keys x
-// 128 dims per block through shared memory (both sides coalesced).
-__global__ void __launch_bounds__(256) transpose_kernel(const char* __restrict__ value,
-                                                        int64_t value_token_stride,
-                                                        int64_t num_keys, int64_t keys_pad,
-                                                        int num_kv_heads, char* __restrict__ vt) {
-  __shared__ uint16_t tile[kHead][64 + 2];
-  const int64_t blocks_per_head = keys_pad / 64;
-  for (int64_t b = blockIdx.x; b < blocks_per_head * num_kv_heads; b += gridDim.x) {
-    const int h = static_cast<int>(b / blocks_per_head);
-    const int64_t k0 = (b - (int64_t)h * blocks_per_head) * 64;
-    __syncthreads();
-    for (int i = threadIdx.x; i < 64 * kHead; i += blockDim.x) {
-      const int kk = i / kHead;
-      const int d = i - kk * kHead;
-      const int64_t key = k0 + kk;
-      tile[d][kk] = key < num_keys
-                        ? reinterpret_cast<const uint16_t*>(value + key * value_token_stride)[h * kHead + d]
-                        : uint16_t(0);
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < 64 * kHead; i += blockDim.x) {
-      const int d = i / 64;
-      const int kk = i - d * 64;
-      reinterpret_cast<uint16_t*>(vt)[((int64_t)h * kHead + d) * keys_pad + k0 + kk] = tile[d][kk];
-    }
-  }
-}
-
 // ---------------------------------------------------------------- host side
 struct Workspace {
-  size_t qd, vt, row_pos, pair_max, total;
-  int64_t rows_pad, keys_pad;
+  size_t qd, row_pos, pair_max, total;
+  int64_t rows_pad;
 };
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -564,12 +536,9 @@ Workspace layout(int64_t num_queries, int64_t num_keys, int64_t num_q_heads, int
   const int64_t groups = num_q_heads / num_kv_heads;
   Workspace w{};
   w.rows_pad = (num_queries * groups + kPairRows - 1) / kPairRows * kPairRows;
-  w.keys_pad = (num_keys + kTile - 1) / kTile * kTile;
   size_t off = 0;
   w.qd = off;
   off = align_up(off + (size_t)num_kv_heads * w.rows_pad * kHead * 2, 1024);
-  w.vt = off;
-  off = align_up(off + (size_t)num_kv_heads * kHead * w.keys_pad * 2, 1024);
   w.row_pos = off;
   off = align_up(off + (size_t)w.rows_pad * 4, 256);
   w.pair_max = off;
@@ -578,7 +547,7 @@ Workspace layout(int64_t num_queries, int64_t num_keys, int64_t num_q_heads, int
   return w;
 }
 
-// kPair Q tiles, kKStages K tiles, one Vt tile, kPair P tiles (+ 1 KiB alignment slack)
+// kPair Q tiles, kKStages K tiles, one V tile, kPair P tiles (+ 1 KiB alignment slack)
 constexpr size_t kDynSmem = 1024 + (2 * kPair + kKStages + 1) * kTileBytes;
 static_assert(kDynSmem + 1024 <= 232448, "shared memory per CTA (static part padded to 1 KiB)");
 
@@ -649,26 +618,19 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
                                            reinterpret_cast<int32_t*>(ws + w.pair_max));
     rc = launch_status("cb_blend_attention (prep)");
     if (rc != CB_OK) return rc;
-    const int64_t blocks = num_kv_heads * (w.keys_pad / 64);
-    const int tgrid = static_cast<int>(std::min<int64_t>(blocks, kSmCount * 8));
-    att::transpose_kernel<<<tgrid, 256, 0, s>>>(static_cast<const char*>(value), value_token_stride,
-                                                 num_keys, w.keys_pad, static_cast<int>(num_kv_heads),
-                                                 ws + w.vt);
-    rc = launch_status("cb_blend_attention (transpose)");
-    if (rc != CB_OK) return rc;
   }
   tc::EncodeTiled encode = nullptr;
   rc = tc::get_encoder(&encode);
   if (rc != CB_OK) return rc;
-  CUtensorMap q_map, k_map, vt_map;
+  CUtensorMap q_map, k_map, v_map;
   rc = tc::encode_3d(encode, &q_map, dtype, ws + w.qd, head_size, w.rows_pad, num_kv_heads,
                      head_size * 2, w.rows_pad * head_size * 2, tc::kTile, 1);
   if (rc == CB_OK)
     rc = tc::encode_3d(encode, &k_map, dtype, key, head_size, num_kv_heads, num_keys, head_size * 2,
                        key_token_stride, 1, tc::kTile);
   if (rc == CB_OK)
-    rc = tc::encode_3d(encode, &vt_map, dtype, ws + w.vt, w.keys_pad, head_size, num_kv_heads,
-                       w.keys_pad * 2, head_size * w.keys_pad * 2, tc::kTile, 1);
+    rc = tc::encode_3d(encode, &v_map, dtype, value, head_size, num_kv_heads, num_keys,
+                       head_size * 2, value_token_stride, 1, tc::kTile);
   if (rc != CB_OK) return rc;
   att::Params c{};
   c.num_kv_heads = static_cast<int>(num_kv_heads);
@@ -687,6 +649,6 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
                                        : att::attention_kernel<__half>;
   rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), att::kDynSmem);
   if (rc != CB_OK) return rc;
-  kernel<<<grid, att::kThreads, att::kDynSmem, s>>>(q_map, k_map, vt_map, c);
+  kernel<<<grid, att::kThreads, att::kDynSmem, s>>>(q_map, k_map, v_map, c);
   return launch_status("cb_blend_attention");
 }

@@ -171,6 +171,47 @@ __device__ __forceinline__ void umma_k128(uint32_t tmem_d, uint32_t a_tile, uint
       "r"(desc_lo(a_tile)), "r"(desc_lo(b_tile)), "r"(idesc), "r"(accumulate_first ? 1u : 0u),
       "n"(kDescHi));
 }
+// B operand stored MN-major (N contiguous), as a TMA tile of 128 K-rows x 64
+// N-elements (SW128, 128 B per row) per box with the second 64 N-elements
+// 16 KiB further: LBO = 16 KiB between the two N atoms, SBO = 1 KiB between
+// 8-row K groups (the common high word), each K step of 16 rows 2 KiB further.
+__device__ __forceinline__ uint32_t desc_lo_mn(uint32_t smem_addr) {
+  return ((smem_addr >> 4) & 0x3FFFu) | (static_cast<uint32_t>(kHalfBytes >> 4) << 16);
+}
+// Eight K steps (K = 128) with A K-major and B MN-major (instruction
+// descriptor with the B-major bit set), both in shared memory.
+__device__ __forceinline__ void umma_k128_bmn(uint32_t tmem_d, uint32_t a_tile, uint32_t b_tile,
+                                              uint32_t idesc, bool accumulate_first) {
+  static_assert(kstep_lo(1) == 2 && kstep_lo(4) == 1024, "K-step offsets baked into umma_k128_bmn");
+  asm volatile(
+      "{\n\t.reg .b64 da, db;\n\t.reg .b32 a, b;\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 da, {%1, %5};\n\tmov.b64 db, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t"
+      "add.u32 a, %1, 2;\n\tadd.u32 b, %2, 128;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 4;\n\tadd.u32 b, %2, 256;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 6;\n\tadd.u32 b, %2, 384;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1024;\n\tadd.u32 b, %2, 512;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1026;\n\tadd.u32 b, %2, 640;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1028;\n\tadd.u32 b, %2, 768;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t"
+      "add.u32 a, %1, 1030;\n\tadd.u32 b, %2, 896;\n\t"
+      "mov.b64 da, {a, %5};\n\tmov.b64 db, {b, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t}" ::"r"(tmem_d),
+      "r"(desc_lo(a_tile)), "r"(desc_lo_mn(b_tile)), "r"(idesc), "r"(accumulate_first ? 1u : 0u),
+      "n"(kDescHi));
+}
 __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
                                      uint32_t accumulate) {
   asm volatile(
