@@ -853,13 +853,13 @@ def attention_bench(args, world: int, rank: int, local: int) -> None:
                        "q_heads_per_rank": hq, "kv_heads_per_rank": int(key.shape[1]),
                        "l2": "inputs larger than L2 (K, V and Q: %d MiB)"
                              % ((key.numel() * 2 + query.numel()) * 2 >> 20)},
-            "gpu_launches": 3 * args.steps, "launch": "eager (prep, value transpose, attention per step)",
+            "gpu_launches": 2 * args.steps, "launch": "eager (query prep, attention per step)",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": peaks["source"],
                          "traffic": load_traffic().get(f"{cfg['name']}:attention:tp{world}")
                          if not ATTENTION_KEYS else None,
                          "flops_note": "causal algorithmic: 4 x 128 x q_heads x sum(position + 1); "
-                                       "timed over the whole step (prep, value transpose, attention)"},
+                                       "timed over the whole step (query prep, attention)"},
             "context": {"torch_sdpa_masked_ms": sdpa_ms},
             "device_error": int(error.item()), "clocks": clocks.summary(), "cpu_baseline": cpu,
         }), flush=True)
