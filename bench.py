@@ -1012,6 +1012,8 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
     cfg = STORE_CONFIG
     device = torch.device("cuda", local)
     connector, caches, heads = store_connector(cfg, world, rank, device)
+    if args.store_no_arena:  # per-batch pinned buffers published as views (A/B study)
+        connector._store.arena = None
     rng = np.random.default_rng(9)
     rng_tokens = rng.integers(0, 151_936, size=(cfg["requests"], cfg["tokens"]), dtype=np.int64)
     blocks = rng.permutation(cfg["requests"] * cfg["tokens"] // cfg["block_size"])
@@ -1078,7 +1080,13 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": d2h,
                     "note": "the Store path starts from vLLM pages in HBM and ends in host memory: value is "
                             "already measured through the connector API with the D2H inside"},
-            "store": {"committed_entries": store.committed_entries, "bytes": store.current_bytes},
+            "store": {"committed_entries": store.committed_entries, "bytes": store.current_bytes,
+                      "committed_tokens": store.committed_entries * cfg["chunk"],
+                      "pinned_arena_bytes": store.arena.pinned_bytes if store.arena is not None else None,
+                      "note": "the LRU budget (16 GiB) holds 455 of the 2,048 chunks offered per step; "
+                              "with the pinned arena a chunk that cannot get a slot fails closed before "
+                              "its D2H, without it every chunk is copied and the surplus fails at "
+                              "publication (d2h_bytes_per_step shows which)"},
             "clocks": clocks.summary(), "cpu_baseline": cpu,
         }), flush=True)
     connector.close()
@@ -1105,6 +1113,8 @@ def main() -> None:
                         help="override the layer count (small profiling captures only)")
     parser.add_argument("--attention-tokens", type=int, default=0,
                         help="config 6 context length override (small profiling captures only)")
+    parser.add_argument("--store-no-arena", action="store_true",
+                        help="config 5: per-batch pinned buffers instead of the pinned arena (A/B study)")
     parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
                         help="host->device mode of the e2e loader (CACHEBLEND_B200_LOAD)")
     args = parser.parse_args()

@@ -96,6 +96,17 @@ CB_API int cb_paged_scatter(const void* src, int64_t src_plane_stride, int64_t s
                      const int64_t* slots, int64_t num_tokens, void* stream);
 
 /*
+ * Strided device -> host copy (copy engine) on `stream`: `rows` rows of
+ * `row_bytes`, `src_pitch` bytes apart in device memory and `dst_pitch` bytes
+ * apart in pinned host memory.  The Store path's batch transfer
+ * (cacheblend_vllm/connector.py:384-447, the D2H of `_enqueue_store_batch`)
+ * into consecutive pinned-arena entries: one transfer per run of entries,
+ * row pitch = the entry size.
+ */
+CB_API int cb_copy_rows_d2h(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                            int64_t row_bytes, int64_t rows, void* stream);
+
+/*
  * Number of common entries of two strictly ascending int64 index lists
  * (device memory), written to *count (device memory) on `stream`.  The
  * overlap of the two selections that the `compare` strategy reports

@@ -19,6 +19,7 @@ and can be plugged in through the same two methods.
 
 from __future__ import annotations
 
+import math
 import re
 import threading
 import time
@@ -35,8 +36,10 @@ from vllm.distributed.kv_transfer.kv_connector.v1.base import (
 )
 
 from . import registry
+from .arena import PinnedArena
 from .config import CacheBlendConfig
 from .executor import Qwen3BlendExecutor
+from .kv_layout import describe_paged
 from .loader import PagedBlendLoader
 from .storage import LocalPinnedCPUStore
 from .store_path import StorePipeline
@@ -221,6 +224,9 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
         except (AssertionError, ImportError):
             self._rank = 0
         self._store = LocalPinnedCPUStore(self.config.chunk_size, self.config.max_local_cpu_bytes)
+        arena = self._make_arena()
+        if arena is not None:
+            self._store.attach_arena(arena)
         registry.register_store(self.engine_id, self._rank, self._store)
         first = self._kv_caches[0]
         device = (first if isinstance(first, torch.Tensor) else first[0]).device
@@ -235,6 +241,22 @@ class CacheBlendConnectorV1(KVConnectorBase_V1, SupportsHMA):
             self._executor = Qwen3BlendExecutor(registry.get_model(self.engine_id), self.config, self.block_size)
         self._trace.emit("worker_registered", rank=self._rank, layers=len(self._kv_caches),
                          cpu_cache_bytes=self.config.max_local_cpu_bytes)
+
+    def _make_arena(self):
+        """A pinned arena sized by ``local_cpu_gb`` when every layer has the same chunk
+        geometry (one entry = every layer of one chunk); None otherwise (hybrid caches
+        keep per-batch pinned buffers)."""
+        geometry = set()
+        for cache in self._kv_caches:
+            paged = describe_paged(cache, self.block_size)
+            geometry.add((tuple(paged.row.dims), paged.dtype))
+        if len(geometry) != 1:
+            return None
+        dims, dtype = geometry.pop()
+        layer_bytes = 2 * self.config.chunk_size * math.prod(dims) * torch.empty((), dtype=dtype).element_size()
+        if layer_bytes * len(self._kv_caches) > self.config.max_local_cpu_bytes:
+            return None
+        return PinnedArena(layer_bytes, len(self._kv_caches), self.config.max_local_cpu_bytes)
 
     def start_load_kv(self, forward_context, **kwargs: Any) -> None:
         metadata = self._get_connector_metadata()

@@ -16,6 +16,14 @@ fail-closed capacity behaviour and hit rates depend on them:
   reserved and no request pins it.
 
 The bytes of a layer are ``numel * element_size`` of the published tensor.
+
+Arena mode (``attach_arena``, used by the Store path): an entry's layers live
+in one slot of a ``PinnedArena`` taken when the entry's first layer transfer is
+reserved (``arena_reserve``).  When no slot is free, committed unpinned entries
+other than the writer are evicted in LRU order until one is; when none can be,
+the entry fails closed exactly as an over-budget put does.  Removing an entry
+returns its slot.  The byte accounting of published layers is unchanged, and
+the arena's size never exceeds ``max_bytes``.
 """
 
 from __future__ import annotations
@@ -43,6 +51,7 @@ class _Entry:
     committed: bool = False
     failed: bool = False
     last_access: float = field(default_factory=time.monotonic)
+    slot: int | None = None  # arena slot holding every layer (arena mode)
 
     def idle(self) -> bool:
         return not self.reserved_layers and not self.pin_count
@@ -67,6 +76,7 @@ class LocalPinnedCPUStore:
         self._bytes = 0
         self._request_pins: dict[str, tuple[SegmentId, ...]] = {}
         self._lock = threading.RLock()
+        self.arena = None  # PinnedArena once attached
 
     # ---- introspection ------------------------------------------------------
     @property
@@ -82,6 +92,58 @@ class LocalPinnedCPUStore:
         """Entries from least to most recently used (for tests and tooling)."""
         with self._lock:
             return list(self._entries)
+
+    # ---- arena mode ------------------------------------------------------------
+    def attach_arena(self, arena) -> None:
+        """Publish the Store path's layers into ``arena`` slots from now on."""
+        with self._lock:
+            if self.arena is not None and self.arena is not arena:
+                raise RuntimeError("the store already has an arena")
+            self.arena = arena
+
+    def arena_reserve(self, segment_ids: Sequence[SegmentId], layer_id: int) -> list[int | None]:
+        """Per segment, the arena slot that layer ``layer_id`` is to be copied into, or
+        None when the transfer is dropped (unknown, failed or committed entry, or no slot
+        could be freed: the entry then fails closed and its reservation is released)."""
+        if self.arena is None:
+            raise RuntimeError("no arena attached")
+        out: list[int | None] = []
+        with self._lock:
+            for sid in segment_ids:
+                entry = self._entries.get(sid)
+                if entry is None:
+                    out.append(None)
+                    continue
+                self._check_layer(entry, layer_id)
+                if entry.committed or entry.failed:
+                    entry.reserved_layers.discard(layer_id)
+                    if entry.failed and entry.idle():
+                        self._remove(sid, entry)
+                    out.append(None)
+                    continue
+                if entry.slot is None:
+                    slot = self.arena.alloc()
+                    if slot is None:
+                        self._evict_slot(exclude=sid)
+                        slot = self.arena.alloc()
+                    if slot is None:
+                        entry.reserved_layers.discard(layer_id)
+                        entry.failed = True
+                        if entry.idle():
+                            self._remove(sid, entry)
+                        out.append(None)
+                        continue
+                    entry.slot = slot
+                out.append(entry.slot)
+        return out
+
+    def _evict_slot(self, exclude: SegmentId | None = None) -> None:
+        """Evict the least recently used committed, unpinned entry holding a slot."""
+        for sid, entry in self._committed.items():
+            if sid == exclude or entry.pin_count or entry.slot is None:
+                continue
+            self._remove(sid, entry)
+            return
 
     # ---- writers -------------------------------------------------------------
     def begin_put(
@@ -289,8 +351,11 @@ class LocalPinnedCPUStore:
 
     def clear(self) -> None:
         with self._lock:
-            for sid in list(self._entries):
+            for sid, entry in list(self._entries.items()):
                 self.matcher.unregister(sid)
+                if entry.slot is not None:
+                    self.arena.free(entry.slot)
+                    entry.slot = None
             self._entries.clear()
             self._committed.clear()
             self._request_pins.clear()
@@ -313,6 +378,11 @@ class LocalPinnedCPUStore:
         self._entries.pop(segment_id, None)
         self._committed.pop(segment_id, None)
         self._bytes -= entry.size_bytes
+        if entry.slot is not None:
+            # later copies into the slot are ordered after any still in flight
+            # (one Store stream), and readers pin the entries they read
+            self.arena.free(entry.slot)
+            entry.slot = None
 
     def _evict(self, required_bytes: int = 0, exclude: SegmentId | None = None) -> None:
         if self._bytes + required_bytes <= self.max_bytes:

@@ -14,9 +14,13 @@ stream (cacheblend_vllm/connector.py:384-549):
   then drop the staging buffers (they may still be read until then).
 
 B200 specifics: the staging is chunk-major ``[chunks, 2, chunk, H, D]`` so the
-gather is one ``cb_paged_gather`` launch, the D2H is one copy-engine transfer
-of the whole batch, and every published chunk view is contiguous (one DMA
-when the chunk is loaded again).
+gather is one ``cb_paged_gather`` launch and every published chunk view is
+contiguous (one DMA when the chunk is loaded again).  With a pinned arena
+attached to the store, each chunk's layer is copied straight into its entry's
+arena slot: chunks in consecutive slots go in one strided copy-engine
+transfer (``cb_copy_rows_d2h``, row pitch = the entry size), so a batch of
+chunks begun together is still one transfer.  Without an arena the batch goes
+to a fresh pinned buffer in one transfer and its chunks are published as views.
 """
 
 from __future__ import annotations
@@ -115,14 +119,19 @@ class StorePipeline:
                     finish = torch.cuda.Event(enable_timing=True)
                     finish.record(self.stream)
                     self.kernel_events.append((begin, finish, staging.numel() * staging.element_size()))
-                host = torch.empty(shape, dtype=paged.dtype, pin_memory=True)
-                host.copy_(staging, non_blocking=True)
-                self.d2h_bytes += host.numel() * host.element_size()
+                arena_slots = self._arena_copy(pending, staging)
+                if arena_slots is None:
+                    host = torch.empty(shape, dtype=paged.dtype, pin_memory=True)
+                    host.copy_(staging, non_blocking=True)
+                    self.d2h_bytes += host.numel() * host.element_size()
+                else:
+                    host = None
                 event = torch.cuda.Event()
                 event.record(self.stream)
                 device_slots_.record_stream(self.stream)
             future = self._pool.submit(
-                self._publish_after_event, event, pending, host, request_id, store_enqueued_ns
+                self._publish_after_event, event, pending, host, request_id, store_enqueued_ns,
+                arena_slots, shape[1:], paged.dtype,
             )
         except Exception:
             self._slots.release()
@@ -131,6 +140,35 @@ class StorePipeline:
             self._futures.add(future)
             self._pending_counts[request_id] = self._pending_counts.get(request_id, 0) + 1
         future.add_done_callback(self._done)
+
+    def _arena_copy(self, pending: list[tuple[Any, int, int]], staging: torch.Tensor) -> list | None:
+        """Reserve arena slots for the batch's chunks and copy each chunk's layer into its
+        slot (one strided transfer per run of consecutive slots) on the Store stream.
+        Returns the slot per chunk (None: dropped, fail closed) or None when the batch
+        does not use the arena (no arena, mixed layers or another chunk geometry)."""
+        arena = self.store.arena
+        if arena is None or not pending:
+            return None
+        layer_id = pending[0][1]
+        chunk_bytes = staging[0].numel() * staging.element_size()
+        if chunk_bytes != arena.layer_bytes or any(layer != layer_id for _, layer, _ in pending):
+            return None
+        slots = self.store.arena_reserve([sid for sid, _, _ in pending], layer_id)
+        kept = [(i, slot) for i, slot in enumerate(slots) if slot is not None]
+        stream = self.stream.cuda_stream
+        start = 0
+        while start < len(kept):
+            end = start + 1
+            while (end < len(kept) and kept[end][0] == kept[end - 1][0] + 1
+                   and kept[end][1] == kept[end - 1][1] + 1
+                   and kept[end][1] // arena.slots_per_segment == kept[start][1] // arena.slots_per_segment):
+                end += 1
+            index, slot = kept[start]
+            _native.call("cb_copy_rows_d2h", arena.layer_ptr(slot, layer_id), arena.entry_bytes,
+                         staging[index].data_ptr(), chunk_bytes, chunk_bytes, end - start, stream)
+            self.d2h_bytes += (end - start) * chunk_bytes
+            start = end
+        return slots
 
     def _describe(self, kv_layer: Any):
         """``describe_paged`` memoised on the layer tensors' identity and geometry."""
@@ -164,17 +202,37 @@ class StorePipeline:
                 committed |= result
         return committed
 
+    def publish_arena_batch(self, pending: list[tuple[Any, int, int]], slots: list,
+                            chunk_shape: tuple[int, ...], dtype: torch.dtype) -> bool:
+        """Publish each copied chunk as a view of its arena slot; dropped chunks (no
+        slot) were already released by the reservation."""
+        arena = self.store.arena
+        layer_id = pending[0][1] if pending else 0
+        sids, views = [], []
+        for (sid, _, _), slot in zip(pending, slots):
+            if slot is not None:
+                sids.append(sid)
+                views.append(arena.layer_view(slot, layer_id, tuple(chunk_shape), dtype))
+        results = self.store.put_layers_host(sids, layer_id, views) if sids else []
+        return any(result for result in results if result is not None)
+
     def _publish_after_event(
         self,
         event: torch.cuda.Event,
         pending: list[tuple[Any, int, int]],
-        host: torch.Tensor,
+        host: torch.Tensor | None,
         request_id: str | None = None,
         store_enqueued_ns: int | None = None,
+        arena_slots: list | None = None,
+        chunk_shape: tuple[int, ...] = (),
+        dtype: torch.dtype | None = None,
     ) -> bool:
         try:
             event.synchronize()
-            committed = self.publish_host_batch(pending, host)
+            if arena_slots is not None:
+                committed = self.publish_arena_batch(pending, arena_slots, chunk_shape, dtype)
+            else:
+                committed = self.publish_host_batch(pending, host)
             if self.tracer.enabled:
                 self.tracer.emit(
                     "save_store_finished",

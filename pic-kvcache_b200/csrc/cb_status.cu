@@ -105,3 +105,27 @@ int launch_status(const char* kernel) {
 extern "C" int cb_abi_version(void) { return 1; }
 
 extern "C" const char* cb_last_error(void) { return cb::g_last_error; }
+
+// Strided device -> host copy on the copy engine: `rows` rows of `row_bytes`,
+// rows `src_pitch` apart in device memory and `dst_pitch` apart in (pinned)
+// host memory.  One transfer for a Store batch whose chunks land in
+// consecutive arena entries (row pitch = the entry size).
+extern "C" int cb_copy_rows_d2h(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                                int64_t row_bytes, int64_t rows, void* stream) {
+  using namespace cb;
+  clear_error();
+  CB_REQUIRE(rows >= 0 && row_bytes >= 0, "negative size");
+  if (rows == 0 || row_bytes == 0) return CB_OK;
+  CB_REQUIRE(dst != nullptr && src != nullptr, "null pointer argument");
+  CB_REQUIRE(dst_pitch >= row_bytes && src_pitch >= row_bytes, "pitch smaller than a row");
+  CB_BIND(stream, src);
+  cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_pitch), src,
+                                    static_cast<size_t>(src_pitch), static_cast<size_t>(row_bytes),
+                                    static_cast<size_t>(rows), cudaMemcpyDeviceToHost,
+                                    reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("cudaMemcpy2DAsync failed: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return CB_OK;
+}

@@ -46,7 +46,7 @@ def _pages(rng, device, layout):
     return layers, planes
 
 
-def _worker(device, max_bytes, kv_caches):
+def _worker(device, max_bytes, kv_caches, arena=False):
     connector = object.__new__(connector_module.CacheBlendConnectorV1)
     connector.config = CacheBlendConfig.from_extra_config(
         {"chunk_size": CHUNK, "strict_version_check": False, "local_cpu_gb": max_bytes / (1 << 30)}
@@ -60,6 +60,8 @@ def _worker(device, max_bytes, kv_caches):
     connector._kv_caches = kv_caches
     connector._layer_ids = {f"model.layers.{i}.self_attn.attn": i for i in range(LAYERS)}
     connector._store = LocalPinnedCPUStore(CHUNK, max_bytes)
+    if arena:  # as register_kv_caches does: one pinned arena sized by local_cpu_gb
+        connector._store.attach_arena(connector._make_arena())
     connector._pipeline = StorePipeline(connector._store, BS, CHUNK, device=device)
     return connector
 
@@ -74,11 +76,12 @@ def _save(connector, request_id, tokens, slots, save_end):
     connector.wait_for_save()
 
 
+@pytest.mark.parametrize("arena", [False, True])
 @pytest.mark.parametrize("layout", ["flash_attn", "flashinfer", "separate"])
-def test_saved_chunks_match_oracle_gather(cuda, layout):
+def test_saved_chunks_match_oracle_gather(cuda, layout, arena):
     rng = np.random.default_rng(11)
     kv_caches, planes = _pages(rng, cuda, layout)
-    connector = _worker(cuda, 1 << 30, kv_caches)
+    connector = _worker(cuda, 1 << 30, kv_caches, arena)
     tokens = rng.integers(0, 150_000, size=3 * CHUNK + 37).tolist()
     blocks = rng.permutation(POOL)[: (len(tokens) + BS - 1) // BS]
     slots = connector_module._slot_mapping(blocks.tolist(), BS, len(tokens))
@@ -103,11 +106,12 @@ def test_saved_chunks_match_oracle_gather(cuda, layout):
         connector.close()
 
 
-def test_store_capacity_fails_closed(cuda):
+@pytest.mark.parametrize("arena", [False, True])
+def test_store_capacity_fails_closed(cuda, arena):
     rng = np.random.default_rng(12)
     kv_caches, planes = _pages(rng, cuda, "flash_attn")
     chunk_bytes = 2 * CHUNK * HEADS * HD * 2
-    connector = _worker(cuda, 2 * LAYERS * chunk_bytes, kv_caches)  # room for two chunks
+    connector = _worker(cuda, 2 * LAYERS * chunk_bytes, kv_caches, arena)  # room for two chunks
     tokens = rng.integers(0, 150_000, size=3 * CHUNK).tolist()
     blocks = rng.permutation(POOL)[: 3 * CHUNK // BS]
     slots = connector_module._slot_mapping(blocks.tolist(), BS, len(tokens))
@@ -116,6 +120,8 @@ def test_store_capacity_fails_closed(cuda):
         store = connector._store
         assert store.current_bytes <= 2 * LAYERS * chunk_bytes
         assert store.committed_entries == 2
+        if arena:
+            assert store.arena.pinned_bytes <= 2 * LAYERS * chunk_bytes
         segments = store.match("model", tokens, 0)
         store.pin("check", segments)
         for seg in segments:
@@ -178,3 +184,54 @@ def test_saved_chunks_reload_at_new_positions(cuda):
     finally:
         registry.unregister_store("store-test", 0)
         connector.close()
+
+
+def test_arena_fragmented_slots_match_oracle(cuda):
+    """Eviction leaves the arena's free slots scattered: a later batch lands in
+    runs of consecutive slots (one strided copy each) and single slots, and every
+    published chunk still equals the oracle's gather; pinned memory never grows."""
+    rng = np.random.default_rng(21)
+    kv_caches, planes = _pages(rng, cuda, "flash_attn")
+    chunk_bytes = 2 * CHUNK * HEADS * HD * 2
+    connector = _worker(cuda, 6 * LAYERS * chunk_bytes, kv_caches, arena=True)  # six entries
+    store = connector._store
+    try:
+        requests = {}
+        for name in ("a", "b", "c"):
+            tokens = rng.integers(0, 150_000, size=3 * CHUNK).tolist()
+            blocks = rng.permutation(POOL)[: 3 * CHUNK // BS]
+            slots = connector_module._slot_mapping(blocks.tolist(), BS, len(tokens))
+            requests[name] = (tokens, slots)
+            if name == "c":
+                # keep a's middle chunk and b's last chunk pinned: c must take slots
+                # 0, 2 and 3 (a's first and last, b's first) around them
+                seg_a = store.match("model", requests["a"][0], 0)
+                seg_b = store.match("model", requests["b"][0], 0)
+                store.pin("keep", (seg_a[1], seg_b[2]))
+            _save(connector, name, tokens, slots, len(tokens))
+        assert store.arena.used_slots == 6 and store.arena.pinned_bytes == 6 * LAYERS * chunk_bytes
+        slot_of = {sid: entry.slot for sid, entry in store._entries.items()}
+        tokens, slots = requests["c"]
+        segments = store.match("model", tokens, 0)
+        assert len(segments) == 3
+        assert sorted(slot_of[seg.segment_id] for seg in segments) == [0, 2, 3]
+        store.pin("check", segments)
+        for seg in segments:
+            chunk_slots = slots[seg.target_start : seg.target_start + CHUNK].numpy()
+            for layer in range(LAYERS):
+                want = oracle.paged_gather(planes[layer][0], planes[layer][1], chunk_slots, BS)
+                assert np.array_equal(_bits(store.get_layer("check", seg, layer)), want)
+        # the pinned survivors are intact too
+        for name, index in (("a", 1), ("b", 2)):
+            tok, sl = requests[name]
+            seg = store.match("model", tok, 0)
+            assert len(seg) >= 1
+            seg = [x for x in seg if x.target_start == index * CHUNK][0]
+            store.pin("old", [seg])
+            chunk_slots = sl[seg.target_start : seg.target_start + CHUNK].numpy()
+            for layer in range(LAYERS):
+                want = oracle.paged_gather(planes[layer][0], planes[layer][1], chunk_slots, BS)
+                assert np.array_equal(_bits(store.get_layer("old", seg, layer)), want)
+    finally:
+        connector.close()
+
