@@ -1,0 +1,179 @@
+"""The layerwise side executor (Qwen3BlendExecutor._compute_layer,
+cacheblend_vllm/ascend.py:487-630) driven with small stand-in Qwen3 layers on
+the GPU: a plain layer and a kv_deviation check layer.  The executor's seams
+(K-deviation score, select, staging write-back, attention over the staging)
+run on the sm_100a kernels; the expectation restates the reference's layer in
+torch with the oracle's deviation and select and the reference's attention
+formula.  Selected indices and the staging bytes must match exactly; hidden
+states within the attention tolerance (bf16 products downstream)."""
+
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from cacheblend_b200.config import CacheBlendConfig
+from cacheblend_b200.executor import BlendExecutionState, Qwen3BlendExecutor
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN, HQ, HKV, HD, INTER = 256, 4, 2, 128, 384
+
+
+class _Norm:
+    """vLLM RMSNorm calling convention: norm(x) or norm(x, residual) -> (norm(x + r), x + r)."""
+
+    def __init__(self, dim, gen, device):
+        self.w = (1.0 + 0.1 * torch.randn(dim, generator=gen)).to(device)
+
+    def _apply(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * self.w).to(x.dtype)
+
+    def __call__(self, x, residual=None):
+        if residual is None:
+            return self._apply(x)
+        s = x + residual
+        return self._apply(s), s
+
+
+class _Linear:
+    def __init__(self, out_dim, in_dim, gen, device):
+        self.w = (torch.randn(out_dim, in_dim, generator=gen) * in_dim ** -0.5).to(torch.bfloat16).to(device)
+
+    def __call__(self, x):
+        return x @ self.w.t(), None
+
+
+class _Mlp:
+    def __init__(self, gen, device):
+        self.up = _Linear(INTER, HIDDEN, gen, device)
+        self.down = _Linear(HIDDEN, INTER, gen, device)
+
+    def __call__(self, x):
+        return self.down(torch.nn.functional.silu(self.up(x)[0]))[0]
+
+
+class _Rope:
+    """NeoX rotary over the full head with vLLM's cos_sin_cache layout."""
+
+    def __init__(self, max_pos, device):
+        inv = 1.0 / (1e6 ** (torch.arange(0, HD, 2, dtype=torch.float32) / HD))
+        freqs = torch.arange(max_pos, dtype=torch.float32)[:, None] * inv[None, :]
+        self.cos_sin_cache = torch.cat((freqs.cos(), freqs.sin()), dim=-1).to(device)
+        self.head_size, self.rotary_dim, self.is_neox_style = HD, HD, True
+
+    def _rotate(self, x, positions):
+        shape = x.shape
+        x = x.view(x.shape[0], -1, HD).float()
+        cos, sin = self.cos_sin_cache[positions].chunk(2, dim=-1)
+        cos, sin = cos[:, None, :], sin[:, None, :]
+        x1, x2 = x[..., : HD // 2], x[..., HD // 2 :]
+        out = torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1)
+        return out.to(torch.bfloat16).reshape(shape)
+
+    def __call__(self, positions, q, k):
+        return self._rotate(q, positions), self._rotate(k, positions)
+
+
+def _layer(gen, device, max_pos):
+    attn = SimpleNamespace(num_heads=HQ, num_kv_heads=HKV, head_size=HD,
+                           impl=SimpleNamespace(scale=HD ** -0.5))
+    self_attn = SimpleNamespace(
+        qkv_proj=_Linear((HQ + 2 * HKV) * HD, HIDDEN, gen, device), q_size=HQ * HD, kv_size=HKV * HD,
+        head_dim=HD, q_norm=_Norm(HD, gen, device), k_norm=_Norm(HD, gen, device),
+        rotary_emb=_Rope(max_pos, device), attn=attn, o_proj=_Linear(HIDDEN, HQ * HD, gen, device))
+    return SimpleNamespace(input_layernorm=_Norm(HIDDEN, gen, device), self_attn=self_attn,
+                           post_attention_layernorm=_Norm(HIDDEN, gen, device), mlp=_Mlp(gen, device))
+
+
+def _reference_attention(query, key, value, positions, scale):
+    groups = HQ // HKV
+    masked = positions[:, None] < torch.arange(key.shape[0], device=query.device)[None, :]
+    out = torch.empty_like(query)
+    for h in range(HKV):
+        q = query[:, h * groups:(h + 1) * groups]
+        w = torch.einsum("qgd,kd->gqk", q, key[:, h]) * scale
+        w = w.masked_fill(masked[None], torch.finfo(w.dtype).min)
+        p = torch.softmax(w.float(), dim=-1).to(query.dtype)
+        out[:, h * groups:(h + 1) * groups] = torch.einsum("gqk,kd->qgd", p, value[:, h])
+    return out
+
+
+def _reference_layer(layer, hidden, residual, positions, old_kv, compute_start, gap_mask, check, ratio):
+    """ascend.py:487-630 for one layer, kv_deviation strategy, in torch + oracle."""
+    sa = layer.self_attn
+    if residual is None:
+        residual = hidden
+        hidden = layer.input_layernorm(hidden)
+    else:
+        hidden, residual = layer.input_layernorm(hidden, residual)
+    qkv, _ = sa.qkv_proj(hidden)
+    q, k, v = qkv.split([sa.q_size, sa.kv_size, sa.kv_size], dim=-1)
+    q = sa.q_norm(q.view(-1, HQ, HD)).view(q.shape)
+    k = sa.k_norm(k.view(-1, HKV, HD)).view(k.shape)
+    q, k = sa.rotary_emb(positions, q, k)
+    query_indices = torch.arange(q.shape[0], device=q.device)
+    absolute = compute_start + query_indices
+    flat_k = old_kv[0].reshape(old_kv.shape[1], -1)
+    flat_v = old_kv[1].reshape(old_kv.shape[1], -1)
+    selected = None
+    if check:
+        bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+        scores = oracle.kv_deviation(bits(k), bits(flat_k), oracle.BF16, absolute.cpu().numpy())
+        gaps = gap_mask[absolute.cpu().numpy()]
+        selected = torch.from_numpy(oracle.select(scores, gaps, ratio)).to(q.device)
+        q, k, v, residual = q[selected], k[selected], v[selected], residual[selected]
+        absolute = compute_start + selected
+        positions = positions[selected]
+    flat_k[absolute] = k
+    flat_v[absolute] = v
+    out = _reference_attention(q.view(-1, HQ, HD), old_kv[0].view(-1, HKV, HD), old_kv[1].view(-1, HKV, HD),
+                               absolute, sa.attn.impl.scale).reshape(-1, HQ * HD)
+    hidden, _ = sa.o_proj(out)
+    hidden, residual = layer.post_attention_layernorm(hidden, residual)
+    return layer.mlp(hidden), residual, positions, selected
+
+
+def test_executor_layers_match_reference(cuda):
+    gen = torch.Generator().manual_seed(8)
+    ctx, compute_start = 520, 40  # staging rows [0, 520), tokens computed from position 40
+    n = ctx - compute_start
+    layers = [_layer(gen, cuda, ctx), _layer(gen, cuda, ctx)]
+    executor = object.__new__(Qwen3BlendExecutor)
+    executor.config = CacheBlendConfig.from_extra_config(
+        {"check_layers": [1], "recompute_ratios": [0.15], "selection_strategy": "kv_deviation",
+         "strict_version_check": False})
+    executor.block_size = 16
+    executor.tp_group = None
+    executor.layers = layers
+    gap_mask = np.zeros(ctx, dtype=bool)
+    gap_mask[200:260] = True
+    gap_mask[ctx - 1] = True
+    hidden = (torch.randn(n, HIDDEN, generator=gen) * 0.5).to(torch.bfloat16).to(cuda)
+    staging = [(torch.randn(2, ctx, HKV, HD, generator=gen)).to(torch.bfloat16).to(cuda) for _ in layers]
+    ref_staging = [s.clone() for s in staging]
+
+    state = BlendExecutionState(compute_start, torch.arange(compute_start, ctx, device=cuda), gap_mask)
+    h, r = hidden, None
+    ref_h, ref_r, ref_pos = hidden, None, torch.arange(compute_start, ctx, device=cuda)
+    for layer_id, layer in enumerate(layers):
+        h, r, state, staging[layer_id] = executor._compute_layer(layer_id, layer, h, r, state, staging[layer_id])
+        ref_h, ref_r, ref_pos, selected = _reference_layer(
+            layer, ref_h, ref_r, ref_pos, ref_staging[layer_id], compute_start, gap_mask,
+            check=layer_id == 1, ratio=0.15)
+        if selected is not None:
+            assert torch.equal(state.important_indices, selected)
+            assert torch.equal(state.positions, ref_pos)
+        # staging after the write-back: fresh K/V rows of the computed tokens (bit-exact)
+        assert torch.equal(staging[layer_id], ref_staging[layer_id]), layer_id
+        diff = (h.float() - ref_h.float()).abs()
+        assert float(diff.max()) <= 5e-2 + 5e-2 * float(ref_h.float().abs().max()), layer_id
+        assert float(diff.mean()) <= 5e-3, layer_id
+        # continue both from the same values so the next layer compares like with like
+        ref_h, ref_r = h, r
+    assert h.shape[0] == state.important_indices.numel()
