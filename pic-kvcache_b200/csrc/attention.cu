@@ -131,23 +131,15 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return r;
 }
 
-// Pairs of fp32 values rounded to T and widened back, on the FMA pipe instead
-// of the conversion unit (which shares its issue rate with exp2).
-// bf16: Veltkamp splitting at 16 bits, c = y (2^16 + 1), hi = c - (c - y),
-// leaves the upper 8 significant bits of y rounded to nearest even: equal to
-// the conversion for every fp32 value with 2^-126 <= |y| < 2^110 (checked
-// exhaustively); below that only subnormals differ, by less than 2^-126.
-// fp16 keeps the conversion instructions (its narrower exponent range makes
-// the rounding point depend on the magnitude).
+// Pairs of fp32 values rounded to T and widened back.  bf16: on the FMA pipe
+// (bf16_round_pair), keeping the conversion unit for exp2.  fp16 keeps the
+// conversion instructions (its narrower exponent range makes the rounding point
+// depend on the magnitude).
 template <typename T>
 struct RoundPair;
 template <>
 struct RoundPair<__nv_bfloat16> {
-  static __device__ __forceinline__ float2 apply(float2 y) {
-    const float2 c = __fmul2_rn(y, make_float2(65537.0f, 65537.0f));
-    const float2 d = __ffma2_rn(y, make_float2(-1.0f, -1.0f), c);
-    return __ffma2_rn(d, make_float2(-1.0f, -1.0f), c);
-  }
+  static __device__ __forceinline__ float2 apply(float2 y) { return bf16_round_pair(y); }
 };
 template <>
 struct RoundPair<__half> {
