@@ -173,3 +173,44 @@ def test_attention_rejects_unsupported(cuda):
     q = torch.zeros(4, 8, 128, dtype=torch.float32, device=cuda)
     with pytest.raises(NotImplementedError):
         blend_attention(q, q, q, torch.arange(4, device=cuda), 1.0)
+
+
+@pytest.mark.parametrize(
+    "nq,nk,hq,hkv,positions",
+    [
+        (1, 1, 8, 8, "zero"),        # a single key
+        (40, 300, 16, 4, "zero"),    # every query at position 0: one key each
+        (64, 640, 32, 1, "dup"),     # 32 query heads on one KV head; repeated positions
+        (97, 127, 8, 2, "last"),     # keys one short of a tile
+        (97, 128, 8, 2, "last"),     # keys exactly one tile
+        (300, 256, 8, 8, "dup"),     # groups 1, 300 rows: pairs of 128-row tiles, padding
+    ],
+)
+def test_attention_edge_shapes(cuda, nq, nk, hq, hkv, positions):
+    gen = torch.Generator(device=cuda).manual_seed(nq + nk)
+    if positions == "zero":
+        pos = torch.zeros(nq, dtype=torch.long, device=cuda)
+    elif positions == "last":
+        pos = torch.full((nq,), nk - 1, dtype=torch.long, device=cuda)
+    else:
+        pos = torch.randint(0, nk, (nq,), generator=gen, device=cuda).sort().values
+    query = torch.randn(nq, hq, 128, generator=gen, device=cuda).to(torch.bfloat16)
+    key = torch.randn(nk, hkv, 128, generator=gen, device=cuda).to(torch.bfloat16)
+    value = torch.randn(nk, hkv, 128, generator=gen, device=cuda).to(torch.bfloat16)
+    error = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = blend_attention(query, key, value, pos, 128 ** -0.5, device_error=error)
+    torch.cuda.synchronize()
+    assert int(error.item()) == 0
+    want = reference_attention(query, key, value, pos, 128 ** -0.5)
+    _check(got, want)
+    if positions == "zero":  # one visible key: the output is that key's value row
+        assert torch.equal(got, value[0][None].repeat_interleave(hq // hkv, dim=1).expand_as(got))
+
+
+def test_attention_rejects_misaligned_rows(cuda):
+    base = torch.zeros(8 * 129 * 128 + 8, dtype=torch.bfloat16, device=cuda)
+    # rows 129 heads apart would be fine; an odd element offset breaks 16-byte alignment
+    key = base[1 : 1 + 8 * 2 * 128].view(8, 2, 128)
+    query = torch.zeros(4, 2, 128, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(NotImplementedError):
+        blend_attention(query, key, key, torch.arange(4, device=cuda), 1.0)
