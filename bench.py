@@ -821,6 +821,23 @@ def attention_bench(args, world: int, rank: int, local: int) -> None:
         torch.cuda.synchronize(device)
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    # the fused-logit mode (fp32 logits, the reference's fused NPU kernel semantics), same steps
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            blend_attention(query, key, value, pos, scale, workspace=workspace, device_error=error,
+                            stream=stream, exact_rounding=False)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for _ in range(args.steps):
+            blend_attention(query, key, value, pos, scale, workspace=workspace, device_error=error,
+                            stream=stream, exact_rounding=False)
+        f1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    fused_ms = max_over_ranks(f0.elapsed_time(f1), world, device) / args.steps
     flops = attention_flops(positions, hq)
     # context: torch SDPA with the boolean causal-by-position mask (the generic path)
     allowed = pos[:, None] >= torch.arange(key.shape[0], device=device)[None, :]
@@ -860,7 +877,12 @@ def attention_bench(args, world: int, rank: int, local: int) -> None:
                          if not ATTENTION_KEYS else None,
                          "flops_note": "causal algorithmic: 4 x 128 x q_heads x sum(position + 1); "
                                        "timed over the whole step (query prep, attention)"},
-            "context": {"torch_sdpa_masked_ms": sdpa_ms},
+            "context": {"torch_sdpa_masked_ms": sdpa_ms,
+                        "fused_logits": {"ms_per_step": fused_ms,
+                                         "tflops": flops / (fused_ms / 1e3) / 1e12,
+                                         "frac": flops / (fused_ms / 1e3) / 1e12 / peak,
+                                         "note": "fp32 logits (the reference's fused NPU attention); "
+                                                 "value above keeps the einsum path's bf16 roundings"}},
             "device_error": int(error.item()), "clocks": clocks.summary(), "cpu_baseline": cpu,
         }), flush=True)
 

@@ -236,6 +236,8 @@ CB_API int cb_blend_attention_workspace_size(int64_t num_queries, int64_t num_ke
  * query head h attends KV head h / (num_q_heads / num_kv_heads):
  *   w = T(T(q . k) * scale), p = softmax over keys k <= pos of w (fp32),
  *   out = T(sum_k p v).
+ * exact_rounding = 0 computes w = (q . k) * scale in fp32 instead (the
+ * reference's fused attention kernel, ascend.py:814-830); it needs scale > 0.
  * Strides in bytes, rows and heads 16-byte aligned, heads contiguous within a
  * row.  On the tensor cores: QK^T and PV with tcgen05.mma, accumulators in
  * TMEM, operands staged by TMA; device_error (optional) receives a code if a
@@ -246,8 +248,9 @@ CB_API int cb_blend_attention(const void* query, int64_t query_token_stride, con
                               int64_t value_token_stride, int64_t num_keys, int64_t num_q_heads,
                               int64_t num_kv_heads, int64_t head_size, int dtype,
                               const int64_t* query_positions, int64_t num_queries, float scale,
-                              void* out, int64_t out_token_stride, void* workspace,
-                              int64_t workspace_bytes, int32_t* device_error, void* stream);
+                              int exact_rounding, void* out, int64_t out_token_stride,
+                              void* workspace, int64_t workspace_bytes, int32_t* device_error,
+                              void* stream);
 
 /*
  * Workspace bytes cb_sparse_q_scores needs for `num_queries` sparse queries

@@ -102,7 +102,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "cb_blend_attention": (
         _i32,
         [_ptr, _i64, _ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _i64,
-         ctypes.c_float, _ptr, _i64, _ptr, _i64, _ptr, _ptr],
+         ctypes.c_float, _i32, _ptr, _i64, _ptr, _i64, _ptr, _ptr],
     ),
     "cb_sparse_q_workspace_size": (_i32, [_i64, _i64, _i64, _i64, _i32, _ptr]),
     "cb_sparse_q_scores": (

@@ -44,9 +44,14 @@ def blend_attention(
     workspace: torch.Tensor | None = None,
     device_error: torch.Tensor | None = None,
     stream: torch.cuda.Stream | None = None,
+    exact_rounding: bool = True,
 ) -> torch.Tensor:
     """out [Nq, Hq, D] for query [Nq, Hq, D] at ``query_positions`` (each in [0, Nk)),
-    key / value [Nk, Hkv, D] (rows = positions)."""
+    key / value [Nk, Hkv, D] (rows = positions).
+
+    ``exact_rounding`` keeps the einsum path's roundings (element-type logits, element-type
+    logit * scale); False computes fp32 logits * scale like the reference's fused attention
+    kernel (ascend.py:814-830) and flash attention, about a third faster."""
     _native.require_cuda(query, key, value)
     if query.ndim != 3 or key.ndim != 3 or value.shape != key.shape:
         raise ValueError("query must be [tokens, q_heads, head]; key and value [keys, kv_heads, head]")
@@ -72,7 +77,8 @@ def blend_attention(
         "cb_blend_attention", query.data_ptr(), query.stride(0) * esize, key.data_ptr(),
         key.stride(0) * esize, value.data_ptr(), value.stride(0) * esize, num_keys, num_q_heads,
         num_kv_heads, head_size, _native.dtype_code(query.dtype), positions.data_ptr(), num_queries,
-        float(scale), out.data_ptr(), out.stride(0) * esize, workspace.data_ptr(), workspace.numel(),
+        float(scale), int(bool(exact_rounding)), out.data_ptr(), out.stride(0) * esize,
+        workspace.data_ptr(), workspace.numel(),
         0 if device_error is None else device_error.data_ptr(), _native.stream_handle(stream),
     )
     return out

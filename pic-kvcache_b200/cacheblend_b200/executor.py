@@ -17,6 +17,8 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+import os
+
 from .attention import attention_supported, attention_workspace_bytes, blend_attention
 from .config import CacheBlendConfig
 from .loader import PagedBlendLoader
@@ -24,6 +26,12 @@ from .rope import validate_rope_support
 from .selection import kv_deviation, select_tokens, selection_overlap, sparse_q_scores
 from .trace import PipelineTracer
 from .types import BlendPlan
+
+
+# CACHEBLEND_B200_ATTENTION=fused: fp32 logits like the reference's fused NPU attention
+# (ascend.py:814-830) instead of the einsum path's element-type roundings (the default,
+# which is what the reference runs on a CUDA device).
+_FUSED_ATTENTION = os.environ.get("CACHEBLEND_B200_ATTENTION", "").lower() == "fused"
 
 
 def _embed(model, input_ids: torch.Tensor) -> torch.Tensor:
@@ -225,7 +233,8 @@ class Qwen3BlendExecutor:
             if workspace is None or workspace.numel() < need or workspace.device != query.device:
                 workspace = torch.empty(need, dtype=torch.uint8, device=query.device)
                 self._attention_workspace = workspace
-            return blend_attention(query, key, value, q_positions, scale, workspace=workspace)
+            return blend_attention(query, key, value, q_positions, scale, workspace=workspace,
+                                   exact_rounding=not _FUSED_ATTENTION or scale <= 0)
         k_positions = torch.arange(key.shape[0], device=query.device)
         cache = self.config.cache_attention_mask and state.important_indices is not None
         allowed = state.attention_mask if cache else None

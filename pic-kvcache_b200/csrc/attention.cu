@@ -154,7 +154,11 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
-template <typename T>
+// EXACT: the reference einsum path's roundings (T logits, T logit * scale);
+// otherwise fused semantics: fp32 logits times scale, as the reference's fused
+// attention kernel (npu_fused_infer_attention_score, ascend.py:814-830) and
+// flash attention compute them.
+template <typename T, bool EXACT>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap q_map,
                      const __grid_constant__ CUtensorMap k_map,
@@ -353,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.s_empty[x]);
-        // the reference's roundings: T logits, T (logit * scale); keys > pos masked
+        // EXACT: the reference's roundings, w = T(T(s) * scale); fused: w = s (the
+        // scale is folded into the exp2 argument below); keys > pos masked
         const int valid = min(max(pos - kt * kTile + 1, 0), kTile);
         float2 w[64];
         const float2 sc2 = make_float2(c.scale, c.scale);
@@ -361,7 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 64; ++j) {
           const float2 sv = make_float2(__uint_as_float(v[j >> 4][(2 * j) & 31]),
                                         __uint_as_float(v[j >> 4][(2 * j + 1) & 31]));
-          w[j] = RoundPair<T>::apply(__fmul2_rn(RoundPair<T>::apply(sv), sc2));
+          if constexpr (EXACT)
+            w[j] = RoundPair<T>::apply(__fmul2_rn(RoundPair<T>::apply(sv), sc2));
+          else
+            w[j] = sv;
         }
         if (valid < kTile) {  // this row's position ends inside the tile
 #pragma unroll
@@ -375,8 +383,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
 #pragma unroll
         for (int j = 0; j < 64; ++j) mx[j & 3] = max3(mx[j & 3], w[j].x, w[j].y);
-        // log2-domain tile max (rounding is monotonic: max(w) * log2e = max(w * log2e))
-        const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * kLog2e;
+        // log2-domain tile max: w times a positive multiplier (log2e, or scale * log2e
+        // when the scale is folded in), and rounding is monotonic, so max(w) * mul =
+        // max(w * mul)
+        const float mul = EXACT ? kLog2e : c.scale * kLog2e;
+        const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * mul;
         const bool grow = tile_max > m_used + kRescaleLog2 || (m_used == -INFINITY && tile_max > -INFINITY);
         // the P buffer is free and O settled once the previous tile's P V is done
         if (kt > 0 && !wait_warp(&sh.pv_done[x], (t - 1) & 1)) { ok = false; break; }
@@ -399,10 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           l *= corr;
           m_used = m_new;
         }
-        // p = 2^(w log2e - m_used) rounded to T into the SW128 P tile; the sum in fp32
+        // p = 2^(w mul - m_used) rounded to T into the SW128 P tile; the sum in fp32
         // (a padding row keeps m_used = -inf: its p are exact zeros)
         const float base_m = m_used == -INFINITY ? 0.0f : m_used;
-        const float2 l2e = make_float2(kLog2e, kLog2e);
+        const float2 l2e = make_float2(mul, mul);
         const float2 nm = make_float2(-base_m, -base_m);
         float2 sm[4];
 #pragma unroll
@@ -577,8 +588,9 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
                                   int64_t value_token_stride, int64_t num_keys, int64_t num_q_heads,
                                   int64_t num_kv_heads, int64_t head_size, int dtype,
                                   const int64_t* query_positions, int64_t num_queries, float scale,
-                                  void* out, int64_t out_token_stride, void* workspace,
-                                  int64_t workspace_bytes, int32_t* device_error, void* stream) {
+                                  int exact_rounding, void* out, int64_t out_token_stride,
+                                  void* workspace, int64_t workspace_bytes, int32_t* device_error,
+                                  void* stream) {
   CB_BIND(stream, out);
   int rc = att::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
   if (rc != CB_OK) return rc;
@@ -637,8 +649,13 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
   c.out_token_stride = out_token_stride;
   c.error = device_error;
   const int grid = static_cast<int>(std::min<int64_t>(num_kv_heads * c.q_pairs, kSmCount));
-  auto kernel = dtype == CB_DTYPE_BF16 ? att::attention_kernel<__nv_bfloat16>
-                                       : att::attention_kernel<__half>;
+  CB_REQUIRE(exact_rounding || scale > 0.0f,
+             "the fused-logit mode needs a positive scale (got %g)", static_cast<double>(scale));
+  auto kernel = dtype == CB_DTYPE_BF16
+                    ? (exact_rounding ? att::attention_kernel<__nv_bfloat16, true>
+                                      : att::attention_kernel<__nv_bfloat16, false>)
+                    : (exact_rounding ? att::attention_kernel<__half, true>
+                                      : att::attention_kernel<__half, false>);
   rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), att::kDynSmem);
   if (rc != CB_OK) return rc;
   kernel<<<grid, att::kThreads, att::kDynSmem, s>>>(q_map, k_map, v_map, c);

@@ -214,3 +214,38 @@ def test_attention_rejects_misaligned_rows(cuda):
     query = torch.zeros(4, 2, 128, dtype=torch.bfloat16, device=cuda)
     with pytest.raises(NotImplementedError):
         blend_attention(query, key, key, torch.arange(4, device=cuda), 1.0)
+
+
+def fused_reference(query, key, value, positions, scale):
+    """The reference's fused-kernel semantics (ascend.py:814-830): fp32 logits times
+    the scale, fp32 softmax over keys <= position, output in the element type."""
+    groups = query.shape[1] // key.shape[1]
+    masked = positions[:, None] < torch.arange(key.shape[0], device=query.device)[None, :]
+    out = torch.empty_like(query)
+    for h in range(key.shape[1]):
+        q = query[:, h * groups:(h + 1) * groups].float()
+        w = torch.einsum("qgd,kd->gqk", q, key[:, h].float()) * scale
+        w = w.masked_fill(masked[None], float("-inf"))
+        p = torch.softmax(w, dim=-1)
+        out[:, h * groups:(h + 1) * groups] = torch.einsum("gqk,kd->qgd", p, value[:, h].float()).to(query.dtype)
+    return out
+
+
+@pytest.mark.parametrize("nq,nk,hq,hkv,dtype", [(300, 1000, 32, 8, torch.bfloat16), (77, 77, 8, 8, torch.float16),
+                                                (1229, 8192, 32, 8, torch.bfloat16)])
+def test_attention_fused_logits(cuda, nq, nk, hq, hkv, dtype):
+    query, key, value, positions = _inputs(cuda, nq, nk, hq, hkv, dtype, nq + 3 * nk)
+    error = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = blend_attention(query, key, value, positions, 128 ** -0.5, device_error=error, exact_rounding=False)
+    torch.cuda.synchronize()
+    assert int(error.item()) == 0
+    _check(got, fused_reference(query, key, value, positions, 128 ** -0.5))
+    # the two modes differ only by the logit roundings: within the same tolerance of each other
+    _check(got, blend_attention(query, key, value, positions, 128 ** -0.5))
+
+
+def test_attention_fused_logits_rejects_nonpositive_scale(cuda):
+    q = torch.zeros(4, 8, 128, dtype=torch.bfloat16, device=cuda)
+    k = torch.zeros(4, 8, 128, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError):
+        blend_attention(q, k, k, torch.arange(4, device=cuda), -1.0, exact_rounding=False)
