@@ -1,11 +1,13 @@
 """The layerwise side executor (Qwen3BlendExecutor._compute_layer,
 cacheblend_vllm/ascend.py:487-630) driven with small stand-in Qwen3 layers on
-the GPU: a plain layer and a kv_deviation check layer.  The executor's seams
-(K-deviation score, select, staging write-back, attention over the staging)
-run on the sm_100a kernels; the expectation restates the reference's layer in
-torch with the oracle's deviation and select and the reference's attention
-formula.  Selected indices and the staging bytes must match exactly; hidden
-states within the attention tolerance (bf16 products downstream)."""
+the GPU: a plain layer and a check layer under each selection strategy
+(kv_deviation, sparse_q, compare).  The executor's seams (K-deviation score,
+Sparse-Q score, select, staging write-back, attention over the staging) run on
+the sm_100a kernels; the expectation restates the reference's layer in torch
+with the oracle's deviation, Sparse-Q and select and the reference's attention
+formula.  Selected indices and the staging bytes must match exactly (Sparse-Q:
+except ties within its 1e-3 tolerance); hidden states within the attention
+tolerance (bf16 products downstream)."""
 
 from __future__ import annotations
 
@@ -177,3 +179,111 @@ def test_executor_layers_match_reference(cuda):
         # continue both from the same values so the next layer compares like with like
         ref_h, ref_r = h, r
     assert h.shape[0] == state.important_indices.numel()
+
+
+class _Tracer:
+    enabled = True
+
+    def __init__(self):
+        self.events = []
+
+    def emit(self, name, **fields):
+        self.events.append((name, fields))
+
+
+def _executor(layers, strategy):
+    executor = object.__new__(Qwen3BlendExecutor)
+    executor.config = CacheBlendConfig.from_extra_config(
+        {"check_layers": [1], "recompute_ratios": [0.15], "selection_strategy": strategy,
+         "strict_version_check": False})
+    executor.block_size = 16
+    executor.tp_group = None
+    executor.layers = layers
+    return executor
+
+
+def _close_selection(got, want, scores, gaps, forced, ratio=0.15):
+    """Index sets equal, or differing only at scores tied with the threshold within 1e-3."""
+    if np.array_equal(got, want):
+        return
+    diff = np.setxor1d(got, want)
+    base = gaps | forced
+    candidates = np.flatnonzero(~base)
+    k = len(want) - int(base.sum())
+    threshold = np.sort(scores[candidates])[::-1][k - 1]
+    assert np.all(np.abs(scores[diff] - threshold) <= 1e-3 * abs(threshold)), diff
+
+
+@pytest.mark.parametrize("strategy", ["sparse_q", "compare"])
+def test_executor_query_aware_strategies(cuda, strategy):
+    """sparse_q: score the check layer's queries against the staged keys (fresh
+    keys written in place) on the tensor cores, attend with every row, prune
+    after the MLP; compare: prune by K-deviation exactly as kv_deviation does
+    and report the overlap of the two selections (ascend.py:545-630)."""
+    gen = torch.Generator().manual_seed(9)
+    ctx, compute_start = 700, 60
+    n = ctx - compute_start
+    layers = [_layer(gen, cuda, ctx), _layer(gen, cuda, ctx)]
+    gap_mask = np.zeros(ctx, dtype=bool)
+    gap_mask[300:380] = True
+    gap_mask[ctx - 1] = True
+    hidden = (torch.randn(n, HIDDEN, generator=gen) * 0.5).to(torch.bfloat16).to(cuda)
+    staging0 = [torch.randn(2, ctx, HKV, HD, generator=gen).to(torch.bfloat16).to(cuda) for _ in layers]
+
+    def run(strategy_name, tracer=None):
+        executor = _executor(layers, strategy_name)
+        staging = [s.clone() for s in staging0]
+        state = BlendExecutionState(compute_start, torch.arange(compute_start, ctx, device=cuda), gap_mask)
+        h, r = hidden, None
+        for layer_id, layer in enumerate(layers):
+            h, r, state, staging[layer_id] = executor._compute_layer(
+                layer_id, layer, h, r, state, staging[layer_id], request_id="req", tracer=tracer)
+        return h, r, state, staging
+
+    if strategy == "sparse_q":
+        h, r, state, staging = run("sparse_q")
+        # expectation: layer 0 as before, then layer 1 with every row and oracle Sparse-Q
+        executor = _executor(layers, "kv_deviation")
+        ref_staging = [s.clone() for s in staging0]
+        ref_state = BlendExecutionState(compute_start, torch.arange(compute_start, ctx, device=cuda), gap_mask)
+        h0, r0, ref_state, ref_staging[0] = executor._compute_layer(0, layers[0], hidden, None, ref_state,
+                                                                    ref_staging[0])
+        assert torch.equal(staging[0], ref_staging[0])
+        sa = layers[1].self_attn
+        hh, rr = layers[1].input_layernorm(h0, r0)
+        qkv, _ = sa.qkv_proj(hh)
+        q, k, v = qkv.split([sa.q_size, sa.kv_size, sa.kv_size], dim=-1)
+        q = sa.q_norm(q.view(-1, HQ, HD)).view(q.shape)
+        k = sa.k_norm(k.view(-1, HKV, HD)).view(k.shape)
+        positions = torch.arange(compute_start, ctx, device=cuda)
+        q, k = sa.rotary_emb(positions, q, k)
+        absolute = np.arange(compute_start, ctx)
+        score_keys = ref_staging[1][0].reshape(ctx, -1).clone()
+        score_keys[torch.from_numpy(absolute).to(cuda)] = k
+        gaps = gap_mask[absolute]
+        cfg = executor.config
+        want_scores, want_forced, _ = oracle.sparse_q_scores(
+            q.view(-1, HQ, HD).float().cpu().numpy(), score_keys.view(ctx, HKV, HD).float().cpu().numpy(),
+            absolute, gaps, HD ** -0.5, 16, cfg.overflow_blocks, cfg.tail_query_tokens)
+        want_sel = oracle.select(want_scores, gaps, 0.15, want_forced)
+        got_sel = state.important_indices.cpu().numpy()
+        _close_selection(got_sel, want_sel, want_scores, gaps, want_forced)
+        assert h.shape[0] == got_sel.size and r.shape[0] == got_sel.size
+        # the staging holds every row's fresh K / V (no pruning before attention)
+        flat_k = ref_staging[1][0].reshape(ctx, -1)
+        flat_k[torch.from_numpy(absolute).to(cuda)] = k
+        assert torch.equal(staging[1][0].reshape(ctx, -1), flat_k)
+    else:
+        tracer = _Tracer()
+        h, r, state, staging = run("compare", tracer)
+        h_dev, r_dev, state_dev, staging_dev = run("kv_deviation")
+        assert torch.equal(state.important_indices, state_dev.important_indices)
+        assert torch.equal(h, h_dev) and torch.equal(r, r_dev)
+        assert all(torch.equal(a, b) for a, b in zip(staging, staging_dev))
+        events = [f for name, f in tracer.events if name == "selection_compared"]
+        assert len(events) == 1
+        event = events[0]
+        assert event["deviation_tokens"] == state_dev.important_indices.numel()
+        sq_sel = run("sparse_q")[2].important_indices.cpu().numpy()
+        overlap = np.intersect1d(sq_sel, state_dev.important_indices.cpu().numpy()).size
+        assert event["overlap_tokens"] == overlap
