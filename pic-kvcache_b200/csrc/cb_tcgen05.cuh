@@ -260,18 +260,6 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
-// Two fp32 values rounded to bf16 (nearest even) and widened back, on the FMA
-// pipe: Veltkamp splitting at 16 bits, c = y (2^16 + 1), hi = c - (c - y)
-// keeps the upper 8 significant bits of y rounded to nearest even.  Equal to
-// the conversion instruction for every fp32 value with 2^-126 <= |y| < 2^110
-// (checked exhaustively); below that only subnormals differ, by less than
-// 2^-126.  The conversion unit is the one exp2 uses, so this keeps it for exp2.
-__device__ __forceinline__ float2 bf16_round_pair(float2 y) {
-  const float2 c = __fmul2_rn(y, make_float2(65537.0f, 65537.0f));
-  const float2 d = __ffma2_rn(y, make_float2(-1.0f, -1.0f), c);
-  return __ffma2_rn(d, make_float2(-1.0f, -1.0f), c);
-}
-
 // 32 lanes x 32 consecutive fp32 columns of this warp's TMEM sub-partition, stored.
 __device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&v)[32]) {
   asm volatile(

@@ -53,9 +53,8 @@ __device__ __forceinline__ float round_logit(uint32_t bits) {
 }
 
 // Rounds two fp32 accumulator values to the 16-bit matmul output type
-// (round to nearest even, one packed cvt) and widens them back.  (The FMA-pipe
-// rounding the attention kernel uses measured 2 % slower here: this kernel's
-// conversion unit has room next to its exp2.)
+// (round to nearest even, one packed cvt) and widens them back.  (The same
+// rounding done on the FMA pipe measured 2 % slower here.)
 template <typename T>
 __device__ __forceinline__ void round_pair(uint32_t lo_bits, uint32_t hi_bits, float& lo, float& hi);
 template <>
