@@ -107,6 +107,22 @@ CB_API int cb_copy_rows_d2h(void* dst, int64_t dst_pitch, const void* src, int64
                             int64_t row_bytes, int64_t rows, void* stream);
 
 /*
+ * Host function (no GPU): the 64-bit polynomial fingerprint of every full
+ * `window` of `tokens` (n - window + 1 values into `out`), identical to
+ * cacheblend_vllm/hashing.py:42-53 (rolling_hash_values) in O(n).
+ */
+CB_API int cb_window_hashes(const int64_t* tokens, int64_t n, int64_t window, uint64_t* out);
+
+/*
+ * Host function (no GPU): ascending offsets i < n with hashes[i] in `known`
+ * (ascending, distinct); at most `max_out` are written, *count receives the
+ * total.  The candidate scan of TokenRangeMatcher.match
+ * (cacheblend_vllm/matcher.py:80-125) before token verification.
+ */
+CB_API int cb_hash_candidates(const uint64_t* hashes, int64_t n, const uint64_t* known,
+                              int64_t num_known, int64_t* out, int64_t max_out, int64_t* count);
+
+/*
  * Number of common entries of two strictly ascending int64 index lists
  * (device memory), written to *count (device memory) on `stream`.  The
  * overlap of the two selections that the `compare` strategy reports

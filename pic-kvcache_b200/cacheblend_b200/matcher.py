@@ -3,12 +3,11 @@
 The fingerprint function is part of the store's wire contract: segment ids
 (and therefore cache hits across processes) depend on it.  It is the 64-bit
 polynomial hash of cacheblend_vllm/hashing.py:18-22 -- base 1,000,003 over
-``token + 1``, wrapping modulo 2**64.  Window hashes at every offset are
-computed in O(N) here (instead of the reference's O(N x window) sliding
-matmul, hashing.py:42-53) from prefix sums in the ring Z/2**64: because the
-base is odd it is invertible modulo 2**64, so
-
-    hash(tokens[i:i+W]) = B**(i+W) * (Q[i+W] - Q[i]),  Q[j] = sum_{t<j} v_t * B**-(t+1)
+``token + 1``, wrapping modulo 2**64.  Window hashes at every offset come from
+one rolling pass in the native library (``cb_window_hashes``, O(N) instead of
+the reference's O(N x window) sliding matmul, hashing.py:42-53), and the
+offsets whose hash is committed from a binary-search scan over the sorted
+committed hashes (``cb_hash_candidates``); both are host code, no GPU.
 
 Matching semantics follow TokenRangeMatcher.match (matcher.py:80-125):
 leftmost-greedy, non-overlapping, with exact token verification.
@@ -21,8 +20,11 @@ from collections import defaultdict
 from collections.abc import Iterable, Sequence
 from dataclasses import dataclass
 
+import ctypes
+
 import numpy as np
 
+from . import _native
 from .types import BlendSegment, SegmentId
 
 POLY_BASE = 1_000_003
@@ -52,20 +54,30 @@ def _powers(base: int, count: int) -> np.ndarray:
 
 
 def window_hashes(tokens: Sequence[int] | np.ndarray, window: int) -> np.ndarray:
-    """uint64 fingerprint of every full window of ``tokens`` (O(N))."""
+    """uint64 fingerprint of every full window of ``tokens`` (O(N), native)."""
     if window <= 0:
         raise ValueError("window must be positive")
-    values = np.asarray(tokens, dtype=np.int64).astype(np.uint64) + np.uint64(1)
+    values = np.ascontiguousarray(tokens, dtype=np.int64)
     n = values.shape[0]
     if n < window:
         return np.empty(0, dtype=np.uint64)
-    with np.errstate(over="ignore"):
-        inv_pows = _powers(_BASE_INV, n + 1)[1:]  # B**-(t+1)
-        prefix = np.zeros(n + 1, dtype=np.uint64)
-        np.cumsum(values * inv_pows, out=prefix[1:])
-        pows = _powers(POLY_BASE, n + 1)
-        starts = np.arange(n - window + 1)
-        return pows[starts + window] * (prefix[starts + window] - prefix[starts])
+    out = np.empty(n - window + 1, dtype=np.uint64)
+    _native.call("cb_window_hashes", values.ctypes.data, n, window, out.ctypes.data)
+    return out
+
+
+def hash_candidates(hashes: np.ndarray, known_sorted: np.ndarray) -> np.ndarray:
+    """Ascending offsets whose hash is in ``known_sorted`` (ascending, distinct uint64)."""
+    hashes = np.ascontiguousarray(hashes, dtype=np.uint64)
+    known_sorted = np.ascontiguousarray(known_sorted, dtype=np.uint64)
+    count = ctypes.c_int64(0)
+    out = np.empty(min(hashes.shape[0], 4096), dtype=np.int64)
+    while True:
+        _native.call("cb_hash_candidates", hashes.ctypes.data, hashes.shape[0], known_sorted.ctypes.data,
+                     known_sorted.shape[0], out.ctypes.data, out.shape[0], ctypes.addressof(count))
+        if count.value <= out.shape[0]:
+            return out[: count.value]
+        out = np.empty(count.value, dtype=np.int64)
 
 
 def chunk_hashes(chunks: np.ndarray) -> np.ndarray:
@@ -93,6 +105,8 @@ class TokenRangeMatcher:
         self._records: dict[SegmentId, FingerprintRecord] = {}
         self._by_hash: dict[tuple[str, int], list[FingerprintRecord]] = defaultdict(list)
         self._hashes: dict[str, set[int]] = defaultdict(set)
+        self._sorted: dict[str, np.ndarray] = {}  # per scope: sorted committed hashes (lazy)
+        self._token_rows: dict[SegmentId, np.ndarray] = {}  # per record: its tokens, for verification
         self._lock = threading.RLock()
 
     def make_record(
@@ -134,17 +148,21 @@ class TokenRangeMatcher:
             self._records[sid] = record
             self._by_hash[(sid.model_scope, sid.content_hash)].append(record)
             self._hashes[sid.model_scope].add(sid.content_hash)
+            self._sorted.pop(sid.model_scope, None)
+            self._token_rows[sid] = np.asarray(record.tokens, dtype=np.int64)
 
     def unregister(self, segment_id: SegmentId) -> None:
         with self._lock:
             if self._records.pop(segment_id, None) is None:
                 return
+            self._token_rows.pop(segment_id, None)
             key = (segment_id.model_scope, segment_id.content_hash)
             remaining = [r for r in self._by_hash[key] if r.segment_id != segment_id]
             if remaining:
                 self._by_hash[key] = remaining
                 return
             del self._by_hash[key]
+            self._sorted.pop(segment_id.model_scope, None)
             scope = self._hashes[segment_id.model_scope]
             scope.discard(segment_id.content_hash)
             if not scope:
@@ -160,20 +178,25 @@ class TokenRangeMatcher:
             known = self._hashes.get(model_scope)
             if not known:
                 return ()
-            hashes = window_hashes(np.asarray(tokens[start_offset:], dtype=np.int64), self.chunk_size)
-            wanted = np.fromiter(known, dtype=np.uint64, count=len(known))
+            wanted = self._sorted.get(model_scope)
+            if wanted is None:
+                wanted = np.sort(np.fromiter(known, dtype=np.uint64, count=len(known)))
+                self._sorted[model_scope] = wanted
+            values = np.asarray(tokens, dtype=np.int64)
+            hashes = window_hashes(values[start_offset:], self.chunk_size)
+            width = self.chunk_size
             next_free = start_offset
-            for rel in np.flatnonzero(np.isin(hashes, wanted)):
-                target = start_offset + int(rel)
+            for rel in hash_candidates(hashes, wanted).tolist():
+                target = start_offset + rel
                 if target < next_free:
                     continue
-                candidates = self._by_hash.get((model_scope, int(hashes[rel])), ())
-                window = tuple(int(t) for t in tokens[target : target + self.chunk_size])
-                record = next((r for r in candidates if r.tokens == window), None)
+                window = values[target : target + width]
+                record = next((r for r in self._by_hash.get((model_scope, int(hashes[rel])), ())
+                               if np.array_equal(self._token_rows[r.segment_id], window)), None)
                 if record is None:
                     continue
                 found.append(BlendSegment(record.segment_id, target))
-                next_free = target + self.chunk_size
+                next_free = target + width
         return tuple(found)
 
     def validate(self, segments: Iterable[BlendSegment]) -> tuple[BlendSegment, ...]:
