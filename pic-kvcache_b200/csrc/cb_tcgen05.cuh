@@ -102,39 +102,20 @@ __device__ __forceinline__ void bulk_load(void* smem, const void* src, uint32_t 
 }
 // K-major, SWIZZLE_128B shared-memory matrix descriptor (sm_100 format):
 // start>>4 | LBO(16 B)>>4 << 16 | SBO(1024 B = 8 rows x 128 B)>>4 << 32 |
-// version 1 << 46 | layout SWIZZLE_128B (2) << 61.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
-  return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) |
-         (1ull << 46) | (2ull << 61);
-}
-// K step kk (16 elements = 32 B) of a 128x128 operand stored as two 128x64
-// SW128 halves 16 KiB apart.
-__device__ __forceinline__ uint64_t operand_desc(uint32_t tile_addr, int kk) {
-  return sw128_desc(tile_addr + (kk >> 2) * kHalfBytes + (kk & 3) * 32);
-}
-// The same descriptor split in words: the high word is the same for every
-// operand here (SBO 1024 B, version 1, SWIZZLE_128B), the low word holds the
-// start address >> 4 (14 bits: shared memory stays below 256 KiB, so adding a
-// K-step offset never carries into the LBO field).  Issuing an MMA then costs
-// one add per operand instead of a 64-bit build.
+// version 1 << 46 | layout SWIZZLE_128B (2) << 61, kept as two words: the high
+// word is the same for every operand here (SBO 1024 B, version 1,
+// SWIZZLE_128B), the low word holds the start address >> 4 (14 bits: shared
+// memory stays below 256 KiB, so adding a K-step offset never carries into the
+// LBO field).  Issuing an MMA then costs one add per operand instead of a
+// 64-bit build.
 constexpr uint32_t kDescHi = 64u | (1u << 14) | (2u << 29);
 __device__ __forceinline__ uint32_t desc_lo(uint32_t smem_addr) {
   return ((smem_addr >> 4) & 0x3FFFu) | (1u << 16);
 }
-// Low-word offset of K step kk (16 elements) within a 128x128 operand stored as
-// two 128x64 SW128 halves 16 KiB apart.
+// Low-word offset of K step kk (16 elements = 32 B) within a 128x128 operand
+// stored as two 128x64 SW128 halves 16 KiB apart.
 __host__ __device__ constexpr uint32_t kstep_lo(int kk) {
   return static_cast<uint32_t>((kk >> 2) * (kHalfBytes >> 4) + (kk & 3) * 2);
-}
-__device__ __forceinline__ void umma_lo(uint32_t tmem_d, uint32_t a_lo, uint32_t b_lo,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
-      "mov.b64 da, {%1, %5};\n\t"
-      "mov.b64 db, {%2, %5};\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(tmem_d),
-      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHi));
 }
 // Eight K steps (K = 128) of a 128x128 product with both operands in shared
 // memory, issued from one asm block: per step two adds and the MMA, nothing
@@ -211,15 +192,6 @@ __device__ __forceinline__ void umma_k128_bmn(uint32_t tmem_d, uint32_t a_tile, 
       "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, 1;\n\t}" ::"r"(tmem_d),
       "r"(desc_lo(a_tile)), "r"(desc_lo_mn(b_tile)), "r"(idesc), "r"(accumulate_first ? 1u : 0u),
       "n"(kDescHi));
-}
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                     uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
-          tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
