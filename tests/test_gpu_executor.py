@@ -7,7 +7,9 @@ the sm_100a kernels; the expectation restates the reference's layer in torch
 with the oracle's deviation, Sparse-Q and select and the reference's attention
 formula.  Selected indices and the staging bytes must match exactly (Sparse-Q:
 except ties within its 1e-3 tolerance); hidden states within the attention
-tolerance (bf16 products downstream)."""
+tolerance (bf16 products downstream).  A last test runs Qwen3BlendExecutor.run
+end to end through PagedBlendLoader (store -> H2D -> relocation -> layers ->
+commit) and compares the pages bit for bit."""
 
 from __future__ import annotations
 
@@ -18,6 +20,7 @@ import pytest
 import torch
 
 import oracle
+from cacheblend_b200.attention import blend_attention
 from cacheblend_b200.config import CacheBlendConfig
 from cacheblend_b200.executor import BlendExecutionState, Qwen3BlendExecutor
 
@@ -106,7 +109,8 @@ def _reference_attention(query, key, value, positions, scale):
     return out
 
 
-def _reference_layer(layer, hidden, residual, positions, old_kv, compute_start, gap_mask, check, ratio):
+def _reference_layer(layer, hidden, residual, positions, old_kv, compute_start, gap_mask, check, ratio,
+                     attention=_reference_attention):
     """ascend.py:487-630 for one layer, kv_deviation strategy, in torch + oracle."""
     sa = layer.self_attn
     if residual is None:
@@ -134,8 +138,8 @@ def _reference_layer(layer, hidden, residual, positions, old_kv, compute_start, 
         positions = positions[selected]
     flat_k[absolute] = k
     flat_v[absolute] = v
-    out = _reference_attention(q.view(-1, HQ, HD), old_kv[0].view(-1, HKV, HD), old_kv[1].view(-1, HKV, HD),
-                               absolute, sa.attn.impl.scale).reshape(-1, HQ * HD)
+    out = attention(q.view(-1, HQ, HD), old_kv[0].view(-1, HKV, HD), old_kv[1].view(-1, HKV, HD),
+                    absolute, sa.attn.impl.scale).reshape(-1, HQ * HD)
     hidden, _ = sa.o_proj(out)
     hidden, residual = layer.post_attention_layernorm(hidden, residual)
     return layer.mlp(hidden), residual, positions, selected
@@ -287,3 +291,78 @@ def test_executor_query_aware_strategies(cuda, strategy):
         sq_sel = run("sparse_q")[2].important_indices.cpu().numpy()
         overlap = np.intersect1d(sq_sel, state_dev.important_indices.cpu().numpy()).size
         assert event["overlap_tokens"] == overlap
+
+
+def test_executor_run_through_the_loader(cuda):
+    """Qwen3BlendExecutor.run end to end (ascend.py:443-485): the loader stages
+    the APC prefix from the pages and two stored chunks relocated from other
+    positions, the executor computes both layers (kv_deviation at layer 1) and
+    the loader commits the span into the pages.  The pages afterwards must equal,
+    bit for bit, the oracle's staging of each layer overwritten with the
+    reference layer's fresh K/V rows."""
+    from cacheblend_b200.loader import PagedBlendLoader
+    from cacheblend_b200.storage import LocalPinnedCPUStore
+    from cacheblend_b200.types import BlendPlan, BlendSegment
+
+    gen = torch.Generator().manual_seed(10)
+    chunk, bs, pool, apc = 64, 16, 64, 64
+    hits = [(400, 128), (64, 320)]  # (source_start, target_start)
+    max_pos = 1024
+    layers = [_layer(gen, cuda, max_pos), _layer(gen, cuda, max_pos)]
+    embed = (torch.randn(1000, HIDDEN, generator=gen) * 0.5).to(torch.bfloat16).to(cuda)
+    model = SimpleNamespace(model=SimpleNamespace(layers=layers, start_layer=0, end_layer=len(layers),
+                                                  embed_tokens=lambda ids: embed[ids]))
+    config = CacheBlendConfig.from_extra_config(
+        {"chunk_size": chunk, "check_layers": [1], "recompute_ratios": [0.15],
+         "selection_strategy": "kv_deviation", "strict_version_check": False})
+    executor = _executor(layers, "kv_deviation")
+    executor.model = model
+    executor.config = config
+    pages = [torch.randn(2, pool, bs, HKV, HD, generator=gen).to(torch.bfloat16).to(cuda) for _ in layers]
+    before = [p.clone() for p in pages]
+    tokens = torch.randint(0, 1000, (400,), generator=gen).tolist()
+    blocks = torch.randperm(pool, generator=gen)[:25]
+    slots = (blocks[:, None] * bs + torch.arange(bs)[None, :]).reshape(-1)[:400]
+    store = LocalPinnedCPUStore(chunk, 1 << 26)
+    chunk_data = {}
+    segments = []
+    for source, target in hits:
+        sid = store.begin_put("scope", source, tokens[target : target + chunk], len(layers))
+        for layer in range(len(layers)):
+            host = torch.randn(2, chunk, HKV, HD, generator=gen).to(torch.bfloat16).pin_memory()
+            chunk_data[(sid, layer)] = host
+            store.put_layer_host(sid, layer, host)
+        segments.append(BlendSegment(sid, target))
+    plan = BlendPlan.from_segments(apc, segments)
+    assert store.pin("req", segments) == tuple(sorted(segments, key=lambda s: s.target_start))
+    loader = PagedBlendLoader(pages, store, "req", plan, slots, bs, config, load_stream=torch.cuda.Stream(cuda))
+    executor.run("req", tokens, plan, loader)
+    torch.cuda.synchronize()
+
+    # expectation, layer by layer
+    bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    end = plan.allocation_end
+    n = end - apc
+    gap_mask = plan.gap_mask()
+    hidden, residual = embed[torch.tensor(tokens[apc:end], device=cuda)], None
+    positions = torch.arange(apc, end, device=cuda)
+    slot_np = slots[:end].numpy()
+    for layer_id, layer in enumerate(layers):
+        k_cache = bits(before[layer_id][0])
+        v_cache = bits(before[layer_id][1])
+        table = oracle.f32_to_bf16(layer.self_attn.rotary_emb.cos_sin_cache.cpu().numpy())
+        segs = [(seg.segment_id.source_start, seg.target_start, chunk, bits(chunk_data[(seg.segment_id, layer_id)]))
+                for seg in plan.segments]
+        staged = oracle.blend_load(oracle.BF16, end, apc, k_cache, v_cache, slot_np, bs, segs,
+                                   np.ones(len(segs), dtype=np.int32), table, HD, HD, True)
+        staging = torch.from_numpy(staged.view(np.int16)).view(torch.bfloat16).to(cuda)
+        # the attention itself is checked elsewhere; here the same kernel keeps the
+        # downstream rows bit-identical so the pages can be compared exactly
+        hidden, residual, positions, _ = _reference_layer(
+            layer, hidden, residual, positions, staging, apc, gap_mask, check=layer_id == 1, ratio=0.15,
+            attention=lambda q, k, v, pos, scale: blend_attention(q, k, v, pos, scale))
+        want = before[layer_id].clone()
+        flat = want.view(2, pool * bs, HKV, HD)
+        idx = torch.from_numpy(slot_np[apc:end]).to(cuda)
+        flat[:, idx] = staging[:, apc:end]
+        assert torch.equal(pages[layer_id], want), layer_id
