@@ -247,7 +247,8 @@ CB_API int cb_blend_attention_workspace_size(int64_t num_queries, int64_t num_ke
  * Causal attention of the computed queries over the whole staging context
  * (Qwen3BlendExecutor._attention, cacheblend_vllm/ascend.py:798-846, its
  * einsum path): query [num_queries][num_q_heads][head_size] at absolute
- * positions query_positions[i] (device int64, each in [0, num_keys)), key and
+ * positions query_positions[i] (device int64; a position >= num_keys sees
+ * every key, as the reference's mask does; a negative one gives zeros), key and
  * value [num_keys][num_kv_heads][head_size] (staging rows = positions),
  * query head h attends KV head h / (num_q_heads / num_kv_heads):
  *   w = T(T(q . k) * scale), p = softmax over keys k <= pos of w (fp32),

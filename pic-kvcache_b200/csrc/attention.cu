@@ -492,10 +492,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Qd[h][r][:] = query[r / groups][h * groups + r % groups][:], zero rows up to
 // rows_pad; row positions; the largest position of each pair of query tiles.
+// A position past the last key sees every key, as the reference's mask
+// (q_pos < k_pos over the staging rows) lets it: it is clamped to num_keys - 1.
+__device__ __forceinline__ int32_t clamp_position(int64_t pos, int64_t num_keys) {
+  return static_cast<int32_t>(pos < num_keys ? (pos < -1 ? -1 : pos) : num_keys - 1);
+}
 __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ query,
                                                    int64_t query_token_stride,
                                                    const int64_t* __restrict__ positions,
-                                                   int64_t num_queries, int num_kv_heads, int groups,
+                                                   int64_t num_queries, int64_t num_keys,
+                                                   int num_kv_heads, int groups,
                                                    int rows_pad, char* __restrict__ qd,
                                                    int32_t* __restrict__ row_pos,
                                                    int32_t* __restrict__ pair_max) {
@@ -517,14 +523,14 @@ __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ quer
       else
         dst[lane] = make_uint4(0, 0, 0, 0);
     }
-    if (h == 0 && lane == 0) row_pos[r] = qi < num_queries ? static_cast<int32_t>(positions[qi]) : -1;
+    if (h == 0 && lane == 0) row_pos[r] = qi < num_queries ? clamp_position(positions[qi], num_keys) : -1;
   }
   const int q_pairs = rows_pad / kPairRows;
   for (int64_t qt = warp; qt < q_pairs; qt += nwarps) {
     int mx = -1;
     for (int r = lane; r < kPairRows; r += 32) {
       const int64_t qi = (qt * kPairRows + r) / groups;
-      if (qi < num_queries) mx = max(mx, static_cast<int>(positions[qi]));
+      if (qi < num_queries) mx = max(mx, static_cast<int>(clamp_position(positions[qi], num_keys)));
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -621,7 +627,8 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
     const int64_t warps = num_kv_heads * w.rows_pad;
     const int grid = static_cast<int>(std::min<int64_t>((warps + 7) / 8, kSmCount * 8));
     att::prep_kernel<<<grid, 256, 0, s>>>(static_cast<const char*>(query), query_token_stride,
-                                           query_positions, num_queries, static_cast<int>(num_kv_heads),
+                                           query_positions, num_queries, num_keys,
+                                           static_cast<int>(num_kv_heads),
                                            groups, static_cast<int>(w.rows_pad), ws + w.qd,
                                            reinterpret_cast<int32_t*>(ws + w.row_pos),
                                            reinterpret_cast<int32_t*>(ws + w.pair_max));

@@ -249,3 +249,12 @@ def test_attention_fused_logits_rejects_nonpositive_scale(cuda):
     k = torch.zeros(4, 8, 128, dtype=torch.bfloat16, device=cuda)
     with pytest.raises(ValueError):
         blend_attention(q, k, k, torch.arange(4, device=cuda), -1.0, exact_rounding=False)
+
+
+def test_attention_positions_past_the_last_key(cuda):
+    """A query position at or past the last staging row sees every key, as the
+    reference's mask over the existing keys lets it."""
+    query, key, value, _ = _inputs(cuda, 40, 300, 16, 4, torch.bfloat16, 77)
+    pos = torch.tensor([299, 300, 5000] + list(range(100, 137)), device=cuda)
+    got = blend_attention(query, key, value, pos, 128 ** -0.5)
+    _check(got, reference_attention(query, key, value, pos, 128 ** -0.5))
