@@ -14,7 +14,8 @@
 // per probability.
 //
 // Layout: rows = (query, group) pairs of one KV head, r = qi * groups + g, in
-// 128-row tiles (dense copy Qd[h][r][:] made by prep_kernel), so every K / V
+// 128-row tiles (one 4-D TMA box over the query tensor: 64 dims x groups x 1
+// KV head x 128/groups queries, rows in that order), so every K / V
 // tile is shared by all groups of the head.  K and V tiles are TMA boxes of the
 // staging rows as they lie ([keys][dims], SWIZZLE_128B):
 //   S = Q K^T   A = Q tile [rows][dims] (K-major),  B = K tile [keys][dims] (K-major) -> TMEM
@@ -228,8 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&sh.q_full, kPair * kTileBytes);
         for (int x = 0; x < kPair; ++x) {
           unsigned char* qb = q_buf + x * kTileBytes;
-          tma_load_3d(qb, &q_map, &sh.q_full, 0, qp * kPairRows + x * kTile, h);
-          tma_load_3d(qb + kHalfBytes, &q_map, &sh.q_full, 64, qp * kPairRows + x * kTile, h);
+          const int q0 = (qp * kPairRows + x * kTile) / c.groups;  // first query of the tile
+          tma_load_4d(qb, &q_map, &sh.q_full, 0, 0, h, q0);
+          tma_load_4d(qb + kHalfBytes, &q_map, &sh.q_full, 64, 0, h, q0);
         }
         q_armed = it & 1;
         const int kt_end = max(c.pair_max[qp], 0) / kTile;
@@ -490,43 +492,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Qd[h][r][:] = query[r / groups][h * groups + r % groups][:], zero rows up to
-// rows_pad; row positions; the largest position of each pair of query tiles.
-// A position past the last key sees every key, as the reference's mask
-// (q_pos < k_pos over the staging rows) lets it: it is clamped to num_keys - 1.
+// Row positions (rows past the last query: -1) and the largest position of
+// each pair of query tiles.  A position past the last key sees every key, as
+// the reference's mask (q_pos < k_pos over the staging rows) lets it: it is
+// clamped to num_keys - 1.
 __device__ __forceinline__ int32_t clamp_position(int64_t pos, int64_t num_keys) {
   return static_cast<int32_t>(pos < num_keys ? (pos < -1 ? -1 : pos) : num_keys - 1);
 }
-__global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ query,
-                                                   int64_t query_token_stride,
-                                                   const int64_t* __restrict__ positions,
-                                                   int64_t num_queries, int64_t num_keys,
-                                                   int num_kv_heads, int groups,
-                                                   int rows_pad, char* __restrict__ qd,
-                                                   int32_t* __restrict__ row_pos,
+__global__ void __launch_bounds__(256) prep_kernel(const int64_t* __restrict__ positions,
+                                                   int64_t num_queries, int64_t num_keys, int groups,
+                                                   int rows_pad, int32_t* __restrict__ row_pos,
                                                    int32_t* __restrict__ pair_max) {
-  constexpr int kRowBytes = kHead * 2;
   const int lane = threadIdx.x & 31;
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  const int64_t total = static_cast<int64_t>(num_kv_heads) * rows_pad;
-  for (int64_t task = warp; task < total; task += nwarps) {
-    const int h = static_cast<int>(task / rows_pad);
-    const int r = static_cast<int>(task - (int64_t)h * rows_pad);
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t threads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t r = tid; r < rows_pad; r += threads) {
     const int64_t qi = r / groups;
-    const int g = r - static_cast<int>(qi) * groups;
-    uint4* dst = reinterpret_cast<uint4*>(qd + task * kRowBytes);
-    if (lane < kRowBytes / 16) {
-      if (qi < num_queries)
-        dst[lane] = reinterpret_cast<const uint4*>(query + qi * query_token_stride +
-                                                   (int64_t)(h * groups + g) * kRowBytes)[lane];
-      else
-        dst[lane] = make_uint4(0, 0, 0, 0);
-    }
-    if (h == 0 && lane == 0) row_pos[r] = qi < num_queries ? clamp_position(positions[qi], num_keys) : -1;
+    row_pos[r] = qi < num_queries ? clamp_position(positions[qi], num_keys) : -1;
   }
   const int q_pairs = rows_pad / kPairRows;
-  for (int64_t qt = warp; qt < q_pairs; qt += nwarps) {
+  for (int64_t qt = tid >> 5; qt < q_pairs; qt += threads >> 5) {
     int mx = -1;
     for (int r = lane; r < kPairRows; r += 32) {
       const int64_t qi = (qt * kPairRows + r) / groups;
@@ -540,7 +525,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ quer
 
 // ---------------------------------------------------------------- host side
 struct Workspace {
-  size_t qd, row_pos, pair_max, total;
+  size_t row_pos, pair_max, total;
   int64_t rows_pad;
 };
 
@@ -551,8 +536,6 @@ Workspace layout(int64_t num_queries, int64_t num_keys, int64_t num_q_heads, int
   Workspace w{};
   w.rows_pad = (num_queries * groups + kPairRows - 1) / kPairRows * kPairRows;
   size_t off = 0;
-  w.qd = off;
-  off = align_up(off + (size_t)num_kv_heads * w.rows_pad * kHead * 2, 1024);
   w.row_pos = off;
   off = align_up(off + (size_t)w.rows_pad * 4, 256);
   w.pair_max = off;
@@ -624,12 +607,10 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
   char* ws = static_cast<char*>(workspace);
   const int groups = static_cast<int>(num_q_heads / num_kv_heads);
   {
-    const int64_t warps = num_kv_heads * w.rows_pad;
-    const int grid = static_cast<int>(std::min<int64_t>((warps + 7) / 8, kSmCount * 8));
-    att::prep_kernel<<<grid, 256, 0, s>>>(static_cast<const char*>(query), query_token_stride,
-                                           query_positions, num_queries, num_keys,
-                                           static_cast<int>(num_kv_heads),
-                                           groups, static_cast<int>(w.rows_pad), ws + w.qd,
+    const int64_t blocks = std::max<int64_t>((w.rows_pad + 255) / 256, w.rows_pad / att::kPairRows / 8 + 1);
+    const int grid = static_cast<int>(std::min<int64_t>(blocks, kSmCount * 4));
+    att::prep_kernel<<<grid, 256, 0, s>>>(query_positions, num_queries, num_keys, groups,
+                                           static_cast<int>(w.rows_pad),
                                            reinterpret_cast<int32_t*>(ws + w.row_pos),
                                            reinterpret_cast<int32_t*>(ws + w.pair_max));
     rc = launch_status("cb_blend_attention (prep)");
@@ -639,8 +620,16 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
   rc = tc::get_encoder(&encode);
   if (rc != CB_OK) return rc;
   CUtensorMap q_map, k_map, v_map;
-  rc = tc::encode_3d(encode, &q_map, dtype, ws + w.qd, head_size, w.rows_pad, num_kv_heads,
-                     head_size * 2, w.rows_pad * head_size * 2, tc::kTile, 1);
+  {
+    // query [num_queries][num_kv_heads * groups][128] as (dims, group, KV head, query)
+    const uint64_t dims[4] = {static_cast<uint64_t>(head_size), static_cast<uint64_t>(groups),
+                              static_cast<uint64_t>(num_kv_heads), static_cast<uint64_t>(num_queries)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(head_size * 2),
+                                 static_cast<uint64_t>(groups * head_size * 2),
+                                 static_cast<uint64_t>(query_token_stride)};
+    rc = tc::encode_4d(encode, &q_map, dtype, query, dims, strides, static_cast<uint32_t>(groups), 1,
+                       static_cast<uint32_t>(tc::kTile / groups));
+  }
   if (rc == CB_OK)
     rc = tc::encode_3d(encode, &k_map, dtype, key, head_size, num_kv_heads, num_keys, head_size * 2,
                        key_token_stride, 1, tc::kTile);

@@ -84,6 +84,14 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity) {
     if (__shfl_sync(0xffffffffu, static_cast<int>(global_ns() - start > kTimeoutNs), 0)) return false;
   }
 }
+__device__ __forceinline__ void tma_load_4d(void* smem, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(void* smem, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
   asm volatile(
@@ -286,6 +294,27 @@ inline int encode_3d(EncodeTiled encode, CUtensorMap* map, int dtype, const void
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return CB_ERR_INVALID;
+  }
+  return CB_OK;
+}
+
+// 4-D map with a 64 x b1 x b2 x b3 box of 16-bit elements, SWIZZLE_128B,
+// out-of-range elements read as zero.
+inline int encode_4d(EncodeTiled encode, CUtensorMap* map, int dtype, const void* base,
+                     const uint64_t (&dims)[4], const uint64_t (&strides)[3], uint32_t b1,
+                     uint32_t b2, uint32_t b3) {
+  const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t st[3] = {strides[0], strides[1], strides[2]};
+  const cuuint32_t box[4] = {64, b1, b2, b3};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType type =
+      dtype == CB_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode(map, type, 4, const_cast<void*>(base), d, st, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (4-D) failed (%d)", static_cast<int>(r));
     return CB_ERR_INVALID;
   }
   return CB_OK;
