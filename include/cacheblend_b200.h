@@ -107,6 +107,15 @@ CB_API int cb_copy_rows_d2h(void* dst, int64_t dst_pitch, const void* src, int64
                             int64_t row_bytes, int64_t rows, void* stream);
 
 /*
+ * Diagnostics: each of the library's four bounded-wait helpers waits on a
+ * barrier that is never completed, gives up after its bound (about 2 s) and
+ * ORs its bit (1, 2, 4, 8) into *result (device memory, zeroed by the caller)
+ * on `stream`.  A result of 15 shows that a stuck pipeline stage ends in an
+ * error word instead of a hang, and the context stays usable.
+ */
+CB_API int cb_wait_selftest(int32_t* result, void* stream);
+
+/*
  * Host function (no GPU): the 64-bit polynomial fingerprint of every full
  * `window` of `tokens` (n - window + 1 values into `out`), identical to
  * cacheblend_vllm/hashing.py:42-53 (rolling_hash_values) in O(n).

@@ -83,6 +83,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "cb_sorted_overlap": (_i32, [_ptr, _i64, _ptr, _i64, _ptr, _ptr]),
     "cb_copy_rows_d2h": (_i32, [_ptr, _i64, _ptr, _i64, _i64, _i64, _ptr]),
     "cb_window_hashes": (_i32, [_ptr, _i64, _i64, _ptr]),
+    "cb_wait_selftest": (_i32, [_ptr, _ptr]),
     "cb_hash_candidates": (_i32, [_ptr, _i64, _ptr, _i64, _ptr, _i64, _ptr]),
     "cb_relocate_key": (
         _i32,
