@@ -51,7 +51,7 @@ def blend_attention(
 
     ``exact_rounding`` keeps the einsum path's roundings (element-type logits, element-type
     logit * scale); False computes fp32 logits * scale like the reference's fused attention
-    kernel (ascend.py:814-830) and flash attention, about a third faster."""
+    kernel (ascend.py:814-830) and flash attention, about a fifth faster."""
     _native.require_cuda(query, key, value)
     if query.ndim != 3 or key.ndim != 3 or value.shape != key.shape:
         raise ValueError("query must be [tokens, q_heads, head]; key and value [keys, kv_heads, head]")
