@@ -41,6 +41,9 @@ class PinnedArena:
         self._allocated = 0  # slots backed by segments
         self._used = 0
         self._cursor = 0
+        # per (segment, layer shape, dtype): the segment as [slots, layers, *shape], so a
+        # run of consecutive slots yields its views with one slice and one unbind
+        self._shaped: dict[tuple[int, tuple[int, ...], torch.dtype], torch.Tensor] = {}
 
     # ---- introspection --------------------------------------------------------
     @property
@@ -96,6 +99,33 @@ class PinnedArena:
         segment, base = self._locate(slot)
         start = base + layer * self.layer_bytes
         return segment[start : start + self.layer_bytes].view(dtype).view(shape)
+
+    def _shaped_segment(self, index: int, shape: tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
+        key = (index, shape, dtype)
+        view = self._shaped.get(key)
+        if view is None:
+            segment = self._segments[index]
+            view = segment.view(dtype).view(segment.numel() // self.entry_bytes, self.num_layers, *shape)
+            self._shaped[key] = view
+        return view
+
+    def layer_views(self, slots: list[int], layer: int, shape: tuple[int, ...],
+                    dtype: torch.dtype) -> list[torch.Tensor]:
+        """``layer_view`` of every slot in ``slots``, built per run of consecutive slots of
+        one segment with a single slice (the Store path publishes a batch at a time)."""
+        shape = tuple(shape)
+        out: list[torch.Tensor] = []
+        i = 0
+        while i < len(slots):
+            index, first = divmod(slots[i], self.slots_per_segment)
+            j = i + 1
+            while (j < len(slots) and slots[j] == slots[j - 1] + 1
+                   and slots[j] // self.slots_per_segment == index):
+                j += 1
+            view = self._shaped_segment(index, shape, dtype)
+            out.extend(view[first : first + (j - i), layer].unbind(0))
+            i = j
+        return out
 
     def layer_ptr(self, slot: int, layer: int) -> int:
         segment, base = self._locate(slot)

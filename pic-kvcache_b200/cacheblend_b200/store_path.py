@@ -208,11 +208,9 @@ class StorePipeline:
         slot) were already released by the reservation."""
         arena = self.store.arena
         layer_id = pending[0][1] if pending else 0
-        sids, views = [], []
-        for (sid, _, _), slot in zip(pending, slots):
-            if slot is not None:
-                sids.append(sid)
-                views.append(arena.layer_view(slot, layer_id, tuple(chunk_shape), dtype))
+        kept = [(sid, slot) for (sid, _, _), slot in zip(pending, slots) if slot is not None]
+        sids = [sid for sid, _ in kept]
+        views = arena.layer_views([slot for _, slot in kept], layer_id, tuple(chunk_shape), dtype)
         results = self.store.put_layers_host(sids, layer_id, views) if sids else []
         return any(result for result in results if result is not None)
 

@@ -127,3 +127,19 @@ def test_store_arena_slots_return_on_abort_and_clear():
     assert store.arena.used_slots == 3
     store.clear()
     assert store.arena.used_slots == 0 and store.committed_entries == 0
+
+
+def test_layer_views_match_layer_view_across_runs_and_segments():
+    arena = _arena(7, segment_entries=3)  # segments of 3, 3 and 1 entries
+    slots = [arena.alloc() for _ in range(7)]
+    for slot in slots:
+        for layer in range(LAYERS):
+            arena.layer_view(slot, layer, LAYER_SHAPE, torch.float32).fill_(slot * 10 + layer)
+    picks = [0, 1, 2, 3, 4, 6, 5, 1]  # runs inside a segment, across a boundary, out of order
+    views = arena.layer_views(picks, 2, LAYER_SHAPE, torch.float32)
+    assert len(views) == len(picks)
+    for slot, view in zip(picks, views):
+        assert view.shape == LAYER_SHAPE and view.is_contiguous()
+        assert view.data_ptr() == arena.layer_ptr(slot, 2)
+        assert torch.all(view == slot * 10 + 2)
+    assert arena.layer_views([], 0, LAYER_SHAPE, torch.float32) == []
