@@ -32,6 +32,7 @@ host cores with the same metric (rank 0 only).
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -1029,6 +1030,49 @@ def store_reference(args, world: int) -> None:
     }), flush=True)
 
 
+def freeze_gc_heap() -> None:
+    """vLLM's own startup freeze when it is importable, else the same three collections
+    and ``gc.freeze``."""
+    try:
+        from vllm.utils.gc_utils import freeze_gc_heap as vllm_freeze
+    except ImportError:
+        gc.collect(0)
+        gc.collect(1)
+        gc.collect(2)
+        gc.freeze()
+    else:
+        vllm_freeze()
+
+
+class GcPauses:
+    """Collections (count, total and longest pause per generation) while entered."""
+
+    def __init__(self):
+        self.pauses: list[tuple[int, float]] = []
+        self._start = 0.0
+
+    def _callback(self, phase: str, info: dict) -> None:
+        if phase == "start":
+            self._start = time.perf_counter()
+        else:
+            self.pauses.append((info["generation"], (time.perf_counter() - self._start) * 1e3))
+
+    def __enter__(self):
+        gc.callbacks.append(self._callback)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        gc.callbacks.remove(self._callback)
+
+    def summary(self) -> dict:
+        out = {}
+        for generation in (0, 1, 2):
+            ms = [t for g, t in self.pauses if g == generation]
+            out[f"gen{generation}"] = {"count": len(ms), "total_ms": round(sum(ms), 2),
+                                       "max_ms": round(max(ms), 2) if ms else 0.0}
+        return out
+
+
 def store_bench(args, world: int, rank: int, local: int) -> None:
     """Config 5: Store path (gather complete chunks -> D2H -> LRU publication) for 36 layers."""
     cfg = STORE_CONFIG
@@ -1040,6 +1084,11 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
     rng_tokens = rng.integers(0, 151_936, size=(cfg["requests"], cfg["tokens"]), dtype=np.int64)
     blocks = rng.permutation(cfg["requests"] * cfg["tokens"] // cfg["block_size"])
     metas = [store_metadata(cfg, step, rng_tokens, blocks) for step in range(max(args.warmup, 3) + args.steps)]
+    # the serving process freezes its startup heap before taking requests
+    # (vllm/v1/engine/core.py: freeze_gc_heap after init), so a full collection
+    # walks only what serving allocated; the pauses inside the timed steps are reported
+    freeze_gc_heap()
+    gc_pauses = GcPauses()
     row_bytes = heads * cfg["head_dim"] * 2
     step_tokens = cfg["requests"] * cfg["tokens"]
     offered = step_tokens * cfg["layers"] * 2 * row_bytes
@@ -1053,7 +1102,7 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
     torch.cuda.synchronize(device)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks, gc_pauses:
         start.record()
         for step in range(args.steps):
             store_step(connector, caches, metas[max(args.warmup, 3) + step])
@@ -1091,7 +1140,8 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
             "config": {"workload": cfg["name"], "requests": cfg["requests"], "tokens_per_request": cfg["tokens"],
                        "layers": cfg["layers"], "kv_heads_per_rank": heads, "lru_gb": cfg["local_cpu_gb"],
                        "inflight_batches": cfg["inflight"], "store_workers": cfg["workers"],
-                       "parallelism": f"tp{world}", "l2": "pages 72 GiB, far larger than L2"},
+                       "parallelism": f"tp{world}", "l2": "pages 72 GiB, far larger than L2",
+                       "gc": "startup heap frozen as vLLM's engine core does (freeze_gc_heap)"},
             "gpu_launches": len(events),
             "roofline": {"bound": "hbm", "kernel": "store_gather", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
@@ -1104,6 +1154,7 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
                             "already measured through the connector API with the D2H inside"},
             "store": {"committed_entries": store.committed_entries, "bytes": store.current_bytes,
                       "committed_tokens": store.committed_entries * cfg["chunk"],
+                      "gc_pauses_in_timed_steps": gc_pauses.summary(),
                       "pinned_arena_bytes": store.arena.pinned_bytes if store.arena is not None else None,
                       "note": "the LRU budget (16 GiB) holds 455 of the 2,048 chunks offered per step; "
                               "with the pinned arena a chunk that cannot get a slot fails closed before "
@@ -1112,6 +1163,7 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
             "clocks": clocks.summary(), "cpu_baseline": cpu,
         }), flush=True)
     connector.close()
+    gc.unfreeze()
 
 
 def main() -> None:

@@ -15,6 +15,7 @@ leftmost-greedy, non-overlapping, with exact token verification.
 
 from __future__ import annotations
 
+import functools
 import threading
 from collections import defaultdict
 from collections.abc import Iterable, Sequence
@@ -40,8 +41,10 @@ def content_hash(tokens: Sequence[int]) -> int:
     return value
 
 
+@functools.lru_cache(maxsize=16)
 def _powers(base: int, count: int) -> np.ndarray:
-    """[base**0, base**1, ..., base**(count-1)] modulo 2**64 as uint64."""
+    """[base**0, base**1, ..., base**(count-1)] modulo 2**64 as uint64 (read-only,
+    cached: every chunk of one width shares the weights)."""
     out = np.empty(count, dtype=np.uint64)
     if count == 0:
         return out
@@ -50,6 +53,7 @@ def _powers(base: int, count: int) -> np.ndarray:
         out[1:] = np.uint64(base)
         with np.errstate(over="ignore"):
             np.cumprod(out, out=out)
+    out.flags.writeable = False
     return out
 
 
@@ -126,14 +130,22 @@ class TokenRangeMatcher:
     ) -> list[FingerprintRecord]:
         """Records of ``count`` consecutive chunks starting at ``tokens[first_start]``."""
         width = self.chunk_size
-        rows = np.asarray(tokens[first_start : first_start + count * width], dtype=np.int64)
+        span = tokens[first_start : first_start + count * width]
+        if isinstance(span, list):
+            # a list of ints (vLLM's token ids): the record tuples are list slices
+            rows = np.fromiter(span, dtype=np.int64, count=len(span))
+        else:
+            rows = np.asarray(span, dtype=np.int64)
         if rows.shape[0] != count * width:
             raise ValueError(f"fingerprint requires {count * width} tokens, got {rows.shape[0]}")
         rows = rows.reshape(count, width)
         hashes = chunk_hashes(rows).tolist()
+        if isinstance(span, list):
+            chunks = [tuple(span[i * width : (i + 1) * width]) for i in range(count)]
+        else:
+            chunks = [tuple(row) for row in rows.tolist()]
         return [
-            FingerprintRecord(SegmentId(model_scope, hashes[i], first_start + i * width, width),
-                              tuple(rows[i].tolist()))
+            FingerprintRecord(SegmentId(model_scope, hashes[i], first_start + i * width, width), chunks[i])
             for i in range(count)
         ]
 

@@ -16,15 +16,18 @@ stream (cacheblend_vllm/connector.py:384-549):
 B200 specifics: the staging is chunk-major ``[chunks, 2, chunk, H, D]`` so the
 gather is one ``cb_paged_gather`` launch and every published chunk view is
 contiguous (one DMA when the chunk is loaded again).  With a pinned arena
-attached to the store, each chunk's layer is copied straight into its entry's
-arena slot: chunks in consecutive slots go in one strided copy-engine
-transfer (``cb_copy_rows_d2h``, row pitch = the entry size), so a batch of
+attached to the store, the chunks' slots are reserved before the gather (a
+batch whose chunks all fail closed launches nothing) and each chunk's layer
+is copied straight into its entry's arena slot: chunks in consecutive slots go
+in one strided copy-engine transfer (``cb_copy_rows_d2h``, row pitch = the
+entry size), so a batch of
 chunks begun together is still one transfer.  Without an arena the batch goes
 to a fresh pinned buffer in one transfer and its chunks are published as views.
 """
 
 from __future__ import annotations
 
+import math
 import threading
 import time
 from concurrent.futures import Future, ThreadPoolExecutor
@@ -81,16 +84,30 @@ class StorePipeline:
         request_id: str,
         store_enqueued_ns: int | None = None,
     ) -> None:
-        """Gather + D2H of one request's chunks of one layer on the Store stream."""
-        self._slots.acquire()
+        """Gather + D2H of one request's chunks of one layer on the Store stream.
+
+        With an arena the chunks' slots are reserved first: a batch whose chunks all
+        fail closed there launches nothing and takes no in-flight slot.  When the
+        enqueue itself fails, the batch's layer reservations are given up
+        (``cancel_layer``), so no entry or arena slot waits for a put that never comes."""
         try:
             paged = self._describe(kv_layer)
             _native.require_cuda(paged.key)
             chunks = len(pending)
             if chunks * self.chunk_size != slots.numel():
                 raise ValueError("slots must cover the pending chunks exactly")
-            serving = torch.cuda.current_stream(paged.device)
             shape = (chunks, 2, self.chunk_size, *paged.row.dims)
+            arena_slots = self._arena_reserve(pending, shape, paged.dtype)
+        except Exception:
+            self._cancel(pending)
+            raise
+        if arena_slots is not None and all(slot is None for slot in arena_slots):
+            with self._lock:
+                self._pending_counts[request_id] = self._pending_counts.get(request_id, 0) + 1
+            return
+        self._slots.acquire()
+        try:
+            serving = torch.cuda.current_stream(paged.device)
             with torch.cuda.stream(self.stream):
                 self.stream.wait_stream(serving)
                 staging = self._staging.get(request_id)
@@ -119,13 +136,13 @@ class StorePipeline:
                     finish = torch.cuda.Event(enable_timing=True)
                     finish.record(self.stream)
                     self.kernel_events.append((begin, finish, staging.numel() * staging.element_size()))
-                arena_slots = self._arena_copy(pending, staging)
-                if arena_slots is None:
+                if arena_slots is not None:
+                    self._arena_copy(pending, arena_slots, staging)
+                    host = None
+                else:
                     host = torch.empty(shape, dtype=paged.dtype, pin_memory=True)
                     host.copy_(staging, non_blocking=True)
                     self.d2h_bytes += host.numel() * host.element_size()
-                else:
-                    host = None
                 event = torch.cuda.Event()
                 event.record(self.stream)
                 device_slots_.record_stream(self.stream)
@@ -135,25 +152,33 @@ class StorePipeline:
             )
         except Exception:
             self._slots.release()
+            self._cancel(pending)
             raise
         with self._lock:
             self._futures.add(future)
             self._pending_counts[request_id] = self._pending_counts.get(request_id, 0) + 1
         future.add_done_callback(self._done)
 
-    def _arena_copy(self, pending: list[tuple[Any, int, int]], staging: torch.Tensor) -> list | None:
-        """Reserve arena slots for the batch's chunks and copy each chunk's layer into its
-        slot (one strided transfer per run of consecutive slots) on the Store stream.
-        Returns the slot per chunk (None: dropped, fail closed) or None when the batch
-        does not use the arena (no arena, mixed layers or another chunk geometry)."""
+    def _arena_reserve(self, pending: list[tuple[Any, int, int]], shape: tuple[int, ...],
+                       dtype: torch.dtype) -> list | None:
+        """Reserve arena slots for the batch's chunks.  Returns the slot per chunk (None:
+        dropped, fail closed) or None when the batch does not use the arena (no arena,
+        mixed layers or another chunk geometry)."""
         arena = self.store.arena
         if arena is None or not pending:
             return None
         layer_id = pending[0][1]
-        chunk_bytes = staging[0].numel() * staging.element_size()
+        chunk_bytes = math.prod(shape[1:]) * dtype.itemsize
         if chunk_bytes != arena.layer_bytes or any(layer != layer_id for _, layer, _ in pending):
             return None
-        slots = self.store.arena_reserve([sid for sid, _, _ in pending], layer_id)
+        return self.store.arena_reserve([sid for sid, _, _ in pending], layer_id)
+
+    def _arena_copy(self, pending: list[tuple[Any, int, int]], slots: list, staging: torch.Tensor) -> None:
+        """Copy each reserved chunk's layer from the staging into its slot on the Store
+        stream, one strided transfer per run of consecutive slots."""
+        arena = self.store.arena
+        layer_id = pending[0][1]
+        chunk_bytes = staging[0].numel() * staging.element_size()
         kept = [(i, slot) for i, slot in enumerate(slots) if slot is not None]
         stream = self.stream.cuda_stream
         start = 0
@@ -168,7 +193,10 @@ class StorePipeline:
                          staging[index].data_ptr(), chunk_bytes, chunk_bytes, end - start, stream)
             self.d2h_bytes += (end - start) * chunk_bytes
             start = end
-        return slots
+
+    def _cancel(self, pending: list[tuple[Any, int, int]]) -> None:
+        for segment_id, layer_id, _ in pending:
+            self.store.cancel_layer(segment_id, layer_id)
 
     def _describe(self, kv_layer: Any):
         """``describe_paged`` memoised on the layer tensors' identity and geometry."""

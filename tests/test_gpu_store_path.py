@@ -235,3 +235,35 @@ def test_arena_fragmented_slots_match_oracle(cuda):
     finally:
         connector.close()
 
+
+
+def test_arena_reservation_precedes_the_gather(cuda):
+    """A batch whose chunks all fail closed at the arena reservation launches no
+    gather and copies nothing; an enqueue that raises after its slot was reserved
+    gives the slot and the entry's layer reservation back."""
+    rng = np.random.default_rng(14)
+    kv_caches, _ = _pages(rng, cuda, "flash_attn")
+    chunk_bytes = 2 * CHUNK * HEADS * HD * 2
+    connector = _worker(cuda, 2 * LAYERS * chunk_bytes, kv_caches, arena=True)  # two entries
+    pipe, store = connector._pipeline, connector._store
+    tokens = rng.integers(0, 150_000, size=4 * CHUNK).tolist()
+    blocks = rng.permutation(POOL)[: 4 * CHUNK // BS]
+    slots = connector_module._slot_mapping(blocks.tolist(), BS, len(tokens))
+    try:
+        _save(connector, "a", tokens[: 2 * CHUNK], slots[: 2 * CHUNK], 2 * CHUNK)
+        store.pin("keep", store.match("model", tokens[: 2 * CHUNK], 0))
+        pipe.kernel_events, before = [], pipe.d2h_bytes
+        _save(connector, "b", tokens[2 * CHUNK :], slots[2 * CHUNK :], 2 * CHUNK)
+        assert pipe.kernel_events == [] and pipe.d2h_bytes == before
+        assert store.committed_entries == 2 and store.arena.used_slots == 2
+        store.release("keep")
+        sids = store.begin_put_chunks("model", 0, tokens[2 * CHUNK :], 1, LAYERS)
+        assert store.reserve_layers(sids, 0) == [True]
+        bad = torch.full((CHUNK,), POOL * BS, dtype=torch.long)  # one past the last page slot
+        with pytest.raises(IndexError):  # host-side range check, after the slot reservation
+            pipe.enqueue([(sids[0], 0, CHUNK)], kv_caches[0], bad, "c")
+        assert sids[0] not in store._entries
+        assert store.committed_entries == 1 and store.arena.used_slots == 1  # one evicted for it
+        assert pipe.kernel_events == []
+    finally:
+        connector.close()
