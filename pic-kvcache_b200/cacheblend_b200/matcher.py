@@ -15,6 +15,7 @@ leftmost-greedy, non-overlapping, with exact token verification.
 
 from __future__ import annotations
 
+import array
 import functools
 import threading
 from collections import defaultdict
@@ -133,7 +134,7 @@ class TokenRangeMatcher:
         span = tokens[first_start : first_start + count * width]
         if isinstance(span, list):
             # a list of ints (vLLM's token ids): the record tuples are list slices
-            rows = np.fromiter(span, dtype=np.int64, count=len(span))
+            rows = np.frombuffer(array.array("q", span), dtype=np.int64)
         else:
             rows = np.asarray(span, dtype=np.int64)
         if rows.shape[0] != count * width:
