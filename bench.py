@@ -89,7 +89,9 @@ STORE_CONFIG = {"name": "qwen3-8b-store-64x8k", "layers": 36, "kv_heads": 8, "he
 CONFIGS = {
     1: Shape("qwen3-0.6b-cpu-plumbing", 28, 8, 16, 128, 4096, 256, 12, 16, 2048, 40960, 1e6, 1, 0.15),
     2: Shape("qwen3-8b-32k-kv_deviation", 36, 8, 32, 128, 32768, 256, 89, 16, 2304, 40960, 1e6, 1, 0.15),
-    4: Shape("qwen3-32b-64k-kv_deviation", 64, 8, 64, 128, 65536, 256, 192, 16, 4352, 40960, 1e6, 1, 0.15),
+    # a 64K prompt needs a RoPE table past Qwen3-32B's native 40,960 positions: vLLM builds
+    # 131,072 for the YaRN-extended (factor 4) context
+    4: Shape("qwen3-32b-64k-kv_deviation", 64, 8, 64, 128, 65536, 256, 192, 16, 4352, 131072, 1e6, 1, 0.15),
 }
 
 
@@ -97,6 +99,9 @@ def make_plan(shape: Shape, seed: int):
     """Seeded plan: reused chunks at random chunk slots, random source offsets."""
     from cacheblend_b200.types import BlendPlan, BlendSegment, SegmentId
 
+    if shape.tokens > shape.max_position:
+        # target rows past the RoPE table would be zero-filled (fail closed), not relocated
+        raise ValueError(f"{shape.name}: {shape.tokens} tokens exceed the RoPE table ({shape.max_position})")
     rng = np.random.default_rng(seed)
     chunks = shape.tokens // shape.chunk
     hits = np.sort(rng.choice(chunks, size=shape.hit_chunks, replace=False))
