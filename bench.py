@@ -6,10 +6,10 @@ One step = one blend request carried through every layer of the model:
 per layer the fused blend load (APC prefix gather + gap zeroing + RoPE
 relocation + placement of the reused chunks into staging), at the check layer
 the K-deviation score + recompute top-k, and the commit scatter of the
-recomputed span into vLLM pages.  Workload = BASELINE config 2 (Qwen3-8B
-shapes: 36 layers, 8 KV heads, head_dim 128, bf16, 32,768-token prompt in 128
-chunks of 256 with 89 reused chunks at random non-contiguous positions,
-block_size 16, kv_deviation at layer 1 with ratio 0.15).  Synthetic data
+recomputed span into vLLM pages.  Default workload: Qwen3-8B shapes (36
+layers, 8 KV heads, head_dim 128, bf16), a 32,768-token prompt in 128 chunks
+of 256 with 89 reused chunks at random non-contiguous positions, block_size
+16, kv_deviation at layer 1 with ratio 0.15.  Synthetic data
 (seeded N(0,1) bf16); the model math between load and commit is not part of
 the path and is not run.
 

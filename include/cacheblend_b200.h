@@ -13,7 +13,8 @@
  * `cb_last_error()` returns a thread-local message for the last failure on
  * the calling thread.  The library allocates no device or host memory and
  * keeps no global mutable state besides that per-thread string (and the
- * per-device address cache of cb_sparse_q_scores_static), so it is
+ * per-context caches of kernel attributes and of cb_sparse_q_scores_static's
+ * array address), so it is
  * re-entrant and may be called from several host threads on several streams.
  * Kernels run on the device that owns `stream`; for the legacy NULL stream,
  * on the device that holds the call's output buffer.
@@ -294,20 +295,24 @@ CB_API int cb_sparse_q_workspace_size(int64_t num_queries, int64_t num_q_heads,
  * query group head and sparse query i (query row query_rows[i] of `query`,
  * position query_positions[i]) the causal softmax over keys 0..position of
  * round_dtype(q . k) * scale is added into scores[key] (fp32, [num_keys]).
- * query: [tokens, num_q_heads, 128] rows `query_token_stride` bytes apart;
- * key: [num_keys, num_kv_heads, 128] rows `key_token_stride` bytes apart.
- * Positions must lie in [0, num_keys).  Runs on the tcgen05 tensor cores in
- * two passes (row log-sum-exp, then per-key mass); `workspace` (1 KiB
+ * query: [num_query_tokens, num_q_heads, 128] rows `query_token_stride` bytes
+ * apart; key: [num_keys, num_kv_heads, 128] rows `key_token_stride` bytes
+ * apart.  query_rows and query_positions are device int64 [num_queries].  A
+ * position >= num_keys sees every key (the reference's mask); a query row
+ * outside [0, num_query_tokens) or a negative position is not read, adds
+ * nothing and stores code 4 into *device_error.  Runs on the tcgen05 tensor
+ * cores in two passes (row log-sum-exp, then per-key mass); `workspace` (1 KiB
  * aligned, device memory, cb_sparse_q_workspace_size bytes) holds the
  * intermediate state.  Pipeline waits are bounded (2 s); a timeout stores a
- * nonzero code into *device_error (nullable).
+ * nonzero code (1-3) into *device_error (nullable).
  */
-CB_API int cb_sparse_q_scores(const void* query, int64_t query_token_stride, const void* key,
-                       int64_t key_token_stride, int64_t num_keys, int64_t num_q_heads,
-                       int64_t num_kv_heads, int64_t head_size, int dtype,
-                       const int64_t* query_rows, const int64_t* query_positions,
-                       int64_t num_queries, float scale, float* scores, void* workspace,
-                       int64_t workspace_bytes, int32_t* device_error, void* stream);
+CB_API int cb_sparse_q_scores(const void* query, int64_t query_token_stride,
+                              int64_t num_query_tokens, const void* key,
+                              int64_t key_token_stride, int64_t num_keys, int64_t num_q_heads,
+                              int64_t num_kv_heads, int64_t head_size, int dtype,
+                              const int64_t* query_rows, const int64_t* query_positions,
+                              int64_t num_queries, float scale, float* scores, void* workspace,
+                              int64_t workspace_bytes, int32_t* device_error, void* stream);
 
 /*
  * cb_sparse_q_scores without a workspace argument.  No counterpart in the
@@ -317,19 +322,24 @@ CB_API int cb_sparse_q_scores(const void* query, int64_t query_token_stride, con
  * allocator -- the workspace is a 32 MiB array inside this library (one per
  * GPU that loads it, held until the process exits); the function allocates
  * nothing.  Requests whose workspace (cb_sparse_q_workspace_size) exceeds
- * 32 MiB - 1 KiB are rejected with CB_ERR_INVALID.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress); make that first
- * call before any stream capture.  All calls on a device share the array:
- * calls whose executions overlap on the GPU race and must be serialized (one
- * stream, or events).  Nothing in the array needs to start at zero: every call
- * rewrites the parts it reads.
+ * 32 MiB - 1 KiB are rejected with CB_ERR_INVALID.  The array's device address
+ * is looked up (cudaGetSymbolAddress) on every call made outside a stream
+ * capture and recorded per CUDA context; a call inside a capture uses the
+ * recorded address, so make one call on EACH device (each context) outside
+ * capture before capturing there -- otherwise the captured call returns
+ * CB_ERR_INVALID.  All calls on a device share the array: calls whose
+ * executions overlap on the GPU race and must be serialized (one stream, or
+ * events).  Nothing in the array needs to start at zero: every call rewrites
+ * the parts it reads.
  */
 CB_API int cb_sparse_q_scores_static(const void* query, int64_t query_token_stride,
-                              const void* key, int64_t key_token_stride, int64_t num_keys,
-                              int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
-                              int dtype, const int64_t* query_rows,
-                              const int64_t* query_positions, int64_t num_queries, float scale,
-                              float* scores, int32_t* device_error, void* stream);
+                                     int64_t num_query_tokens, const void* key,
+                                     int64_t key_token_stride, int64_t num_keys,
+                                     int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                     int dtype, const int64_t* query_rows,
+                                     const int64_t* query_positions, int64_t num_queries,
+                                     float scale, float* scores, int32_t* device_error,
+                                     void* stream);
 
 #ifdef __cplusplus
 }

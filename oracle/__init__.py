@@ -295,6 +295,43 @@ def sparse_q_masks(gap_mask: np.ndarray, block_size: int, overflow_blocks: int,
     return query, forced, not has_gap
 
 
+def sparse_q_key_mass(query: np.ndarray, key: np.ndarray, positions: np.ndarray, scale: float,
+                      chunk: int = 8, dtype: int = BF16) -> np.ndarray:
+    """Attention mass per key from the given queries (the loop of ascend.py:681-697), float64.
+
+    query [Q, Hq, D] (the sparse queries, in order) and key [N, Hkv, D] as fp32
+    arrays holding values of ``dtype``; positions [Q].  Per chunk of ``chunk`` queries
+    and per (KV head, group): logits = T(q . k) * fp32 scale (T = the matmul output
+    type, bf16 or fp16), keys after a query's
+    position masked (their exp is exactly 0, as exp(finfo.min - max) is in the
+    reference), fp32 softmax over the keys, summed per key.
+    """
+    q = np.asarray(query, dtype=np.float32)
+    pos = np.asarray(positions, dtype=np.int64)
+    heads, kv_heads = q.shape[1], key.shape[1]
+    if heads % kv_heads:
+        raise ValueError("query heads must be divisible by KV heads")
+    groups = heads // kv_heads
+    keys = np.asarray(key, dtype=np.float32)
+    total = np.zeros(key.shape[0], dtype=np.float64)
+    scale32 = np.float32(scale)
+    for start in range(0, q.shape[0], chunk):
+        stop = min(start + chunk, q.shape[0])
+        limit = int(pos[start:stop].max()) + 1
+        masked = pos[start:stop, None] < np.arange(limit)[None, :]
+        block = np.zeros(limit, dtype=np.float64)
+        for h in range(kv_heads):
+            k_h = keys[:limit, h, :]  # [limit, D]
+            for g in range(groups):
+                logits = _round_to(q[start:stop, h * groups + g, :] @ k_h.T, dtype) * scale32
+                logits[masked] = -np.inf
+                e = np.exp(logits - logits.max(axis=1, keepdims=True), dtype=np.float32)
+                probs = e / e.sum(axis=1, keepdims=True, dtype=np.float32)
+                block += probs.sum(axis=0, dtype=np.float64)
+        total[:limit] += block
+    return total
+
+
 def sparse_q_scores(query: np.ndarray, key: np.ndarray, absolute: np.ndarray,
                     gap_mask: np.ndarray, scale: float, block_size: int, overflow_blocks: int,
                     tail_query_tokens: int, chunk: int = 8,
@@ -302,38 +339,16 @@ def sparse_q_scores(query: np.ndarray, key: np.ndarray, absolute: np.ndarray,
     """Sparse-Q attention mass per key (ascend.py:638-711), numpy fp32.
 
     query [A, Hq, D] and key [N, Hkv, D] as fp32 arrays holding bf16 values.
-    Logits are rounded to bf16 (torch bf16 matmul output) before the fp32
-    scale; masked logits are dropped (exp(finfo.min - max) == 0).  Returns the
-    per-active-token scores (or the full per-key vector when ``full``).
+    Queries are the gap tokens (or the tail, ascend.py:652-673); their mass per
+    key comes from ``sparse_q_key_mass``.  Returns the per-active-token scores
+    (or the full per-key vector when ``full``), the forced mask and the stats.
     """
     query_mask, forced, tail_fallback = sparse_q_masks(
         gap_mask, block_size, overflow_blocks, tail_query_tokens
     )
     rows = np.flatnonzero(query_mask)
-    q = query[rows].astype(np.float32)
     pos = np.asarray(absolute, dtype=np.int64)[rows]
-    heads, kv_heads = query.shape[1], key.shape[1]
-    if heads % kv_heads:
-        raise ValueError("query heads must be divisible by KV heads")
-    groups = heads // kv_heads
-    keys = key.astype(np.float32)
-    total = np.zeros(key.shape[0], dtype=np.float64)
-    scale32 = np.float32(scale)
-    for start in range(0, rows.shape[0], chunk):
-        stop = min(start + chunk, rows.shape[0])
-        limit = int(pos[start:stop].max()) + 1
-        block = np.zeros(limit, dtype=np.float64)
-        for h in range(kv_heads):
-            k_h = keys[:limit, h, :]  # [limit, D]
-            for g in range(groups):
-                q_hg = q[start:stop, h * groups + g, :]  # [c, D]
-                logits = round_bf16(q_hg @ k_h.T) * scale32  # fp32
-                for r in range(stop - start):
-                    valid = int(pos[start + r]) + 1
-                    row = logits[r, :valid].astype(np.float32)
-                    e = np.exp(row - row.max(), dtype=np.float32)
-                    block[:valid] += (e / e.sum(dtype=np.float32)).astype(np.float64)
-        total[:limit] += block
+    total = sparse_q_key_mass(query[rows], key, pos, scale, chunk)
     stats = {
         "active_tokens": int(query.shape[0]),
         "gap_tokens": int(np.sum(gap_mask)),

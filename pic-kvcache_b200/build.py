@@ -45,7 +45,8 @@ def sources() -> list[Path]:
 
 
 def _inputs() -> list[Path]:
-    return sources() + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h")) + [Path(__file__)]
+    return (sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
+            + [Path(__file__)])
 
 
 def up_to_date() -> bool:

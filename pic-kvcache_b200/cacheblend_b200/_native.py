@@ -21,7 +21,7 @@ LIB_PATH = Path(
     os.environ.get("CACHEBLEND_B200_LIB")
     or Path(__file__).resolve().parent / "_lib" / "libcacheblend_b200.so"
 )
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 CB_OK = 0
 CB_ERR_INVALID = -1
@@ -110,12 +110,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "cb_sparse_q_workspace_size": (_i32, [_i64, _i64, _i64, _i64, _i32, _ptr]),
     "cb_sparse_q_scores": (
         _i32,
-        [_ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _ptr, _i64,
+        [_ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _ptr, _i64,
          ctypes.c_float, _ptr, _ptr, _i64, _ptr, _ptr],
     ),
     "cb_sparse_q_scores_static": (
         _i32,
-        [_ptr, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _ptr, _i64,
+        [_ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i64, _i64, _i32, _ptr, _ptr, _i64,
          ctypes.c_float, _ptr, _ptr, _ptr],
     ),
 }

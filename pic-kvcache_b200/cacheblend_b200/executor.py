@@ -1,253 +1,331 @@
-"""Layerwise side executor for Qwen3 with the hot-path seams on B200 kernels.
+"""Layerwise side executor: drives one blend request through the local Qwen3
+layers and hands the CacheBlend work to the sm_100a seams.
 
-Control flow follows Qwen3BlendExecutor (cacheblend_vllm/ascend.py:410-846):
-embed the span, then per layer get the loader's staging (old K/V), run the
-model's norms / qkv / q-k norm + RoPE, at check layers score and select the
-tokens to recompute, prune, write the fresh K/V into the staging, attend,
-o_proj + MLP, and commit the staging back into vLLM's pages.  The model math
-is vLLM's own modules; the CacheBlend work -- staging load, K-deviation,
-Sparse-Q scoring, top-k selection (with the TP all-reduce) and the commit --
-runs on the sm_100a kernels through ``cacheblend_b200``.
+Behaviour kept from Qwen3BlendExecutor (cacheblend_vllm/ascend.py:410-846):
+per layer the loader's staging ([2, allocation_end, H, D], old K/V) is taken,
+the rows still being computed are projected with the model's own modules
+(input norm, qkv, q/k norm, RoPE), check layers score and prune them, the rows'
+fresh K/V overwrite the staging, the rows attend over the whole staging, then
+o_proj, post-attention norm and MLP run and the staging is committed back to
+vLLM's pages.  Strategies at a check layer:
+
+* ``kv_deviation`` -- prune before the layer's attention by K-deviation
+  (ascend.py:534-543, 600-609);
+* ``sparse_q`` -- score the gap queries against the staged keys with the fresh
+  keys written in place, attend with every row, prune after the MLP
+  (ascend.py:545-566, 618-630);
+* ``compare`` -- prune by K-deviation and trace the overlap of both selections
+  (ascend.py:568-577).
+
+How it is organised here: a layer is four stages over a ``_Rows`` bundle
+(``_project`` -> ``_choose`` -> ``_stage_and_attend`` -> ``_feed_forward``),
+each stage a call into vLLM's modules or one ``cacheblend_b200`` entry point
+(``kv_deviation``, ``sparse_q_scores``, ``select_tokens``, ``blend_attention``).
+The gap mask stays on the host, and the absolute rows are mirrored there while
+they are a plain range (before any pruning), so the check layer's masks and
+budgets need no device read.
 """
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import numpy as np
 import torch
 
-import os
-
 from .attention import attention_supported, attention_workspace_bytes, blend_attention
 from .config import CacheBlendConfig
-from .loader import PagedBlendLoader
 from .rope import validate_rope_support
 from .selection import kv_deviation, select_tokens, selection_overlap, sparse_q_scores
 from .trace import PipelineTracer
 from .types import BlendPlan
 
-
 # CACHEBLEND_B200_ATTENTION=fused: fp32 logits like the reference's fused NPU attention
 # (ascend.py:814-830) instead of the einsum path's element-type roundings (the default,
-# which is what the reference runs on a CUDA device).
+# which is what the reference computes on a CUDA device).
 _FUSED_ATTENTION = os.environ.get("CACHEBLEND_B200_ATTENTION", "").lower() == "fused"
 
+_EMBEDDING_HOOKS = ("get_input_embeddings", "embed_input_ids")
 
-def _embed(model, input_ids: torch.Tensor) -> torch.Tensor:
-    if hasattr(model, "get_input_embeddings"):
-        embeddings = model.get_input_embeddings()
-        if callable(embeddings):
-            return embeddings(input_ids)
-    if hasattr(model, "embed_input_ids"):
-        return model.embed_input_ids(input_ids)
-    if hasattr(model.model, "embed_tokens"):
-        return model.model.embed_tokens(input_ids)
-    raise AttributeError(f"{type(model).__name__} has no supported embedding API")
+
+def _token_embeddings(model, token_ids: torch.Tensor) -> torch.Tensor:
+    """Embeddings of ``token_ids`` through whichever hook this vLLM model exposes."""
+    getter = getattr(model, "get_input_embeddings", None)
+    if getter is not None:
+        table = getter()
+        if callable(table):
+            return table(token_ids)
+    embed = getattr(model, "embed_input_ids", None)
+    if embed is not None:
+        return embed(token_ids)
+    inner = getattr(model.model, "embed_tokens", None)
+    if inner is not None:
+        return inner(token_ids)
+    raise AttributeError(f"{type(model).__name__} exposes none of {_EMBEDDING_HOOKS} or embed_tokens")
+
+
+def _tensor_parallel_group():
+    """vLLM's TP group coordinator, or None outside a vLLM worker."""
+    try:
+        from vllm.distributed.parallel_state import get_tp_group
+
+        return get_tp_group()
+    except (AssertionError, ImportError):
+        return None
 
 
 @dataclass(slots=True)
 class BlendExecutionState:
+    """Per-request state carried from layer to layer.
+
+    ``important_indices``: rows (relative to ``compute_start``) still computed,
+    None while every row is; ``positions``: their token positions;
+    ``gap_mask``: host bool [allocation_end]; ``attention_mask``: cached mask
+    of the torch attention fallback."""
+
     compute_start: int
     positions: torch.Tensor
-    gap_mask: np.ndarray  # host copy: [allocation_end]
+    gap_mask: np.ndarray
     important_indices: torch.Tensor | None = None
     attention_mask: torch.Tensor | None = None
 
 
+@dataclass(slots=True)
+class _Rows:
+    """One layer's tensors for the rows it computes, row-aligned."""
+
+    q: torch.Tensor
+    k: torch.Tensor
+    v: torch.Tensor
+    residual: torch.Tensor
+    relative: torch.Tensor  # row ids relative to compute_start (device, int64)
+    positions: torch.Tensor
+    absolute: torch.Tensor  # staging rows = compute_start + relative
+    absolute_host: np.ndarray | None  # host mirror when known without a device read
+
+    def keep(self, chosen: torch.Tensor) -> _Rows:
+        return _Rows(self.q[chosen], self.k[chosen], self.v[chosen], self.residual[chosen],
+                     self.relative[chosen], self.positions[chosen], self.absolute[chosen], None)
+
+    def host_absolute(self) -> np.ndarray:
+        if self.absolute_host is None:  # rows pruned by an earlier check layer: one read
+            self.absolute_host = self.absolute.detach().to("cpu").numpy()
+        return self.absolute_host
+
+    def span(self) -> slice | None:
+        """The staging rows as one slice when they are a plain ascending range."""
+        host = self.absolute_host
+        if host is None or host.size == 0:
+            return None
+        first = int(host[0])
+        return slice(first, first + host.size) if int(host[-1]) == first + host.size - 1 else None
+
+
+@dataclass(slots=True)
+class _Choice:
+    """What a check layer decided: rows to keep before attention / after the MLP."""
+
+    before_attention: torch.Tensor | None = None
+    after_feed_forward: torch.Tensor | None = None
+    stats: dict | None = None
+
+
+def _overwrite_rows(plane: torch.Tensor, rows: _Rows, values: torch.Tensor) -> None:
+    """plane[absolute rows] = values (a plain copy when the rows are a range)."""
+    where = rows.span()
+    if where is not None:
+        plane[where].copy_(values)
+    else:
+        plane[rows.absolute] = values
+
+
 class Qwen3BlendExecutor:
+    """Runs the blend span through this rank's decoder layers, one layer at a time."""
+
     def __init__(self, model, config: CacheBlendConfig, block_size: int):
-        self.model = model
-        self.config = config
         if block_size <= 0:
             raise ValueError("vLLM KV cache block_size must be positive")
-        self.block_size = block_size
-        self.layers = list(model.model.layers[model.model.start_layer : model.model.end_layer])
-        if not self.layers:
+        inner = model.model
+        layers = list(inner.layers[inner.start_layer : inner.end_layer])
+        if not layers:
             raise RuntimeError("Qwen3 model has no local decoder layers")
-        if max(config.check_layers) >= len(self.layers):
+        if max(config.check_layers) >= len(layers):
             raise ValueError(
                 "CacheBlend check layer exceeds the local Qwen3 layer range: "
-                f"check_layers={config.check_layers}, layers={len(self.layers)}"
+                f"check_layers={config.check_layers}, layers={len(layers)}"
             )
-        validate_rope_support(model, self.layers[0].self_attn.rotary_emb)
-        try:
-            from vllm.distributed.parallel_state import get_tp_group
+        validate_rope_support(model, layers[0].self_attn.rotary_emb)
+        self.model = model
+        self.config = config
+        self.block_size = block_size
+        self.layers = layers
+        self.tp_group = _tensor_parallel_group()
 
-            self.tp_group = get_tp_group()
-        except (AssertionError, ImportError):
-            self.tp_group = None
-
-    # ------------------------------------------------------------------ run
-    def run(self, request_id: str, tokens: list[int], plan: BlendPlan, loader: PagedBlendLoader) -> None:
-        if plan.allocation_end <= plan.apc_prefix_tokens:
+    # ------------------------------------------------------------------ request
+    def run(self, request_id: str, tokens: list[int], plan: BlendPlan, loader) -> None:
+        """Layerwise pass over ``[apc_prefix, allocation_end)`` with the loader's
+        prefetch(l + 1) overlapping layer l (ascend.py:433-485)."""
+        first, end = plan.apc_prefix_tokens, plan.allocation_end
+        if end <= first:
             return
-        device = loader.kv_caches[0].device if isinstance(loader.kv_caches[0], torch.Tensor) \
-            else loader.kv_caches[0][0].device
-        input_ids = torch.tensor(
-            tokens[plan.apc_prefix_tokens : plan.allocation_end], dtype=torch.long, device=device
-        )
-        hidden_states = _embed(self.model, input_ids)
+        cache = loader.kv_caches[0]
+        device = (cache if isinstance(cache, torch.Tensor) else cache[0]).device
+        hidden = _token_embeddings(self.model, torch.tensor(tokens[first:end], dtype=torch.long,
+                                                              device=device))
+        state = BlendExecutionState(first, torch.arange(first, end, device=device), plan.gap_mask())
         residual = None
-        positions = torch.arange(plan.apc_prefix_tokens, plan.allocation_end, device=device)
-        state = BlendExecutionState(plan.apc_prefix_tokens, positions, plan.gap_mask())
+        depth = len(self.layers)
+        tracer = loader.tracer
         loader.prefetch(0, self.layers[0].self_attn.rotary_emb)
-        for layer_id, layer in enumerate(self.layers):
-            old_kv = loader.get(layer_id)
-            if layer_id + 1 < len(self.layers):
-                loader.prefetch(layer_id + 1, self.layers[layer_id + 1].self_attn.rotary_emb)
-            hidden_states, residual, state, old_kv = self._compute_layer(
-                layer_id, layer, hidden_states, residual, state, old_kv,
-                request_id=request_id, tracer=loader.tracer,
-            )
-            if loader.tracer is not None and loader.tracer.enabled:
-                loader.tracer.emit(
-                    "layer_compute_enqueued",
-                    request_id=request_id,
-                    layer_id=layer_id,
-                    computed_tokens=int(hidden_states.shape[0]),
-                    check_layer=layer_id in self.config.check_layers,
-                )
-            loader.commit(layer_id, old_kv)
+        for index in range(depth):
+            staging = loader.get(index)
+            if index + 1 < depth:
+                loader.prefetch(index + 1, self.layers[index + 1].self_attn.rotary_emb)
+            hidden, residual, state, staging = self._compute_layer(
+                index, self.layers[index], hidden, residual, state, staging,
+                request_id=request_id, tracer=tracer)
+            _emit(tracer, "layer_compute_enqueued", request_id, layer_id=index,
+                  computed_tokens=int(hidden.shape[0]), check_layer=index in self.config.check_layers)
+            loader.commit(index, staging)
 
-    def _compute_layer(self, layer_id, layer, hidden_states, residual, state, old_kv,
-                       request_id=None, tracer: PipelineTracer | None = None):
+    # -------------------------------------------------------------------- layer
+    def _compute_layer(self, layer_id: int, layer, hidden_states: torch.Tensor,
+                       residual: torch.Tensor | None, state: BlendExecutionState,
+                       old_kv: torch.Tensor, request_id: str | None = None,
+                       tracer: PipelineTracer | None = None):
+        """One decoder layer over the computed rows; returns (hidden, residual, state, staging)."""
+        rows = self._project(layer, hidden_states, residual, state)
+        choice = self._choose(layer_id, layer, rows, state, old_kv, request_id, tracer)
+        if choice.before_attention is not None:
+            rows = rows.keep(choice.before_attention)
+            _narrow(state, rows.relative, rows.positions)
+        attended = self._stage_and_attend(layer, rows, old_kv, state)
+        hidden, residual = self._feed_forward(layer, attended, rows.residual)
+        if choice.after_feed_forward is not None:
+            chosen = choice.after_feed_forward
+            hidden, residual = hidden[chosen], residual[chosen]
+            _narrow(state, rows.relative[chosen], rows.positions[chosen])
+            _emit(tracer, "selection_finished", request_id, layer_id=layer_id, strategy="sparse_q",
+                  selected_tokens=int(chosen.numel()), **(choice.stats or {}))
+        return hidden, residual, state, old_kv
+
+    def _project(self, layer, hidden: torch.Tensor, residual: torch.Tensor | None,
+                 state: BlendExecutionState) -> _Rows:
+        """Input norm (fused with the residual add after the first layer), qkv
+        projection, per-head q/k norm and RoPE at the rows' positions."""
         if residual is None:
-            residual = hidden_states
-            hidden_states = layer.input_layernorm(hidden_states)
+            residual, hidden = hidden, layer.input_layernorm(hidden)
         else:
-            hidden_states, residual = layer.input_layernorm(hidden_states, residual)
-        qkv, _ = layer.self_attn.qkv_proj(hidden_states)
-        q, k, v = qkv.split(
-            [layer.self_attn.q_size, layer.self_attn.kv_size, layer.self_attn.kv_size], dim=-1
-        )
-        query_indices = (
-            torch.arange(q.shape[0], device=q.device)
-            if state.important_indices is None
-            else state.important_indices
-        )
-        absolute_indices = state.compute_start + query_indices
-        q, k = self._qk_post_process(layer.self_attn, state.positions, q, k)
-        flat_old_k = old_kv[0].reshape(old_kv.shape[1], -1)
-        flat_old_v = old_kv[1].reshape(old_kv.shape[1], -1)
-        check_layer = layer_id in self.config.check_layers
+            hidden, residual = layer.input_layernorm(hidden, residual)
+        attn = layer.self_attn
+        qkv, _ = attn.qkv_proj(hidden)
+        q, k, v = qkv.split([attn.q_size, attn.kv_size, attn.kv_size], dim=-1)
+        width = attn.head_dim
+        q = attn.q_norm(q.reshape(q.shape[0], -1, width)).reshape(q.shape)
+        k = attn.k_norm(k.reshape(k.shape[0], -1, width)).reshape(k.shape)
+        q, k = attn.rotary_emb(state.positions, q, k)
+        count = q.shape[0]
+        if state.important_indices is None:
+            relative = torch.arange(count, device=q.device)
+            host = np.arange(state.compute_start, state.compute_start + count, dtype=np.int64)
+        else:
+            relative, host = state.important_indices, None
+        return _Rows(q, k, v, residual, relative, state.positions, state.compute_start + relative, host)
+
+    def _choose(self, layer_id: int, layer, rows: _Rows, state: BlendExecutionState,
+                staging: torch.Tensor, request_id, tracer) -> _Choice:
+        """Scores and selections of a check layer (nothing elsewhere)."""
+        if layer_id not in self.config.check_layers:
+            return _Choice()
         strategy = self.config.selection_strategy
-        deviation_selected = sparse_q_selected = None
-        stats: dict = {}
-        if check_layer:
-            abs_host = absolute_indices.detach().to("cpu").numpy()
-            active_gap_mask = state.gap_mask[abs_host]
-        if check_layer and strategy in {"kv_deviation", "compare"}:
-            scores = kv_deviation(k, flat_old_k, absolute_indices)
-            deviation_selected = self._select(scores, active_gap_mask, layer_id)
-        if check_layer and strategy in {"sparse_q", "compare"}:
+        gaps = state.gap_mask[rows.host_absolute()]
+        cached_k = staging[0].view(staging.shape[1], -1)  # a view: sparse_q writes through it
+        choice = _Choice()
+        by_deviation = by_query = None
+        if strategy in ("kv_deviation", "compare"):
+            deviation = kv_deviation(rows.k, cached_k, rows.absolute)
+            by_deviation = self._select(deviation, gaps, layer_id)
+            choice.before_attention = by_deviation
+        if strategy in ("sparse_q", "compare"):
             attn = layer.self_attn.attn
-            score_keys = flat_old_k if strategy == "sparse_q" else flat_old_k.clone()
-            score_keys[absolute_indices] = k
-            scores, forced, stats = self._sparse_q_scores(
-                q.view(-1, int(attn.num_heads), int(attn.head_size)),
-                score_keys.view(-1, int(attn.num_kv_heads), int(attn.head_size)),
-                abs_host,
-                active_gap_mask,
-                float(attn.impl.scale),
-            )
-            sparse_q_selected = self._select(scores, active_gap_mask, layer_id, forced_mask=forced)
-        if check_layer and strategy == "compare" and tracer is not None and tracer.enabled:
-            overlap, union = selection_overlap(deviation_selected, sparse_q_selected)
-            tracer.emit("selection_compared", request_id=request_id, layer_id=layer_id,
-                        deviation_tokens=deviation_selected.numel(),
-                        sparse_q_tokens=sparse_q_selected.numel(), overlap_tokens=overlap,
-                        jaccard=overlap / max(union, 1), **stats)
-        if check_layer and strategy in {"kv_deviation", "compare"}:
-            selected = deviation_selected
-            q, k, v = q[selected], k[selected], v[selected]
-            residual = residual[selected]
-            query_indices = query_indices[selected]
-            absolute_indices = state.compute_start + query_indices
-            state.important_indices = query_indices
-            state.positions = state.positions[selected]
-            state.attention_mask = None
-        flat_old_k[absolute_indices] = k
-        flat_old_v[absolute_indices] = v
+            # the boundary score sees the fresh keys of the computed rows; in
+            # sparse_q mode they are written into the staging itself (the
+            # write-back below stores the same values), in compare mode into a copy
+            keys = cached_k if strategy == "sparse_q" else cached_k.clone()
+            _overwrite_rows(keys, rows, rows.k)
+            heads, kv_heads, head = int(attn.num_heads), int(attn.num_kv_heads), int(attn.head_size)
+            scores, forced, stats = sparse_q_scores(
+                rows.q.view(-1, heads, head), keys.view(-1, kv_heads, head), rows.host_absolute(),
+                gaps, float(attn.impl.scale), self.block_size, self.config.overflow_blocks,
+                self.config.tail_query_tokens)
+            by_query = self._select(scores, gaps, layer_id, forced_mask=forced)
+            choice.stats = stats
+            if strategy == "sparse_q":
+                choice.after_feed_forward = by_query
+        if strategy == "compare" and tracer is not None and tracer.enabled:
+            overlap, union = selection_overlap(by_deviation, by_query)
+            _emit(tracer, "selection_compared", request_id, layer_id=layer_id,
+                  deviation_tokens=by_deviation.numel(), sparse_q_tokens=by_query.numel(),
+                  overlap_tokens=overlap, jaccard=overlap / max(union, 1), **choice.stats)
+        return choice
+
+    def _select(self, scores: torch.Tensor, gaps: np.ndarray, layer_id: int,
+                forced_mask=None) -> torch.Tensor:
+        """TP-summed, budgeted top-k united with the gap (and forced) rows (ascend.py:757-796)."""
+        return select_tokens(scores, gaps, self.config.ratio_for_layer(layer_id), forced_mask,
+                             tp_group=self.tp_group, global_selection=self.config.tp_global_selection)
+
+    def _stage_and_attend(self, layer, rows: _Rows, staging: torch.Tensor,
+                          state: BlendExecutionState) -> torch.Tensor:
+        """Fresh K/V of the computed rows into the staging, then their attention over it."""
+        plane_rows = staging.shape[1]
+        _overwrite_rows(staging[0].view(plane_rows, -1), rows, rows.k)
+        _overwrite_rows(staging[1].view(plane_rows, -1), rows, rows.v)
         attn = layer.self_attn.attn
-        num_heads, num_kv_heads, head_size = int(attn.num_heads), int(attn.num_kv_heads), int(attn.head_size)
-        attn_output = self._attention(
-            q.view(-1, num_heads, head_size),
-            old_kv[0].view(-1, num_kv_heads, head_size),
-            old_kv[1].view(-1, num_kv_heads, head_size),
-            absolute_indices,
-            float(attn.impl.scale),
-            state,
-        ).reshape(-1, num_heads * head_size)
-        hidden_states, _ = layer.self_attn.o_proj(attn_output)
-        hidden_states, residual = layer.post_attention_layernorm(hidden_states, residual)
-        hidden_states = layer.mlp(hidden_states)
-        if check_layer and strategy == "sparse_q":
-            hidden_states = hidden_states[sparse_q_selected]
-            residual = residual[sparse_q_selected]
-            query_indices = query_indices[sparse_q_selected]
-            state.important_indices = query_indices
-            state.positions = state.positions[sparse_q_selected]
-            state.attention_mask = None
-            if tracer is not None and tracer.enabled:
-                tracer.emit("selection_finished", request_id=request_id, layer_id=layer_id,
-                            strategy="sparse_q", selected_tokens=int(sparse_q_selected.numel()), **stats)
-        return hidden_states, residual, state, old_kv
+        heads, kv_heads, head = int(attn.num_heads), int(attn.num_kv_heads), int(attn.head_size)
+        out = self._attend(rows.q.view(-1, heads, head), staging[0].view(-1, kv_heads, head),
+                           staging[1].view(-1, kv_heads, head), rows.absolute, float(attn.impl.scale),
+                           state)
+        return out.reshape(-1, heads * head)
 
-    # ------------------------------------------------------------- seams
-    def _sparse_q_scores(self, query, key, absolute_indices, gap_mask, scale):
-        """Per-active-token Sparse-Q scores, forced mask and stats (ascend.py:638-711)."""
-        return sparse_q_scores(
-            query, key, absolute_indices, gap_mask, scale, self.block_size,
-            self.config.overflow_blocks, self.config.tail_query_tokens,
-        )
+    def _feed_forward(self, layer, attended: torch.Tensor, residual: torch.Tensor):
+        hidden, _ = layer.self_attn.o_proj(attended)
+        hidden, residual = layer.post_attention_layernorm(hidden, residual)
+        return layer.mlp(hidden), residual
 
-    def _select(self, scores, gap_mask, layer_id=None, forced_mask=None) -> torch.Tensor:
-        """TP-reduced, budgeted top-k union with gaps/forced (ascend.py:757-796)."""
-        return select_tokens(
-            scores,
-            gap_mask,
-            self.config.ratio_for_layer(layer_id),
-            forced_mask,
-            tp_group=self.tp_group,
-            global_selection=self.config.tp_global_selection,
-        )
-
-    @staticmethod
-    def _qk_post_process(attn_layer, positions, q, k):
-        q_heads = q.view(*q.shape[:-1], q.shape[-1] // attn_layer.head_dim, attn_layer.head_dim)
-        q = attn_layer.q_norm(q_heads).view(q.shape)
-        k_heads = k.view(*k.shape[:-1], k.shape[-1] // attn_layer.head_dim, attn_layer.head_dim)
-        k = attn_layer.k_norm(k_heads).view(k.shape)
-        return attn_layer.rotary_emb(positions, q, k)
-
-    def _attention(self, query, key, value, q_positions, scale, state: BlendExecutionState):
-        """Causal attention of the computed queries over the whole staging context
-        (ascend.py:798-846).  Head size 128 in bf16 / fp16 with query groups
-        dividing 128 (every Qwen3 configuration) runs the tcgen05 kernel; other
-        shapes use torch's SDPA with the same mask."""
+    def _attend(self, query, key, value, positions, scale: float, state: BlendExecutionState):
+        """Causal attention of the computed queries over the whole staging
+        (ascend.py:798-846): the tcgen05 kernel for head size 128 in bf16/fp16
+        with query groups dividing 128 (every Qwen3 shape), torch SDPA with the
+        same mask otherwise."""
         if query.device.type == "cuda" and attention_supported(query, key):
-            need = attention_workspace_bytes(query.shape[0], key.shape[0], query.shape[1],
-                                             key.shape[1], query.shape[2], query.dtype)
-            workspace = getattr(self, "_attention_workspace", None)
-            if workspace is None or workspace.numel() < need or workspace.device != query.device:
-                workspace = torch.empty(need, dtype=torch.uint8, device=query.device)
-                self._attention_workspace = workspace
-            return blend_attention(query, key, value, q_positions, scale, workspace=workspace,
+            need = attention_workspace_bytes(query.shape[0], key.shape[0], query.shape[1], key.shape[1],
+                                             query.shape[2], query.dtype)
+            scratch = getattr(self, "_attention_scratch", None)
+            if scratch is None or scratch.numel() < need or scratch.device != query.device:
+                scratch = torch.empty(need, dtype=torch.uint8, device=query.device)
+                self._attention_scratch = scratch
+            return blend_attention(query, key, value, positions, scale, workspace=scratch,
                                    exact_rounding=not _FUSED_ATTENTION or scale <= 0)
-        k_positions = torch.arange(key.shape[0], device=query.device)
-        cache = self.config.cache_attention_mask and state.important_indices is not None
-        allowed = state.attention_mask if cache else None
-        if allowed is None:
-            allowed = q_positions[:, None] >= k_positions[None, :]
-            if cache:
-                state.attention_mask = allowed
+        reuse = self.config.cache_attention_mask and state.important_indices is not None
+        visible = state.attention_mask if reuse else None
+        if visible is None:
+            visible = positions[:, None] >= torch.arange(key.shape[0], device=query.device)[None, :]
+            if reuse:
+                state.attention_mask = visible
         out = torch.nn.functional.scaled_dot_product_attention(
-            query.transpose(0, 1)[None],
-            key.transpose(0, 1)[None],
-            value.transpose(0, 1)[None],
-            attn_mask=allowed[None, None],
-            scale=scale,
-            enable_gqa=query.shape[1] != key.shape[1],
-        )
+            query.transpose(0, 1)[None], key.transpose(0, 1)[None], value.transpose(0, 1)[None],
+            attn_mask=visible[None, None], scale=scale, enable_gqa=query.shape[1] != key.shape[1])
         return out[0].transpose(0, 1)
+
+
+def _narrow(state: BlendExecutionState, relative: torch.Tensor, positions: torch.Tensor) -> None:
+    state.important_indices = relative
+    state.positions = positions
+    state.attention_mask = None
+
+
+def _emit(tracer: PipelineTracer | None, event: str, request_id, **fields) -> None:
+    if tracer is not None and tracer.enabled:
+        tracer.emit(event, request_id=request_id, **fields)

@@ -11,6 +11,10 @@
 * ``sparse_q_masks`` -- query set, forced set and tail fallback of
   ``_sparse_q_scores`` (ascend.py:652-673); these depend only on the plan's
   gap mask, so they are computed on the host without a device round trip.
+
+Host arrays reach the device through pinned staging (``_upload``): a copy from
+pageable memory would wait for the stream, i.e. synchronise the host with the
+GPU in the middle of the scoring path.
 """
 
 from __future__ import annotations
@@ -21,6 +25,12 @@ import numpy as np
 import torch
 
 from . import _native
+
+
+def _upload(array: np.ndarray, device) -> torch.Tensor:
+    """Host array -> device tensor, asynchronously through pinned memory (torch's
+    pinned-memory cache keeps the staging alive until the copy has run)."""
+    return torch.from_numpy(np.ascontiguousarray(array)).pin_memory().to(device, non_blocking=True)
 
 
 def _as_host_mask(mask: torch.Tensor | np.ndarray, name: str) -> np.ndarray:
@@ -162,9 +172,7 @@ def select_tokens(
     base_count = int(base.sum())
     k = recompute_budget(active, int(gaps.sum()), base_count, ratio)
     if base_mask_device is None:
-        base_mask_device = torch.from_numpy(base.astype(np.uint8)).to(
-            scores.device, non_blocking=True
-        )
+        base_mask_device = _upload(base.astype(np.uint8), scores.device)
     return select_from_scores(scores.contiguous(), base_mask_device, k, base_count + k)
 
 
@@ -244,12 +252,13 @@ def sparse_q_key_mass(
     aligned = (base + 1023) // 1024 * 1024
     usable = workspace.numel() - (aligned - base)
     scores = torch.empty(num_keys, dtype=torch.float32, device=query.device)
-    rows_dev = torch.from_numpy(rows).to(query.device, non_blocking=True)
-    pos_dev = torch.from_numpy(positions).to(query.device, non_blocking=True)
+    rows_dev = _upload(rows, query.device)
+    pos_dev = _upload(positions, query.device)
     esize = query.element_size()
     _native.call(
         "cb_sparse_q_scores",
-        query.data_ptr(), query.stride(0) * esize, key.data_ptr(), key.stride(0) * esize, num_keys,
+        query.data_ptr(), query.stride(0) * esize, query.shape[0], key.data_ptr(), key.stride(0) * esize,
+        num_keys,
         num_q_heads, num_kv_heads, head, _native.dtype_code(query.dtype), rows_dev.data_ptr(),
         pos_dev.data_ptr(), rows.size, float(scale), scores.data_ptr(), aligned, usable,
         0 if device_error is None else device_error.data_ptr(), _native.stream_handle(stream),
@@ -268,15 +277,19 @@ def sparse_q_scores(
     tail_query_tokens: int,
     device_error: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, dict[str, int | bool]]:
-    """``_sparse_q_scores`` (ascend.py:638-711): scores of the active tokens, forced mask, stats.
+    """``_sparse_q_scores`` (ascend.py:638-711): scores of the active tokens (device
+    fp32), forced mask (host bool tensor), stats.
 
+    ``absolute_indices`` and ``gap_mask`` are best given as host arrays (the
+    executor keeps them there): the query rows, forced mask and budgets then
+    come from host data, and the scoring enqueues without any device read.
     ``query_score_chunk_size`` only bounded the reference's temporary tensor;
     the tensor-core kernel streams keys through TMEM and never materialises a
     [queries, context] tensor, so it has no chunk parameter.
     """
     gaps = _as_host_mask(gap_mask, "gap_mask")
     absolute = (
-        absolute_indices.astype(np.int64, copy=False)
+        np.asarray(absolute_indices, dtype=np.int64)
         if isinstance(absolute_indices, np.ndarray)
         else absolute_indices.detach().to("cpu", torch.long).numpy()
     )
@@ -287,8 +300,11 @@ def sparse_q_scores(
     )
     rows = np.flatnonzero(query_mask)
     full = sparse_q_key_mass(query, key, rows, absolute[rows], scale, device_error=device_error)
-    index = torch.from_numpy(absolute).to(query.device, non_blocking=True)
-    scores = full.index_select(0, index)
+    count = absolute.shape[0]
+    if count and np.array_equal(absolute, np.arange(absolute[0], absolute[0] + count)):
+        scores = full[int(absolute[0]) : int(absolute[0]) + count]  # the span: a view, no gather
+    else:
+        scores = full.index_select(0, _upload(absolute, query.device))
     gap_count = int(gaps.sum())
     stats = {
         "active_tokens": int(query.shape[0]),
@@ -298,8 +314,7 @@ def sparse_q_scores(
         "tail_fallback": tail_fallback,
         "overflow_blocks": overflow_blocks,
     }
-    forced_dev = torch.from_numpy(forced).to(query.device, non_blocking=True)
-    return scores, forced_dev, stats
+    return scores, torch.from_numpy(forced), stats
 
 
 def selection_overlap(a: torch.Tensor, b: torch.Tensor) -> tuple[int, int]:

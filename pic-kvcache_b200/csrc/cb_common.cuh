@@ -24,7 +24,14 @@ int bind_stream(void* stream, const void* device_ptr);
 // Converts the launch status into CB_OK / CB_ERR_CUDA.
 int launch_status(const char* kernel);
 
-// Raises `func`'s dynamic shared memory limit on the current device to at
+// The CUDA context current on the calling thread (driver handle, fetched
+// through the runtime's driver entry point; no driver link).  Per-context
+// state -- a device symbol's address, a kernel's shared-memory attribute --
+// is keyed by this handle: a device ordinal can name several contexts over a
+// process's life (cudaDeviceReset, an FFI host with its own context).
+int current_context(void** context);
+
+// Raises `func`'s dynamic shared memory limit in the current context to at
 // least `bytes`.  The attribute is only changed when a launch needs more than
 // any earlier one, so steady-state calls (and calls inside a stream capture
 // after a warm-up launch) make no attribute change.

@@ -2,6 +2,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <cuda.h>  // CUcontext / CUresult only; the driver is reached through the runtime
+
 #include <map>
 #include <mutex>
 #include <utility>
@@ -70,19 +72,43 @@ int bind_stream(void* stream, const void* device_ptr) {
   return CB_OK;
 }
 
-int ensure_dynamic_smem(const void* func, size_t bytes) {
-  static std::mutex lock;
-  static std::map<std::pair<int, const void*>, size_t> granted;
-  int device = -1;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess) {
-    set_error("cudaGetDevice failed: %s", cudaGetErrorString(e));
+int current_context(void** context) {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  static const GetCurrent get = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult found;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<GetCurrent>(fn);
+  }();
+  if (get == nullptr) {
+    set_error("cuCtxGetCurrent is unavailable through the CUDA runtime");
     return CB_ERR_CUDA;
   }
+  CUcontext ctx = nullptr;
+  const CUresult r = get(&ctx);
+  if (r != CUDA_SUCCESS || ctx == nullptr) {
+    set_error("no current CUDA context on this thread (cuCtxGetCurrent: %d)", static_cast<int>(r));
+    return CB_ERR_CUDA;
+  }
+  *context = ctx;
+  return CB_OK;
+}
+
+int ensure_dynamic_smem(const void* func, size_t bytes) {
+  // Keyed by context, not device ordinal: a context created after
+  // cudaDeviceReset (or by another runtime) starts from the default limit.
+  static std::mutex lock;
+  static std::map<std::pair<void*, const void*>, size_t> granted;
+  void* context = nullptr;
+  const int rc = current_context(&context);
+  if (rc != CB_OK) return rc;
   std::lock_guard<std::mutex> guard(lock);
-  size_t& have = granted[std::make_pair(device, func)];
+  size_t& have = granted[std::make_pair(context, func)];
   if (bytes <= have) return CB_OK;
-  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute(%zu bytes) failed: %s", bytes, cudaGetErrorString(e));
     return CB_ERR_CUDA;
@@ -102,7 +128,7 @@ int launch_status(const char* kernel) {
 
 }  // namespace cb
 
-extern "C" int cb_abi_version(void) { return 1; }
+extern "C" int cb_abi_version(void) { return 2; }
 
 extern "C" const char* cb_last_error(void) { return cb::g_last_error; }
 

@@ -28,6 +28,7 @@
 #include <type_traits>
 
 #include "cb_common.cuh"
+#include "cb_context_cache.h"
 #include "cb_tcgen05.cuh"
 
 namespace cb {
@@ -586,16 +587,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ============================================================ prep
 // Dense per-KV-head query rows: qd[h][qi*groups+g][:] = query[rows[qi]][h*groups+g][:],
-// zero rows up to rows_pad; row positions; per-tile position bounds.
+// zero rows up to rows_pad; row positions; per-tile position bounds.  A query
+// row outside [0, query_tokens) or a negative position is not read: its rows
+// are zero and masked (position -1, they see no key) and code 4 is recorded in
+// *error.  A position past the last key sees every key, as the reference's
+// mask `pos_q < key_position` does, so it is clamped to num_keys - 1.
+__device__ __forceinline__ int query_position(const int64_t* rows, const int64_t* positions,
+                                              int64_t qi, int64_t query_tokens, int64_t num_keys) {
+  const int64_t row = rows[qi];
+  const int64_t pos = positions[qi];
+  if (row < 0 || row >= query_tokens || pos < 0) return -1;
+  return static_cast<int>(pos < num_keys ? pos : num_keys - 1);
+}
+
 __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ query,
-                                                   int64_t query_token_stride,
+                                                   int64_t query_token_stride, int64_t query_tokens,
                                                    const int64_t* __restrict__ rows,
                                                    const int64_t* __restrict__ positions,
-                                                   int64_t num_queries, int num_kv_heads, int groups,
+                                                   int64_t num_queries, int64_t num_keys,
+                                                   int num_kv_heads, int groups,
                                                    int rows_pad, int head_bytes, char* __restrict__ qd,
                                                    int32_t* __restrict__ row_pos,
                                                    int32_t* __restrict__ tile_max,
-                                                   int32_t* __restrict__ tile_min) {
+                                                   int32_t* __restrict__ tile_min,
+                                                   int32_t* __restrict__ error) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -607,14 +622,17 @@ __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ quer
     const int64_t qi = r / groups;
     const int g = r - static_cast<int>(qi) * groups;
     uint4* dst = reinterpret_cast<uint4*>(qd + task * head_bytes);
-    if (qi < num_queries) {
+    const int pos = qi < num_queries ? query_position(rows, positions, qi, query_tokens, num_keys) : -1;
+    if (pos >= 0) {
       const uint4* src = reinterpret_cast<const uint4*>(
           query + rows[qi] * query_token_stride + (int64_t)(h * groups + g) * head_bytes);
       for (int u = lane; u < units; u += 32) dst[u] = src[u];
     } else {
       for (int u = lane; u < units; u += 32) dst[u] = make_uint4(0, 0, 0, 0);
+      if (qi < num_queries && h == 0 && g == 0 && lane == 0 && error != nullptr)
+        atomicCAS(error, 0, 4);
     }
-    if (h == 0 && lane == 0) row_pos[r] = qi < num_queries ? static_cast<int32_t>(positions[qi]) : -1;
+    if (h == 0 && lane == 0) row_pos[r] = pos;
   }
   // tile bounds: one warp per query tile
   const int q_tiles = rows_pad / kTile;
@@ -622,9 +640,9 @@ __global__ void __launch_bounds__(256) prep_kernel(const char* __restrict__ quer
     int mx = -1, mn = 0x7fffffff;
     for (int r = lane; r < kTile; r += 32) {
       const int64_t qi = (qt * kTile + r) / groups;
-      const int p = qi < num_queries ? static_cast<int>(positions[qi]) : -1;
+      const int p = qi < num_queries ? query_position(rows, positions, qi, query_tokens, num_keys) : -1;
       mx = max(mx, p);
-      mn = min(mn, p);  // padding (-1) makes the tile "partially visible": always masked
+      mn = min(mn, p);  // a masked row (-1) makes the tile "partially visible": always masked
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
@@ -710,12 +728,33 @@ extern "C" int cb_sparse_q_workspace_size(int64_t num_queries, int64_t num_q_hea
   CB_REQUIRE(bytes != nullptr, "null output");
   int rc = sq::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
   if (rc != CB_OK) return rc;
-  CB_REQUIRE(num_queries >= 0, "negative query count");
+  CB_REQUIRE(num_queries >= 0 && num_queries < (int64_t(1) << 30) &&
+                 num_queries * (num_q_heads / num_kv_heads) < (int64_t(1) << 30),
+             "too many queries");
+  CB_REQUIRE(num_kv_heads <= 1024, "too many KV heads");
   *bytes = static_cast<int64_t>(sq::layout(num_queries, num_q_heads, num_kv_heads, 2).total);
   return CB_OK;
 }
 
-extern "C" int cb_sparse_q_scores(const void* query, int64_t query_token_stride, const void* key,
+namespace cb {
+namespace sq {
+// Argument checks shared by both entry points; everything a size computation
+// multiplies is bounded first, so no product below can overflow.
+int check_counts(int64_t num_query_tokens, int64_t num_keys, int64_t num_q_heads,
+                 int64_t num_kv_heads, int64_t num_queries) {
+  CB_REQUIRE(num_keys >= 0 && num_keys < (int64_t(1) << 31), "num_keys out of range");
+  CB_REQUIRE(num_query_tokens >= 0, "negative query token count");
+  CB_REQUIRE(num_queries >= 0 && num_queries < (int64_t(1) << 30) &&
+                 num_queries * (num_q_heads / num_kv_heads) < (int64_t(1) << 30),
+             "too many queries");
+  CB_REQUIRE(num_kv_heads <= 1024, "too many KV heads");
+  return CB_OK;
+}
+}  // namespace sq
+}  // namespace cb
+
+extern "C" int cb_sparse_q_scores(const void* query, int64_t query_token_stride,
+                                  int64_t num_query_tokens, const void* key,
                                   int64_t key_token_stride, int64_t num_keys, int64_t num_q_heads,
                                   int64_t num_kv_heads, int64_t head_size, int dtype,
                                   const int64_t* query_rows, const int64_t* query_positions,
@@ -724,9 +763,8 @@ extern "C" int cb_sparse_q_scores(const void* query, int64_t query_token_stride,
   CB_BIND(stream, scores);
   int rc = sq::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
   if (rc != CB_OK) return rc;
-  CB_REQUIRE(num_keys >= 0 && num_keys < (int64_t(1) << 31), "num_keys out of range");
-  CB_REQUIRE(num_queries >= 0 && num_queries * (num_q_heads / num_kv_heads) < (int64_t(1) << 30),
-             "too many queries");
+  rc = sq::check_counts(num_query_tokens, num_keys, num_q_heads, num_kv_heads, num_queries);
+  if (rc != CB_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (num_keys == 0) return CB_OK;
   CB_REQUIRE(scores != nullptr && key != nullptr, "null pointer argument");
@@ -773,10 +811,11 @@ extern "C" int cb_sparse_q_scores(const void* query, int64_t query_token_stride,
     const int64_t blocks = (warps + 7) / 8;
     const int grid = static_cast<int>(blocks < kSmCount * 8 ? blocks : kSmCount * 8);
     sq::prep_kernel<<<grid, 256, 0, s>>>(
-        static_cast<const char*>(query), query_token_stride, query_rows, query_positions,
-        num_queries, c.num_kv_heads, groups, rows_pad, static_cast<int>(head_size * esize),
-        ws + w.qd, reinterpret_cast<int32_t*>(ws + w.row_pos),
-        reinterpret_cast<int32_t*>(ws + w.tile_max), reinterpret_cast<int32_t*>(ws + w.tile_min));
+        static_cast<const char*>(query), query_token_stride, num_query_tokens, query_rows,
+        query_positions, num_queries, num_keys, c.num_kv_heads, groups, rows_pad,
+        static_cast<int>(head_size * esize), ws + w.qd, reinterpret_cast<int32_t*>(ws + w.row_pos),
+        reinterpret_cast<int32_t*>(ws + w.tile_max), reinterpret_cast<int32_t*>(ws + w.tile_min),
+        device_error);
     rc = launch_status("cb_sparse_q_scores (prep)");
     if (rc != CB_OK) return rc;
   }
@@ -811,43 +850,68 @@ constexpr int64_t kStaticWorkspaceBytes = int64_t(32) << 20;  // 32 MiB
 static __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
 
 std::mutex g_static_mutex;
-void* g_static_address[64] = {};  // device address of the array, per device ordinal
+// Device address of the array per CUDA context (a device ordinal can name
+// several contexts over the process's life: cudaDeviceReset, or an FFI host
+// that drives its own context).
+cb::ContextTable<void*, 64> g_static_address;
 
-// Device address of the array on the current device (set up on first use).
-int static_workspace(void** address) {
-  int device = -1;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess || device < 0 || device >= 64) {
-    set_error("cb_sparse_q_scores_static: no usable current device (%s)", cudaGetErrorString(e));
+// Device address of the array in the calling thread's current context.  Outside
+// a stream capture it is looked up on every call (cudaGetSymbolAddress is a
+// table lookup once the module is loaded) and recorded for the context; inside
+// a capture only the recorded address is used, so each context needs one call
+// outside capture first.
+int static_workspace(cudaStream_t stream, void** address) {
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &capture);
+  if (e != cudaSuccess) {
+    set_error("cb_sparse_q_scores_static: cudaStreamIsCapturing failed: %s", cudaGetErrorString(e));
     return CB_ERR_CUDA;
   }
-  std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (g_static_address[device] == nullptr) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_static_workspace);
-    if (e != cudaSuccess || ptr == nullptr) {
-      set_error("cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  void* found = nullptr;
+  if (capture == cudaStreamCaptureStatusNone) {
+    e = cudaGetSymbolAddress(&found, g_static_workspace);
+    if (e != cudaSuccess || found == nullptr) {
+      set_error("cb_sparse_q_scores_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
       return CB_ERR_CUDA;
     }
-    g_static_address[device] = ptr;
   }
-  *address = g_static_address[device];
+  void* context = nullptr;
+  int rc = current_context(&context);
+  if (rc != CB_OK) return rc;
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (found != nullptr) {
+    if (!g_static_address.store(context, found)) {
+      set_error("cb_sparse_q_scores_static: more than 64 CUDA contexts");
+      return CB_ERR_INVALID;
+    }
+  } else {
+    found = g_static_address.find(context, nullptr);
+    if (found == nullptr) {
+      set_error("cb_sparse_q_scores_static: first call in this CUDA context made inside a stream "
+                "capture; make one call on each device outside capture first");
+      return CB_ERR_INVALID;
+    }
+  }
+  *address = found;
   return CB_OK;
 }
 }  // namespace
 
 extern "C" int cb_sparse_q_scores_static(const void* query, int64_t query_token_stride,
-                                         const void* key, int64_t key_token_stride,
-                                         int64_t num_keys, int64_t num_q_heads,
-                                         int64_t num_kv_heads, int64_t head_size, int dtype,
-                                         const int64_t* query_rows,
+                                         int64_t num_query_tokens, const void* key,
+                                         int64_t key_token_stride, int64_t num_keys,
+                                         int64_t num_q_heads, int64_t num_kv_heads,
+                                         int64_t head_size, int dtype, const int64_t* query_rows,
                                          const int64_t* query_positions, int64_t num_queries,
                                          float scale, float* scores, int32_t* device_error,
                                          void* stream) {
   CB_BIND(stream, scores);
+  int rc = sq::check_shape(num_q_heads, num_kv_heads, head_size, dtype);
+  if (rc != CB_OK) return rc;
+  rc = sq::check_counts(num_query_tokens, num_keys, num_q_heads, num_kv_heads, num_queries);
+  if (rc != CB_OK) return rc;
   int64_t needed = 0;
-  int rc = cb_sparse_q_workspace_size(num_queries, num_q_heads, num_kv_heads, head_size, dtype,
-                                      &needed);
+  rc = cb_sparse_q_workspace_size(num_queries, num_q_heads, num_kv_heads, head_size, dtype, &needed);
   if (rc != CB_OK) return rc;
   // the scorer wants a 1 KiB aligned workspace; the array is 256-B aligned
   constexpr int64_t kUsable = kStaticWorkspaceBytes - 1024;
@@ -857,12 +921,12 @@ extern "C" int cb_sparse_q_scores_static(const void* query, int64_t query_token_
              (long long)num_queries, (long long)num_q_heads, (long long)num_kv_heads,
              (long long)needed, (long long)kUsable);
   void* base = nullptr;
-  rc = static_workspace(&base);
+  rc = static_workspace(reinterpret_cast<cudaStream_t>(stream), &base);
   if (rc != CB_OK) return rc;
   const uintptr_t raw = reinterpret_cast<uintptr_t>(base);
   void* aligned = reinterpret_cast<void*>((raw + 1023) & ~static_cast<uintptr_t>(1023));
-  return cb_sparse_q_scores(query, query_token_stride, key, key_token_stride, num_keys,
-                            num_q_heads, num_kv_heads, head_size, dtype, query_rows,
+  return cb_sparse_q_scores(query, query_token_stride, num_query_tokens, key, key_token_stride,
+                            num_keys, num_q_heads, num_kv_heads, head_size, dtype, query_rows,
                             query_positions, num_queries, scale, scores, aligned, kUsable,
                             device_error, stream);
 }

@@ -113,8 +113,12 @@ class Rope:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default=os.environ.get("CACHEBLEND_REFERENCE", "/root/reference"))
+    parser.add_argument("--reference", default=os.environ.get("CACHEBLEND_REFERENCE"),
+                        help="checkout of the reference (the directory holding cacheblend_vllm/); "
+                             "or set CACHEBLEND_REFERENCE")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("pass --reference <checkout> or set CACHEBLEND_REFERENCE")
     sys.path.insert(0, args.reference)
     sys.dont_write_bytecode = True
     from cacheblend_vllm.ascend import PagedBlendLoader, Qwen3BlendExecutor, relocate_key
