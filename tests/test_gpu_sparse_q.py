@@ -131,3 +131,46 @@ def test_sparse_q_no_queries_and_error_word(cuda):
         sparse_q_key_mass(torch.zeros(4, 8, 64, device=cuda, dtype=torch.bfloat16),
                           torch.zeros(8, 2, 64, device=cuda, dtype=torch.bfloat16), np.array([0]),
                           np.array([1]), 0.1)
+
+
+def test_sparse_q_abi_bounds_query_rows_and_positions(cuda):
+    """Through the C ABI (the Python wrapper would refuse these on the host): a
+    query row outside [0, num_query_tokens) or a negative position is not read,
+    adds nothing and reports code 4; a position past the last key sees every
+    key, as the reference's mask does."""
+    import ctypes
+
+    from cacheblend_b200 import _native
+
+    lib = _native.load_library()
+    gen = torch.Generator().manual_seed(44)
+    key = torch.randn(400, 2, 128, generator=gen).to(torch.bfloat16).to(cuda)
+    query = torch.randn(6, 16, 128, generator=gen).to(torch.bfloat16).to(cuda)
+    workspace = torch.empty(1 << 22, dtype=torch.uint8, device=cuda)
+    aligned = (workspace.data_ptr() + 1023) // 1024 * 1024
+
+    def run(rows, positions):
+        rows_d = torch.tensor(rows, dtype=torch.long, device=cuda)
+        pos_d = torch.tensor(positions, dtype=torch.long, device=cuda)
+        out = torch.empty(400, dtype=torch.float32, device=cuda)
+        error = torch.zeros(1, dtype=torch.int32, device=cuda)
+        status = lib.cb_sparse_q_scores(
+            query.data_ptr(), query.stride(0) * 2, query.shape[0], key.data_ptr(), key.stride(0) * 2, 400,
+            16, 2, 128, 0, rows_d.data_ptr(), pos_d.data_ptr(), len(rows), ctypes.c_float(128 ** -0.5),
+            out.data_ptr(), aligned, workspace.numel() - (aligned - workspace.data_ptr()), error.data_ptr(),
+            _native.stream_handle())
+        assert status == 0, lib.cb_last_error().decode()
+        torch.cuda.synchronize()
+        return out.cpu().numpy(), int(error.item())
+
+    base, err = run([0, 1, 2], [50, 120, 399])
+    assert err == 0
+    bad_row, err = run([0, 1, 2, 6], [50, 120, 399, 10])  # row 6 does not exist
+    assert err == 4
+    np.testing.assert_allclose(bad_row, base, rtol=RTOL, atol=1e-6)
+    bad_pos, err = run([0, 1, 2, 3], [50, 120, 399, -5])  # negative position
+    assert err == 4
+    np.testing.assert_allclose(bad_pos, base, rtol=RTOL, atol=1e-6)
+    past, err = run([0, 1, 2], [50, 120, 10_000])  # sees every key, like position 399
+    assert err == 0
+    np.testing.assert_allclose(past, base, rtol=RTOL, atol=1e-6)
