@@ -47,33 +47,102 @@ constexpr int kThreads = 128 + 128 * kEpilogueGroups;
 constexpr int kTmemBufs = 4;          // four 128-column fp32 accumulators
 constexpr uint32_t kTmemCols = 512;
 
-// fp32 accumulator value rounded to the 16-bit matmul output type and widened.
-template <typename T>
-__device__ __forceinline__ float round_logit(uint32_t bits) {
-  return Elem<T>::to_f(Elem<T>::from_f(__uint_as_float(bits)));
+// Which score pairs take the FMA-pipe exp2 instead of the MUFU one: bit p of
+// the mask (p = pair index mod 16 inside a thread's 32- or 64-score batch).
+// The MUFU unit does 16 exp2 per SM per clock against 128 FMA-pipe lanes, so
+// moving a share of the exp2s to the polynomial balances the two pipes.
+#ifndef CB_SQ_POLY_PASS1
+#define CB_SQ_POLY_PASS1 0x0000u
+#endif
+#ifndef CB_SQ_POLY_PASS2
+#define CB_SQ_POLY_PASS2 0x0000u
+#endif
+constexpr uint32_t kPolyPass1 = CB_SQ_POLY_PASS1;
+constexpr uint32_t kPolyPass2 = CB_SQ_POLY_PASS2;
+
+// 2^y for two scores on the FMA pipe.  Cody-Waite style split y = j + f with
+// j = rint(y), |f| <= 1/2, by adding and subtracting 1.5 * 2^23 (the sum's low
+// mantissa bits then hold j); 2^f by the degree-3 polynomial of least maximum
+// relative error on [-1/2, 1/2] (7.5e-5; coefficients from a Remez exchange,
+// exp2_poly_fit.py beside this file); 2^j added into the exponent field.  y is
+// clamped to -126 first: then j >= -126 and, since p(f) >= 2^-1/2, the biased
+// exponent 126 + j of the result cannot borrow into the sign bit (at -127 and
+// p(0) < 1 it would, giving NaN).  Within 7.5e-5 relative of 2^y for y >= -125;
+// non-negative and below 2^-124 for smaller y (where the MUFU ex2.ftz returns
+// 0 or nearly so).  Both passes only produce y <= 0 (up to one rounding).
+constexpr float kExp2Round = 12582912.0f;  // 1.5 * 2^23
+constexpr float kExp2C0 = 0.9999280571937561f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.2426111251115799f;
+constexpr float kExp2C3 = 0.0551716685295105f;
+
+__device__ __forceinline__ float2 exp2_poly(float2 y) {
+  y.x = fmaxf(y.x, -126.0f);
+  y.y = fmaxf(y.y, -126.0f);
+  const float2 t = __fadd2_rn(y, make_float2(kExp2Round, kExp2Round));
+  const float2 j = __fadd2_rn(t, make_float2(-kExp2Round, -kExp2Round));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), y);  // exact: y - j
+  float2 p = __ffma2_rn(f, make_float2(kExp2C3, kExp2C3), make_float2(kExp2C2, kExp2C2));
+  p = __ffma2_rn(p, f, make_float2(kExp2C1, kExp2C1));
+  p = __ffma2_rn(p, f, make_float2(kExp2C0, kExp2C0));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
-// Rounds two fp32 accumulator values to the 16-bit matmul output type
-// (round to nearest even, one packed cvt) and widens them back.  (The same
-// rounding done on the FMA pipe measured 2 % slower here.)
+// 2^y of a pair, on the FMA pipe when `poly`, else on the MUFU.
+__device__ __forceinline__ float2 exp2_pair(float2 y, bool poly) {
+  return poly ? exp2_poly(y) : make_float2(ex2(y.x), ex2(y.y));
+}
+
+// Two fp32 accumulator values rounded (nearest even) to the 16-bit matmul
+// output type T with one packed cvt; low half = lo.
 template <typename T>
-__device__ __forceinline__ void round_pair(uint32_t lo_bits, uint32_t hi_bits, float& lo, float& hi);
+__device__ __forceinline__ uint32_t pack_round(uint32_t lo_bits, uint32_t hi_bits);
 template <>
-__device__ __forceinline__ void round_pair<__nv_bfloat16>(uint32_t lo_bits, uint32_t hi_bits,
-                                                          float& lo, float& hi) {
+__device__ __forceinline__ uint32_t pack_round<__nv_bfloat16>(uint32_t lo_bits, uint32_t hi_bits) {
   uint32_t packed;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "r"(hi_bits), "r"(lo_bits));
-  lo = __uint_as_float(packed << 16);
-  hi = __uint_as_float(packed & 0xffff0000u);
+  return packed;
 }
 template <>
-__device__ __forceinline__ void round_pair<__half>(uint32_t lo_bits, uint32_t hi_bits, float& lo,
-                                                   float& hi) {
+__device__ __forceinline__ uint32_t pack_round<__half>(uint32_t lo_bits, uint32_t hi_bits) {
   uint32_t packed;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(packed) : "r"(hi_bits), "r"(lo_bits));
-  const __half2 h2 = *reinterpret_cast<const __half2*>(&packed);
-  lo = __low2float(h2);
-  hi = __high2float(h2);
+  return packed;
+}
+
+// The pair widened back to fp32.
+template <typename T>
+__device__ __forceinline__ float2 unpack(uint32_t packed);
+template <>
+__device__ __forceinline__ float2 unpack<__nv_bfloat16>(uint32_t packed) {
+  return make_float2(__uint_as_float(packed << 16), __uint_as_float(packed & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 unpack<__half>(uint32_t packed) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&packed));
+}
+
+// Elementwise max of two packed pairs (one instruction for two scores).
+template <typename T>
+__device__ __forceinline__ uint32_t pair_max(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t pair_max<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <>
+__device__ __forceinline__ uint32_t pair_max<__half>(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// -inf in T's encoding, in the low half of a packed pair.
+template <typename T>
+__device__ __forceinline__ constexpr uint32_t neg_inf_half() {
+  return std::is_same<T, __nv_bfloat16>::value ? 0xff80u : 0xfc00u;
 }
 
 // Named barrier over the epilogue warpgroups.
@@ -305,23 +374,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int lim = valid - half * 64;  // valid columns in this half
           if (lim <= 0) continue;
-          float x[64];
+          uint32_t pk[32];  // the 64 rounded logits, packed in pairs (low half = even column)
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            round_pair<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31], x[2 * j], x[2 * j + 1]);
-          if (lim < 64) {
+            pk[j] = pack_round<T>(v[j >> 4][(2 * j) & 31], v[j >> 4][(2 * j + 1) & 31]);
+          if (lim < 64) {  // keys past the row's position: -inf
+            constexpr uint32_t ninf = neg_inf_half<T>();
 #pragma unroll
-            for (int j = 0; j < 64; ++j)
-              if (j >= lim) x[j] = -INFINITY;
+            for (int j = 0; j < 32; ++j) {
+              if (2 * j >= lim) pk[j] = ninf | (ninf << 16);
+              else if (2 * j + 1 >= lim) pk[j] = (pk[j] & 0xffffu) | (ninf << 16);
+            }
           }
-          // eight independent chains for the max and the sum
-          float mx[8];
+          // row max: four packed chains, one max per two scores
+          uint32_t mk[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) mx[i] = x[i];
+          for (int i = 0; i < 4; ++i) mk[i] = pk[i];
 #pragma unroll
-          for (int j = 8; j < 64; ++j) mx[j & 7] = fmaxf(mx[j & 7], x[j]);
-          const float cmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+          for (int j = 4; j < 32; ++j) mk[j & 3] = pair_max<T>(mk[j & 3], pk[j]);
+          const float2 mm = unpack<T>(pair_max<T>(pair_max<T>(mk[0], mk[1]), pair_max<T>(mk[2], mk[3])));
+          const float cmax = fmaxf(mm.x, mm.y);
           const float m_new = fmaxf(m, cmax * c.scale_log2);  // scale > 0: max commutes
           // paired fp32 FMA / add: one instruction per two scores
           const float2 scale2 = make_float2(c.scale_log2, c.scale_log2);
@@ -331,8 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 4; ++i) sm[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float2 y = __ffma2_rn(make_float2(x[2 * j], x[2 * j + 1]), scale2, shift2);
-            sm[j & 3] = __fadd2_rn(sm[j & 3], make_float2(ex2(y.x), ex2(y.y)));
+            const float2 y = __ffma2_rn(unpack<T>(pk[j]), scale2, shift2);
+            sm[j & 3] = __fadd2_rn(sm[j & 3], exp2_pair(y, (kPolyPass1 >> (j & 15)) & 1u));
           }
           const float2 s01 = __fadd2_rn(sm[0], sm[1]);
           const float2 s23 = __fadd2_rn(sm[2], sm[3]);
@@ -534,25 +606,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (full) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                float a0, a1, a2, a3;
-                round_pair<T>(v[4 * j], v[4 * j + 1], a0, a1);
-                round_pair<T>(v[4 * j + 2], v[4 * j + 3], a2, a3);
                 const float4 l4 = nlse4[j];
-                const float2 y0 = __ffma2_rn(make_float2(a0, a1), scale2, make_float2(l4.x, l4.y));
-                const float2 y1 = __ffma2_rn(make_float2(a2, a3), scale2, make_float2(l4.z, l4.w));
-                acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], make_float2(ex2(y0.x), ex2(y0.y)));
-                acc[(2 * j + 1) & 3] = __fadd2_rn(acc[(2 * j + 1) & 3], make_float2(ex2(y1.x), ex2(y1.y)));
+                const float2 y0 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j], v[4 * j + 1])), scale2,
+                                             make_float2(l4.x, l4.y));
+                const float2 y1 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j + 2], v[4 * j + 3])), scale2,
+                                             make_float2(l4.z, l4.w));
+                acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], exp2_pair(y0, (kPolyPass2 >> (2 * j)) & 1u));
+                acc[(2 * j + 1) & 3] =
+                    __fadd2_rn(acc[(2 * j + 1) & 3], exp2_pair(y1, (kPolyPass2 >> (2 * j + 1)) & 1u));
               }
             } else {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                float a0, a1, a2, a3;
-                round_pair<T>(v[4 * j], v[4 * j + 1], a0, a1);
-                round_pair<T>(v[4 * j + 2], v[4 * j + 3], a2, a3);
                 const float4 l4 = nlse4[j];
                 const int4 p4 = pos4[j];
-                const float2 y0 = __ffma2_rn(make_float2(a0, a1), scale2, make_float2(l4.x, l4.y));
-                const float2 y1 = __ffma2_rn(make_float2(a2, a3), scale2, make_float2(l4.z, l4.w));
+                const float2 y0 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j], v[4 * j + 1])), scale2,
+                                             make_float2(l4.x, l4.y));
+                const float2 y1 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j + 2], v[4 * j + 3])), scale2,
+                                             make_float2(l4.z, l4.w));
                 const float2 e0 = make_float2(key <= p4.x ? ex2(y0.x) : 0.0f, key <= p4.y ? ex2(y0.y) : 0.0f);
                 const float2 e1 = make_float2(key <= p4.z ? ex2(y1.x) : 0.0f, key <= p4.w ? ex2(y1.y) : 0.0f);
                 acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], e0);
