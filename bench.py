@@ -306,6 +306,17 @@ class DevicePath:
         )
         self._ev_end("deviation", ev, stream)
 
+    def deviation_rotating(self, index: int, rotation: list, stream) -> None:
+        """The check layer's deviation launch on the ``index``-th copy of its inputs."""
+        wl, shape, plan = self.wl, self.wl.shape, self.wl.plan
+        fresh, k_plane = rotation[index]
+        width = wl.heads * shape.head_dim
+        self.native.call(
+            "cb_kv_deviation", fresh.data_ptr(), width * 2, k_plane.data_ptr(), width * 2,
+            plan.allocation_end, 0, plan.apc_prefix_tokens, wl.act, width, 0, self.scores.data_ptr(),
+            stream.cuda_stream,
+        )
+
     def select(self, stream) -> torch.Tensor:
         wl = self.wl
         ev = self._ev("select", stream)
@@ -410,12 +421,16 @@ class DevicePath:
         in a graph, replayed ``reps`` times between two CUDA events on the launching stream."""
         layers = self.wl.shape.layers
         check = self.wl.shape.check_layer
+        k_plane = self.staging[check % 2][0]
+        rotation = [(self.fresh.clone(), k_plane.clone()) for _ in range(4)]
         kinds = {
             "load": (layers, lambda: [self.load_layer(layer, stream) for layer in range(layers)]),
             "scatter": (layers, lambda: [self.commit(layer, self.staging[layer % 2], stream)
                                          for layer in range(layers)]),
-            # single launches per step: ten back to back (same inputs, same outputs)
-            "deviation": (10, lambda: [self.deviation(self.staging[check % 2], stream) for _ in range(10)]),
+            # single launches per step: ten back to back over four rotating input sets (512 MiB
+            # at 8 heads), so each launch reads its fresh and cached K from HBM, not from L2
+            "deviation": (10, lambda: [self.deviation_rotating(i % len(rotation), rotation, stream)
+                                       for i in range(10)]),
             "select": (10, lambda: [self.select(stream) for _ in range(10)]),
         }
         out = {}
@@ -436,9 +451,6 @@ class DevicePath:
             out[name] = start.elapsed_time(end) * 1e3 / (reps * count)
             del graph
         return out
-
-    def launches_per_step(self) -> int:
-        return 2 * self.wl.shape.layers + 2
 
 
 def e2e_step(wl: Workload, load_stream, tp_group=None) -> tuple[torch.Tensor, int]:
@@ -638,77 +650,111 @@ def run_e2e(args, wl: Workload, device, world: int, group, span: int) -> dict:
                           "peak_source": "measured: best single 1 GiB pinned->device copy"}}
 
 
-def cpu_sample(shape: Shape, sample_layers: int, threads: int, seed: int = 2) -> dict:
-    """Time the CPU restatement on ``sample_layers`` layers + one scoring pass."""
-    import oracle
+class CpuRequest:
+    """The whole request on the host: the CPU restatement (oracle/, C + OpenMP) of
+    every layer's blend load (APC prefix gather, gap zeroing, RoPE relocation,
+    chunk placement: ascend.py:224-370) and commit scatter (kv_layout.py:125-161),
+    plus the check layer's K-deviation and top-k select (ascend.py:534-543,
+    757-796).  Inputs are generated once; ``run`` is one timed request."""
 
-    plan = make_plan(shape, seed)
-    rng = np.random.default_rng(seed)
-    hd, heads = shape.head_dim, shape.kv_heads
-    row = heads * hd
-    table = oracle.f32_to_bf16(rope_table(shape, "cpu").numpy())
-    blocks = rng.permutation(shape.pool_blocks)[: shape.tokens // shape.block_size]
-    slots = (blocks[:, None] * shape.block_size + np.arange(shape.block_size)[None, :]).reshape(-1)
-    slots = slots[: plan.allocation_end].astype(np.int64)
-    moved = np.full(len(plan.segments), 1, dtype=np.int32)
-    k = rng.integers(0, 1 << 16, size=(shape.pool_blocks, shape.block_size, heads, hd), dtype=np.uint16)
-    v = rng.integers(0, 1 << 16, size=k.shape, dtype=np.uint16)
-    k &= 0xBFFF  # keep exponents moderate (no inf/NaN patterns)
-    v &= 0xBFFF
-    hosts = [rng.integers(0, 1 << 16, size=(2, shape.chunk, heads, hd), dtype=np.uint16) & 0xBFFF
-             for _ in plan.segments]
-    segments = [(s.source_start, s.target_start, s.length, h) for s, h in zip(plan.segments, hosts)]
-    act = plan.allocation_end - plan.apc_prefix_tokens
-    t0 = time.perf_counter()
-    for _ in range(sample_layers):
-        staging = oracle.blend_load(oracle.BF16, plan.allocation_end, plan.apc_prefix_tokens, k, v, slots,
-                                    shape.block_size, segments, moved, table, hd, hd, True, threads)
-        oracle.paged_scatter(staging[:, plan.apc_prefix_tokens:], k, v, slots[plan.apc_prefix_tokens:],
-                             shape.block_size)
-    t_layers = (time.perf_counter() - t0) / sample_layers
-    fresh = staging[0].reshape(plan.allocation_end, row)[plan.apc_prefix_tokens:].copy()
-    t1 = time.perf_counter()
-    scores = oracle.kv_deviation(fresh, staging[0].reshape(plan.allocation_end, row), oracle.BF16,
-                                 abs_offset=plan.apc_prefix_tokens, nthreads=threads)
-    gaps = plan.gap_mask()[plan.apc_prefix_tokens:]
-    oracle.select(scores, gaps, shape.ratio)
-    t_score = time.perf_counter() - t1
-    step = shape.layers * t_layers + t_score
-    return {"value": act / step, "step_s": step, "layer_s": t_layers, "score_s": t_score, "act": act}
+    def __init__(self, shape: Shape, threads: int, seed: int = 2):
+        import oracle
+
+        self.oracle = oracle
+        self.shape = shape
+        self.threads = threads
+        self.plan = plan = make_plan(shape, seed)
+        rng = np.random.default_rng(seed)
+        hd, heads = shape.head_dim, shape.kv_heads
+        self.row = heads * hd
+        self.table = oracle.f32_to_bf16(rope_table(shape, "cpu").numpy())
+        blocks = rng.permutation(shape.pool_blocks)[: shape.tokens // shape.block_size]
+        slots = (blocks[:, None] * shape.block_size + np.arange(shape.block_size)[None, :]).reshape(-1)
+        self.slots = slots[: plan.allocation_end].astype(np.int64)
+        self.moved = np.full(len(plan.segments), 1, dtype=np.int32)
+        # bf16 bit patterns with moderate exponents (no inf/NaN patterns)
+        self.k = rng.integers(0, 1 << 16, size=(shape.pool_blocks, shape.block_size, heads, hd),
+                              dtype=np.uint16) & 0xBFFF
+        self.v = rng.integers(0, 1 << 16, size=self.k.shape, dtype=np.uint16) & 0xBFFF
+        hosts = [rng.integers(0, 1 << 16, size=(2, shape.chunk, heads, hd), dtype=np.uint16) & 0xBFFF
+                 for _ in plan.segments]
+        self.segments = [(s.source_start, s.target_start, s.length, h) for s, h in zip(plan.segments, hosts)]
+        self.act = plan.allocation_end - plan.apc_prefix_tokens
+        self.gaps = plan.gap_mask()[plan.apc_prefix_tokens:]
+
+    def run(self, layers: int | None = None) -> float:
+        """Seconds for ``layers`` layers (default: all) and the check-layer scoring."""
+        oracle, shape, plan = self.oracle, self.shape, self.plan
+        start = plan.apc_prefix_tokens
+        t0 = time.perf_counter()
+        for layer in range(shape.layers if layers is None else layers):
+            staging = oracle.blend_load(oracle.BF16, plan.allocation_end, start, self.k, self.v, self.slots,
+                                        shape.block_size, self.segments, self.moved, self.table,
+                                        shape.head_dim, shape.head_dim, True, self.threads)
+            if layer == shape.check_layer or (layers is not None and layer == layers - 1):
+                k_plane = staging[0].reshape(plan.allocation_end, self.row)
+                scores = oracle.kv_deviation(k_plane[start:].copy(), k_plane, oracle.BF16, abs_offset=start,
+                                             nthreads=self.threads)
+                oracle.select(scores, self.gaps, shape.ratio)
+            oracle.paged_scatter(staging[:, start:], self.k, self.v, self.slots[start:], shape.block_size)
+        return time.perf_counter() - t0
+
+
+def cpu_baseline(shape: Shape, threads: int, requests: int = 2) -> dict:
+    """The CPU restatement timed on whole requests (best of ``requests``), no extrapolation."""
+    request = CpuRequest(shape, threads)
+    request.run(layers=1)  # warm the pages and the thread pool
+    best = min(request.run() for _ in range(requests))
+    return {"value": request.act / best, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"whole {shape.layers}-layer requests (best of {requests}): every layer's blend "
+                      "load and commit scatter plus the check-layer deviation and select",
+            "ms_per_request": best * 1e3}
+
+
+def workload_config(shape: Shape, span: int, heads: int, world: int, shard: int) -> dict:
+    """The ``config`` of the load+score+scatter lines (the GPU arm and the reference arm alike)."""
+    row = heads * shape.head_dim * 2
+    plan = make_plan(shape, 2)
+    touched = 2 * row * (plan.hit_tokens + plan.apc_prefix_tokens) + 2 * row * plan.allocation_end + 4 * row * span
+    return {"workload": shape.name, "tokens": shape.tokens, "span_tokens": span, "layers": shape.layers,
+            "kv_heads_per_rank": heads, "hit_chunks": shape.hit_chunks, "block_size": shape.block_size,
+            "check_layer": shape.check_layer, "ratio": shape.ratio,
+            "parallelism": f"tp{world}" if shard == world else f"one rank of tp{shard}",
+            "l2": f"inputs larger than L2 (each layer touches {touched / 2**20:.0f} MiB)"}
 
 
 # ---------------------------------------------------------------------------- main
 def run_reference(args, shape: Shape, world: int, rank: int) -> None:
+    """--impl reference: the reference's CPU path (its restatement) on whole requests,
+    all host threads; each timed step is one full request, nothing extrapolated."""
     if rank != 0:
         return
     import oracle
 
     threads = oracle.threads(0)
+    request = CpuRequest(shape, threads)
     for _ in range(args.warmup):
-        cpu_sample(shape, 1, threads)
-    samples = [cpu_sample(shape, args.sample_layers, threads) for _ in range(args.steps)]
-    value = statistics.median(s["value"] for s in samples)
-    step_ms = statistics.median(s["step_s"] for s in samples) * 1e3
-    sample = (f"{args.sample_layers} of {shape.layers} layers (blend load + commit scatter) + the "
-              f"check-layer deviation/select, extrapolated to the full {shape.layers}-layer request")
+        request.run(layers=1)
+    times = [request.run() for _ in range(args.steps)]
+    step_s = statistics.median(times)
+    value = request.act / step_s
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
-        "config": {"workload": shape.name, "tokens": shape.tokens, "layers": shape.layers,
-                   "kv_heads": shape.kv_heads, "hit_chunks": shape.hit_chunks, "parallelism": f"tp{world}"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
+        "config": workload_config(shape, request.act, shape.kv_heads // world, world, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"each step one whole {shape.layers}-layer request (median of "
+                                   f"{args.steps}); warm-up steps run one layer"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
-    """Config 3: Sparse-Q scoring at the boundary layer (tensor-core bound)."""
-    from cacheblend_b200.selection import select_tokens, sparse_q_key_mass, sparse_q_masks
-
+def sparse_q_inputs(world: int, rank: int, device):
+    """Config 3 inputs: 98,303 keys, 16 seeded gap chunks (4,095 queries) as the
+    sparse queries, Q and K ~ N(0, 1) bf16, this rank's share of the heads."""
     cfg = SPARSE_Q_CONFIG
-    device = torch.device("cuda", local)
     hq, hkv = cfg["q_heads"] // world, cfg["kv_heads"] // world
     ctx = cfg["tokens"] - 1  # the last prompt token stays with vLLM (connector.py:664-673)
     rng = np.random.default_rng(3)
@@ -718,6 +764,69 @@ def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
                                        + [np.arange((ctx // 256) * 256, ctx)]))
     key = torch.randn(ctx, hkv, 128, generator=gen, device=device).to(torch.bfloat16)
     query = torch.randn(ctx, hq, 128, generator=gen, device=device).to(torch.bfloat16)
+    return ctx, positions, query, key
+
+
+def sparse_q_cpu_sample(positions: np.ndarray, query, key, scale: float, flops: float,
+                        budget_s: float = 12.0) -> dict:
+    """The oracle's Sparse-Q (numpy, BLAS threads) on query chunks spread over the
+    prompt until about ``budget_s``; scaled to the full step by algorithmic flops."""
+    import oracle
+
+    k = key.float().cpu().numpy()
+    order = np.random.default_rng(7).permutation(positions.size // 8) * 8
+    done_flops, done, t0 = 0.0, 0, time.perf_counter()
+    for start in order:
+        rows = positions[start:start + 8]
+        q = query[torch.from_numpy(rows).to(query.device)].float().cpu().numpy()
+        oracle.sparse_q_key_mass(q, k[: int(rows.max()) + 1], rows, scale)
+        done_flops += float(sum(2 * 128 * query.shape[1] * (int(p) + 1) for p in rows))
+        done += rows.size
+        if time.perf_counter() - t0 > budget_s:
+            break
+    elapsed = time.perf_counter() - t0
+    step_s = elapsed * flops / done_flops
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max([int(info.get("num_threads", 1)) for info in threadpool_info()] + [1])
+    except ImportError:
+        cores = 1
+    return {"value": (key.shape[0]) / step_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{done} of {positions.size} queries (chunks of 8 spread over the prompt), numpy "
+                      f"oracle with BLAS on {cores} threads, scaled to the step by algorithmic flops",
+            "est_ms_per_step": step_s * 1e3}
+
+
+def sparse_q_reference(args) -> None:
+    """--impl reference for config 3: the reference's Sparse-Q (its numpy restatement)
+    on the host, each step a bounded sample of the step's queries scaled by flops."""
+    cfg = SPARSE_Q_CONFIG
+    ctx, positions, query, key = sparse_q_inputs(1, 0, torch.device("cpu"))
+    flops = float(sum(2 * 128 * cfg["q_heads"] * (int(p) + 1) for p in positions))
+    samples = [sparse_q_cpu_sample(positions, query, key, 128 ** -0.5, flops, budget_s=2.0)
+               for _ in range(args.warmup + args.steps)][args.warmup:]
+    value = float(np.median([s["value"] for s in samples]))
+    print(json.dumps({
+        "impl": "reference", "metric": "sparse-q scored span tokens/s (boundary layer, TP-sharded)",
+        "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ctx / value * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
+        "config": {"workload": cfg["name"], "keys": ctx, "queries": int(positions.size),
+                   "q_heads_per_rank": cfg["q_heads"], "kv_heads_per_rank": cfg["kv_heads"]},
+        "cpu_baseline": {**samples[-1], "value": value},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def sparse_q_bench(args, world: int, rank: int, local: int, steps: int, cpu: bool) -> dict | None:
+    """Config 3: Sparse-Q scoring at the boundary layer (tensor-core bound) + select."""
+    from cacheblend_b200.selection import select_tokens, sparse_q_key_mass, sparse_q_masks
+
+    cfg = SPARSE_Q_CONFIG
+    device = torch.device("cuda", local)
+    ctx, positions, query, key = sparse_q_inputs(world, rank, device)
+    hq, hkv = query.shape[1], key.shape[1]
     gaps = np.zeros(ctx, dtype=bool)
     gaps[positions] = True
     qmask, forced, _ = sparse_q_masks(gaps, 16, 1, 64)
@@ -733,7 +842,7 @@ def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
             torch.distributed.all_reduce(mass)
         return select_tokens(mass, gaps, 0.15, forced)
 
-    for _ in range(args.warmup):
+    for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(device)
     barrier(world)
@@ -741,33 +850,42 @@ def sparse_q_bench(args, world: int, rank: int, local: int) -> None:
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         start.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         end.record()
         torch.cuda.synchronize(device)
     barrier(world)
-    ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
-    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
-    peak = float(peaks.get("bf16_tflops", 1590.0))
+    ms = max_over_ranks(start.elapsed_time(end), world, device) / steps
+    peaks = measured_peaks()
+    peak = peaks["bf16_tflops"]
     achieved = flops / (ms / 1e3) / 1e12
     # co-limit: one exp2 per score element in each of the two passes on the MUFU
     # pipe (16 per SM per clock on B200)
     exps = 2.0 * flops / (2 * 128)
     mufu_peak = 16 * 148 * 1.965e9
-    if rank == 0:
-        print(json.dumps({
-            "metric": "sparse-q scored span tokens/s (boundary layer, TP-sharded)", "value": ctx / (ms / 1e3),
-            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic (seeded)",
-            "config": {"workload": cfg["name"], "keys": ctx, "queries": int(positions.size),
-                       "q_heads_per_rank": hq, "kv_heads_per_rank": hkv},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "flops_note": "one causal QK^T counted once (two passes run)",
-                         "co_limit": {"pipe": "mufu exp2", "achieved_per_s": exps / (ms / 1e3),
-                                      "peak_per_s": mufu_peak, "frac": exps / (ms / 1e3) / mufu_peak,
-                                      "peak_source": "16 exp2 per SM per clock x 148 SMs x 1965 MHz (nominal)"}},
-            "device_error": int(error.item()), "clocks": clocks.summary(),
-        }), flush=True)
+    if rank != 0:
+        return None
+    cpu_line = None
+    if cpu and world == 1:
+        cpu_line = sparse_q_cpu_sample(positions, query, key, scale, flops)
+    return {
+        "metric": "sparse-q scored span tokens/s (boundary layer, TP-sharded)", "value": ctx / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16)",
+        "config": {"workload": cfg["name"], "keys": ctx, "queries": int(positions.size),
+                   "q_heads_per_rank": hq, "kv_heads_per_rank": hkv,
+                   "l2": "K and the sparse queries re-streamed per tile pair; 201 MiB of K, larger than L2"},
+        "gpu_launches": 4 * steps, "launch": "eager: query prep, row pass, key pass, select per step",
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peaks["source"],
+                     "flops_note": "one causal QK^T counted once (two passes run); timed over the step "
+                                   "(prep, both passes, select)",
+                     "co_limit": {"pipe": "mufu exp2", "achieved_per_s": exps / (ms / 1e3),
+                                  "peak_per_s": mufu_peak, "frac": exps / (ms / 1e3) / mufu_peak,
+                                  "peak_source": "16 exp2 per SM per clock x 148 SMs x 1965 MHz (nominal)"}},
+        "device_error": int(error.item()), "clocks": clocks.summary(), "cpu_baseline": cpu_line,
+    }
 
 
 def attention_inputs(world: int, rank: int, device):
@@ -1113,7 +1231,7 @@ class GcPauses:
         return out
 
 
-def store_bench(args, world: int, rank: int, local: int) -> None:
+def store_bench(args, world: int, rank: int, local: int, steps: int, cpu_on: bool) -> dict | None:
     """Config 5: Store path (gather complete chunks -> D2H -> LRU publication) for 36 layers."""
     cfg = STORE_CONFIG
     device = torch.device("cuda", local)
@@ -1123,7 +1241,7 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
     rng = np.random.default_rng(9)
     rng_tokens = rng.integers(0, 151_936, size=(cfg["requests"], cfg["tokens"]), dtype=np.int64)
     blocks = rng.permutation(cfg["requests"] * cfg["tokens"] // cfg["block_size"])
-    metas = [store_metadata(cfg, step, rng_tokens, blocks) for step in range(max(args.warmup, 3) + args.steps)]
+    metas = [store_metadata(cfg, step, rng_tokens, blocks) for step in range(max(args.warmup, 3) + steps)]
     # the serving process freezes its startup heap before taking requests
     # (vllm/v1/engine/core.py: freeze_gc_heap after init), so a full collection
     # walks only what serving allocated; the pauses inside the timed steps are reported
@@ -1144,15 +1262,15 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks, gc_pauses:
         start.record()
-        for step in range(args.steps):
+        for step in range(steps):
             store_step(connector, caches, metas[max(args.warmup, 3) + step])
         end.record()
         torch.cuda.synchronize(device)
     barrier(world)
-    ms = max_over_ranks(start.elapsed_time(end), world, device) / args.steps
+    ms = max_over_ranks(start.elapsed_time(end), world, device) / steps
     events = pipeline.kernel_events
     pipeline.kernel_events = None
-    d2h = (pipeline.d2h_bytes - d2h_before) // args.steps  # chunks rejected under pressure are not copied
+    d2h = (pipeline.d2h_bytes - d2h_before) // steps  # chunks rejected under pressure are not copied
     in_step_us = sum(b.elapsed_time(e) for b, e, _ in events) / len(events) * 1e3
     replay_launches = 288
     # K+V rows read from the pages and written to the staging
@@ -1164,18 +1282,19 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
     traffic = load_traffic().get(f"{cfg['name']}:store_gather:tp{world}")
     store = connector._store
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and cpu_on:
         import oracle
 
         threads = oracle.threads(0)
         sample = store_cpu_sample(cfg, heads, threads)
         cpu = {"value": sample["value"], "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": "oracle gather of 4 requests x 1 layer into host memory, extrapolated to 64 x 36"}
+    line = None
     if rank == 0:
         value = step_tokens / (ms / 1e3)
-        print(json.dumps({
+        line = {
             "metric": "stored prompt tokens/s (all layers: gather + D2H + LRU publication)", "value": value,
-            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": max(args.warmup, 3),
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 pages, new token ids every step)",
             "config": {"workload": cfg["name"], "requests": cfg["requests"], "tokens_per_request": cfg["tokens"],
@@ -1207,84 +1326,20 @@ def store_bench(args, world: int, rank: int, local: int) -> None:
                               "its D2H, without it every chunk is copied and the surplus fails at "
                               "publication (d2h_bytes_per_step shows which)"},
             "clocks": clocks.summary(), "cpu_baseline": cpu,
-        }), flush=True)
+        }
     connector.close()
+    del connector, caches
     gc.unfreeze()
+    return line
 
 
-def main() -> None:
-    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=None,
-                        help="timed steps (default 200; 5 for the seconds-long Store step of config 5)")
-    parser.add_argument("--warmup", type=int, default=3)
-    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--config", type=int, choices=sorted(CONFIGS) + [3, 5, 6], default=2)
-    parser.add_argument("--e2e-steps", type=int, default=5)
-    parser.add_argument("--sample-layers", type=int, default=2)
-    parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--no-e2e", action="store_true")
-    parser.add_argument("--tp-shard", type=int, default=0,
-                        help="run one rank's KV-head shard of an N-way TP step on this GPU alone "
-                             "(no all-reduce; per-rank kernel study)")
-    parser.add_argument("--no-graph", action="store_true",
-                        help="time eager launches instead of CUDA-graph replays of the step")
-    parser.add_argument("--layers", type=int, default=0,
-                        help="override the layer count (small profiling captures only)")
-    parser.add_argument("--attention-tokens", type=int, default=0,
-                        help="config 6 context length override (small profiling captures only)")
-    parser.add_argument("--store-no-arena", action="store_true",
-                        help="config 5: per-batch pinned buffers instead of the pinned arena (A/B study)")
-    parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
-                        help="host->device mode of the e2e loader (CACHEBLEND_B200_LOAD)")
-    args = parser.parse_args()
-    if args.steps is None:
-        args.steps = 5 if args.config == 5 else 200
-    if args.config == 3:
-        world, rank, local, group = dist_setup(args)
-        sparse_q_bench(args, world, rank, local)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
-    if args.config == 6:
-        global ATTENTION_KEYS
-        ATTENTION_KEYS = args.attention_tokens
-        world, rank, local, group = dist_setup(args)
-        if args.impl == "reference":
-            if rank == 0:
-                attention_reference(args)
-        else:
-            attention_bench(args, world, rank, local)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
-    if args.config == 5:
-        world, rank, local, group = dist_setup(args)
-        if args.impl == "reference":
-            if rank == 0:
-                store_reference(args, world)
-        else:
-            store_bench(args, world, rank, local)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
-    shape = CONFIGS[args.config]
-    if args.layers:
-        from dataclasses import replace
-
-        shape = replace(shape, name=f"{shape.name}-{args.layers}layers", layers=args.layers)
-    if args.load_mode:
-        os.environ["CACHEBLEND_B200_LOAD"] = args.load_mode
-    world, rank, local, group = dist_setup(args)
-    if args.impl == "reference":
-        run_reference(args, shape, world, rank)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
-
+def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group, steps: int,
+                    e2e_on: bool, cpu_on: bool) -> dict | None:
+    """Load + K-deviation score/select + commit for one request through every layer
+    (configs 1, 2, 4); returns rank 0's line."""
     device = torch.device("cuda", local)
     shard = args.tp_shard if args.tp_shard and world == 1 else world
-    wl = Workload(shape, shard, rank, device, host_store=not args.no_e2e)
+    wl = Workload(shape, shard, rank, device, host_store=e2e_on)
     path = DevicePath(wl, tp_group=group)
     stream = torch.cuda.Stream(device)
     # warm-up (also builds the check-layer fresh K)
@@ -1297,8 +1352,9 @@ def main() -> None:
     barrier(world)
     torch.cuda.synchronize(device)
     path.timing = True
+    eager_steps = min(steps, 50)
     with torch.cuda.stream(stream):
-        for _ in range(min(args.steps, 50)):
+        for _ in range(eager_steps):
             path.step(stream)
     torch.cuda.synchronize(device)
     path.timing = False
@@ -1317,14 +1373,14 @@ def main() -> None:
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks, torch.cuda.stream(stream):
         start.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             path.step(stream)
         end.record(stream)
         torch.cuda.synchronize(device)
     barrier(world)
     path.release()
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world, device)
-    ms_per_step = elapsed_ms / args.steps
+    ms_per_step = elapsed_ms / steps
     span = wl.act
     value = span / (ms_per_step / 1e3)
 
@@ -1347,45 +1403,132 @@ def main() -> None:
                 "peak_source": peaks["source"]}
     per_kernel = {name: {"avg_us": None if ms is None else ms * 1e3,
                          "gbs": None if ms is None else alg[name] / (ms / 1e3) / 1e9,
+                         "frac": None if ms is None else alg[name] / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
                          "eager_event_us": None if eager_ms[name] is None else eager_ms[name] * 1e3,
-                         "launches_per_step": len(path.events[name]) // min(args.steps, 50)}
+                         "launches_per_step": len(path.events[name]) // eager_steps}
                   for name, ms in kernel_ms.items()}
 
     # ---- e2e: public API with host buffers (H2D of reused chunks inside the step)
     e2e = None
-    if not args.no_e2e:
+    if e2e_on:
         e2e = run_e2e(args, wl, device, world, group, span)
+    del path, wl
+    torch.cuda.empty_cache()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and cpu_on:
         import oracle
 
-        threads = oracle.threads(0)
-        sample = cpu_sample(shape, args.sample_layers, threads)
-        cpu = {"value": sample["value"], "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{args.sample_layers} of {shape.layers} layers + check-layer scoring, extrapolated"}
+        cpu = cpu_baseline(shape, oracle.threads(0))
+    if rank != 0:
+        return None
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
+        "config": workload_config(shape, span, shape.kv_heads // shard, world, shard),
+        "gpu_launches": (2 * shape.layers + 2) * steps,
+        "launch": "eager, one stream" if args.no_graph else (
+            ("cuda-graph" if world == 1 else "two cuda-graphs around the NCCL all-reduce")
+            + (", loads on a side stream beside the commits" if 2 * shape.kv_heads // shard * 128 < 2048
+               else "")),
+        "kernel_timing": ("CUDA events around each launch in an eager pass of the same steps"
+                          + ("" if args.no_graph else "; avg_us: each kernel's launches of one step replayed "
+                             "as a CUDA graph between two events (deviation / select: ten launches over "
+                             "four rotating input sets, 512 MiB, so each reads its inputs from HBM)")),
+        "roofline": roofline, "kernels": per_kernel, "e2e": e2e,
+        "clocks": clocks.summary(), "cpu_baseline": cpu,
+    }
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
-            "config": {"workload": shape.name, "tokens": shape.tokens, "span_tokens": span,
-                       "layers": shape.layers, "kv_heads_per_rank": wl.heads, "hit_chunks": shape.hit_chunks,
-                       "block_size": shape.block_size, "check_layer": shape.check_layer, "ratio": shape.ratio,
-                       "parallelism": f"tp{world}" if shard == world else f"one rank of tp{shard}",
-                       "l2": "inputs larger than L2 (each layer touches "
-                       f"{(alg['load'] + alg['scatter']) / 2**20:.0f} MiB)"},
-            "gpu_launches": path.launches_per_step() * args.steps,
-            "launch": "eager, one stream" if args.no_graph else (
-                ("cuda-graph" if world == 1 else "two cuda-graphs around the NCCL all-reduce")
-                + (", loads on a side stream beside the commits" if wl.row_bytes < 2048 else "")),
-            "kernel_timing": ("CUDA events around each launch in an eager pass of the same steps"
-                              + ("" if args.no_graph else "; avg_us: each kernel's launches of one step "
-                                 "(ten for deviation/select) replayed as a CUDA graph between two events")),
-            "roofline": roofline, "kernels": per_kernel, "e2e": e2e,
-            "clocks": clocks.summary(), "cpu_baseline": cpu,
-        }
+
+def extra_configs(args, local: int) -> dict:
+    """Configs 3, 4 and 5 at one GPU with few steps, for the default run's line."""
+    out = {}
+    gc.collect()
+    torch.cuda.empty_cache()
+    cpu_on = not args.no_cpu_baseline
+    began = time.perf_counter()
+    out["3"] = sparse_q_bench(args, 1, 0, local, steps=20, cpu=cpu_on)
+    out["4"] = deviation_bench(args, CONFIGS[4], 1, 0, local, None, steps=20, e2e_on=not args.no_e2e,
+                               cpu_on=cpu_on)
+    gc.collect()
+    torch.cuda.empty_cache()
+    out["5"] = store_bench(args, 1, 0, local, steps=3, cpu_on=cpu_on)
+    for key, line in out.items():
+        if line is not None:
+            line["config_index"] = int(key)
+    out["wall_s"] = time.perf_counter() - began
+    return out
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=None,
+                        help="timed steps (default 200; 5 for the seconds-long Store step of config 5)")
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--config", type=int, choices=sorted(CONFIGS) + [3, 5, 6], default=2)
+    parser.add_argument("--e2e-steps", type=int, default=5)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-extra-configs", action="store_true",
+                        help="config 2 at N=1 only: skip the configs 3/4/5 lines added under 'configs'")
+    parser.add_argument("--tp-shard", type=int, default=0,
+                        help="run one rank's KV-head shard of an N-way TP step on this GPU alone "
+                             "(no all-reduce; per-rank kernel study)")
+    parser.add_argument("--no-graph", action="store_true",
+                        help="time eager launches instead of CUDA-graph replays of the step")
+    parser.add_argument("--layers", type=int, default=0,
+                        help="override the layer count (small profiling captures only)")
+    parser.add_argument("--attention-tokens", type=int, default=0,
+                        help="config 6 context length override (small profiling captures only)")
+    parser.add_argument("--store-no-arena", action="store_true",
+                        help="config 5: per-batch pinned buffers instead of the pinned arena (A/B study)")
+    parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
+                        help="host->device mode of the e2e loader (CACHEBLEND_B200_LOAD)")
+    args = parser.parse_args()
+    if args.steps is None:
+        args.steps = 5 if args.config == 5 else 200
+    if args.load_mode:
+        os.environ["CACHEBLEND_B200_LOAD"] = args.load_mode
+    world, rank, local, group = dist_setup(args)
+    line = None
+    if args.config == 3:
+        if args.impl == "reference":
+            if rank == 0:
+                sparse_q_reference(args)
+        else:
+            line = sparse_q_bench(args, world, rank, local, args.steps, not args.no_cpu_baseline)
+    elif args.config == 6:
+        global ATTENTION_KEYS
+        ATTENTION_KEYS = args.attention_tokens
+        if args.impl == "reference":
+            if rank == 0:
+                attention_reference(args)
+        else:
+            attention_bench(args, world, rank, local)
+    elif args.config == 5:
+        if args.impl == "reference":
+            if rank == 0:
+                store_reference(args, world)
+        else:
+            line = store_bench(args, world, rank, local, args.steps, not args.no_cpu_baseline)
+    else:
+        shape = CONFIGS[args.config]
+        if args.layers:
+            from dataclasses import replace
+
+            shape = replace(shape, name=f"{shape.name}-{args.layers}layers", layers=args.layers)
+        if args.impl == "reference":
+            run_reference(args, shape, world, rank)
+        else:
+            line = deviation_bench(args, shape, world, rank, local, group, args.steps, not args.no_e2e,
+                                   not args.no_cpu_baseline)
+            if (line is not None and world == 1 and args.config == 2 and not args.tp_shard
+                    and not args.layers and not args.no_extra_configs):
+                line["configs"] = extra_configs(args, local)
+    if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -81,8 +81,7 @@ def test_bench_reference_arm_under_torchrun():
     env = dict(os.environ, OMP_NUM_THREADS="2")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(REPO / "bench.py"),
-           "--impl", "reference", "--gpus", "2", "--config", "1", "--steps", "1", "--warmup", "0",
-           "--sample-layers", "1"]
+           "--impl", "reference", "--gpus", "2", "--config", "1", "--steps", "1", "--warmup", "0"]
     proc = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stderr[-2000:]
     lines = [line for line in proc.stdout.splitlines() if line.startswith("{")]
@@ -90,3 +89,5 @@ def test_bench_reference_arm_under_torchrun():
     line = json.loads(lines[0])
     assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "port" and line["e2e"]["h2d_bytes_per_step"] == 0
+    # the same workload description as the GPU arm prints
+    assert line["config"]["workload"] == "qwen3-0.6b-cpu-plumbing" and line["config"]["parallelism"] == "tp2"
