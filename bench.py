@@ -1333,6 +1333,47 @@ def store_bench(args, world: int, rank: int, local: int, steps: int, cpu_on: boo
     return line
 
 
+def host_link_scan(args, world: int, rank: int, local: int) -> dict | None:
+    """Pinned host <-> device copy bandwidth with every rank copying at once (the
+    multi-GPU e2e line rests on the box's aggregate host link).  Each rank copies
+    a 1 GiB pinned buffer to its GPU and back, ``args.steps`` times, between
+    barriers; the aggregate is all ranks' bytes over the slowest rank's time."""
+    device = torch.device("cuda", local)
+    nbytes = 1 << 30
+    host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host.fill_(1)
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    out = {}
+    for name, dst, src in (("h2d", dev, host), ("d2h", host, dev)):
+        for _ in range(2):
+            dst.copy_(src, non_blocking=True)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            dst.copy_(src, non_blocking=True)
+        end.record()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        mine = start.elapsed_time(end) / 1e3
+        slowest = max_over_ranks(mine, world, device)
+        out[name] = {"per_rank_gbs": nbytes * args.steps / mine / 1e9,
+                     "aggregate_gbs": world * nbytes * args.steps / slowest / 1e9}
+    gathered = [None] * world
+    if world > 1:
+        torch.distributed.all_gather_object(gathered, out)
+    else:
+        gathered = [out]
+    if rank != 0:
+        return None
+    return {"metric": "pinned host <-> device copy GB/s, all ranks at once", "n_gpus": world,
+            "steps": args.steps, "bytes_per_copy": nbytes,
+            "h2d_aggregate_gbs": out["h2d"]["aggregate_gbs"], "d2h_aggregate_gbs": out["d2h"]["aggregate_gbs"],
+            "per_rank": gathered}
+
+
 def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group, steps: int,
                     e2e_on: bool, cpu_on: bool) -> dict | None:
     """Load + K-deviation score/select + commit for one request through every layer
@@ -1408,6 +1449,24 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
                          "launches_per_step": len(path.events[name]) // eager_steps}
                   for name, ms in kernel_ms.items()}
 
+    # ---- the step's one collective: the fp32 score all-reduce (NCCL), timed alone
+    allreduce = None
+    if world > 1:
+        for _ in range(5):
+            torch.distributed.all_reduce(path.scores, group=group)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(50):
+            torch.distributed.all_reduce(path.scores, group=group)
+        a1.record()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        us = max_over_ranks(a0.elapsed_time(a1), world, device) * 1e3 / 50
+        allreduce = {"avg_us": us, "bytes": path.scores.numel() * 4, "share_of_step": us / (ms_per_step * 1e3),
+                     "timing": "50 back-to-back NCCL all-reduces of the step's fp32 score vector, max over ranks"}
+
     # ---- e2e: public API with host buffers (H2D of reused chunks inside the step)
     e2e = None
     if e2e_on:
@@ -1436,7 +1495,7 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
                           + ("" if args.no_graph else "; avg_us: each kernel's launches of one step replayed "
                              "as a CUDA graph between two events (deviation / select: ten launches over "
                              "four rotating input sets, 512 MiB, so each reads its inputs from HBM)")),
-        "roofline": roofline, "kernels": per_kernel, "e2e": e2e,
+        "roofline": roofline, "kernels": per_kernel, "e2e": e2e, "allreduce": allreduce,
         "clocks": clocks.summary(), "cpu_baseline": cpu,
     }
 
@@ -1487,6 +1546,8 @@ def main() -> None:
                         help="config 5: per-batch pinned buffers instead of the pinned arena (A/B study)")
     parser.add_argument("--load-mode", choices=["copy", "zerocopy"], default=None,
                         help="host->device mode of the e2e loader (CACHEBLEND_B200_LOAD)")
+    parser.add_argument("--host-link", action="store_true",
+                        help="measure pinned host<->device bandwidth with every rank copying at once")
     args = parser.parse_args()
     if args.steps is None:
         args.steps = 5 if args.config == 5 else 200
@@ -1494,7 +1555,9 @@ def main() -> None:
         os.environ["CACHEBLEND_B200_LOAD"] = args.load_mode
     world, rank, local, group = dist_setup(args)
     line = None
-    if args.config == 3:
+    if args.host_link:
+        line = host_link_scan(args, world, rank, local)
+    elif args.config == 3:
         if args.impl == "reference":
             if rank == 0:
                 sparse_q_reference(args)
