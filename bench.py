@@ -32,6 +32,7 @@ host cores with the same metric (rank 0 only).
 from __future__ import annotations
 
 import argparse
+import ctypes
 import gc
 import json
 import math
@@ -250,7 +251,16 @@ class DevicePath:
         self.selected = torch.empty(gaps + self.k, dtype=torch.long, device=dev)
         # fresh K for the check layer = cached hits + noise, prepared once
         self.fresh = None
-        self.events: dict[str, list] = {"load": [], "scatter": [], "deviation": [], "select": []}
+        # one rank: the check layer's deviation and select run as one fused launch
+        # (cb_kv_deviation_select); with TP the score all-reduce sits between them
+        self.fused = tp_group is None
+        self.fused_workspace = None
+        if self.fused:
+            size = ctypes.c_int64(0)
+            self.native.call("cb_kv_deviation_select_workspace_size", ctypes.addressof(size))
+            self.fused_workspace = torch.zeros(size.value, dtype=torch.uint8, device=dev)
+        score_kinds = ["deviation_select"] if self.fused else ["deviation", "select"]
+        self.events: dict[str, list] = {name: [] for name in ["load", "scatter", *score_kinds]}
         self.timing = False
         self.graphs: list = []
         self.side = torch.cuda.Stream(dev)  # the loader's Load stream in the pipelined step
@@ -287,6 +297,8 @@ class DevicePath:
         return buf
 
     def score(self, buf: torch.Tensor, stream) -> torch.Tensor:
+        if self.fused:
+            return self.deviation_select(buf, stream)
         self.deviation(buf, stream)
         if self.tp_group is not None:
             torch.distributed.all_reduce(self.scores, group=self.tp_group)
@@ -305,6 +317,31 @@ class DevicePath:
             plan.apc_prefix_tokens, wl.act, width, 0, self.scores.data_ptr(), stream.cuda_stream,
         )
         self._ev_end("deviation", ev, stream)
+
+    def _fresh_for(self, buf: torch.Tensor) -> torch.Tensor:
+        wl, plan = self.wl, self.wl.plan
+        if self.fresh is None:
+            k_plane = buf[0].reshape(plan.allocation_end, -1)
+            self.fresh = (k_plane[plan.apc_prefix_tokens:].float() + wl.fresh_noise).to(torch.bfloat16)
+        return self.fresh
+
+    def deviation_select(self, buf: torch.Tensor, stream, rotation: tuple | None = None) -> torch.Tensor:
+        """The check layer's deviation and select in one launch (one rank)."""
+        wl, shape, plan = self.wl, self.wl.shape, self.wl.plan
+        fresh = self._fresh_for(buf)
+        cached = buf
+        if rotation is not None:
+            fresh, cached = rotation
+        width = wl.heads * shape.head_dim
+        ev = self._ev("deviation_select", stream)
+        self.native.call(
+            "cb_kv_deviation_select", fresh.data_ptr(), width * 2, cached.data_ptr(), width * 2,
+            plan.allocation_end, 0, plan.apc_prefix_tokens, wl.act, width, 0, self.base_mask.data_ptr(),
+            self.k, self.scores.data_ptr(), self.selected.data_ptr(), self.selected.numel(),
+            self.fused_workspace.data_ptr(), self.fused_workspace.numel(), stream.cuda_stream,
+        )
+        self._ev_end("deviation_select", ev, stream)
+        return self.selected
 
     def deviation_rotating(self, index: int, rotation: list, stream) -> None:
         """The check layer's deviation launch on the ``index``-th copy of its inputs."""
@@ -389,10 +426,13 @@ class DevicePath:
             if side is not main:
                 main.wait_event(done(side))
             if layer == check:
-                self.deviation(self.staging[layer % 2], main)
-                if part == "until":
-                    break
-                self.select(main)
+                if self.fused:
+                    self.deviation_select(self.staging[layer % 2], main)
+                else:
+                    self.deviation(self.staging[layer % 2], main)
+                    if part == "until":
+                        break
+                    self.select(main)
             self.commit(layer, self.staging[layer % 2], main)
             if side is not main:
                 committed[layer] = done(main)
@@ -427,12 +467,16 @@ class DevicePath:
             "load": (layers, lambda: [self.load_layer(layer, stream) for layer in range(layers)]),
             "scatter": (layers, lambda: [self.commit(layer, self.staging[layer % 2], stream)
                                          for layer in range(layers)]),
-            # single launches per step: ten back to back over four rotating input sets (512 MiB
-            # at 8 heads), so each launch reads its fresh and cached K from HBM, not from L2
-            "deviation": (10, lambda: [self.deviation_rotating(i % len(rotation), rotation, stream)
-                                       for i in range(10)]),
-            "select": (10, lambda: [self.select(stream) for _ in range(10)]),
         }
+        # single launches per step: ten back to back over four rotating input sets (512 MiB
+        # at 8 heads), so each launch reads its fresh and cached K from HBM, not from L2
+        if self.fused:
+            kinds["deviation_select"] = (10, lambda: [self.deviation_select(
+                None, stream, rotation[i % len(rotation)]) for i in range(10)])
+        else:
+            kinds["deviation"] = (10, lambda: [self.deviation_rotating(i % len(rotation), rotation, stream)
+                                               for i in range(10)])
+            kinds["select"] = (10, lambda: [self.select(stream) for _ in range(10)])
         out = {}
         for name, (count, launch) in kinds.items():
             torch.cuda.synchronize(self.wl.device)
@@ -456,7 +500,7 @@ class DevicePath:
 def e2e_step(wl: Workload, load_stream, tp_group=None) -> tuple[torch.Tensor, int]:
     """One request through the public API: loader (H2D from the pinned store) + select."""
     from cacheblend_b200.loader import PagedBlendLoader
-    from cacheblend_b200.selection import kv_deviation, select_tokens
+    from cacheblend_b200.selection import deviation_select, kv_deviation, select_tokens
 
     shape, plan = wl.shape, wl.store_plan
     loader = PagedBlendLoader(wl.pages, wl.store, "bench-request", plan, wl.slot_mapping,
@@ -470,8 +514,12 @@ def e2e_step(wl: Workload, load_stream, tp_group=None) -> tuple[torch.Tensor, in
             k_plane = buf[0].reshape(plan.allocation_end, -1)
             if not hasattr(wl, "e2e_fresh"):
                 wl.e2e_fresh = (k_plane[plan.apc_prefix_tokens:].float() + wl.fresh_noise).to(torch.bfloat16)
-            scores = kv_deviation(wl.e2e_fresh, k_plane, absolute_offset=plan.apc_prefix_tokens)
-            selected = select_tokens(scores, wl.gap_mask, shape.ratio, tp_group=tp_group)
+            if tp_group is None:  # one rank: deviation and select in one launch
+                selected, _ = deviation_select(wl.e2e_fresh, k_plane, wl.gap_mask, shape.ratio,
+                                               absolute_offset=plan.apc_prefix_tokens)
+            else:
+                scores = kv_deviation(wl.e2e_fresh, k_plane, absolute_offset=plan.apc_prefix_tokens)
+                selected = select_tokens(scores, wl.gap_mask, shape.ratio, tp_group=tp_group)
         loader.commit(layer, buf)
     host = selected.to("cpu")  # device -> host read of the step's result
     return host, host.numel() * host.element_size()
@@ -562,6 +610,8 @@ def algorithmic_bytes(wl: Workload) -> dict[str, float]:
         "scatter": 2 * (2 * rb * act),
         "deviation": 2 * rb * act + 4 * act,
         "select": 4 * act * 6 + act,
+        # one pass over both K planes, the scores written and read back once by the last cluster
+        "deviation_select": 2 * rb * act + 4 * act + 4 * act + act,
     }
 
 

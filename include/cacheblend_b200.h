@@ -245,6 +245,37 @@ CB_API int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t
                    int64_t* out_index, int64_t out_capacity, void* stream);
 
 /*
+ * Bytes of the workspace cb_kv_deviation_select needs (a 2048-bin histogram
+ * and a completion ticket).
+ */
+CB_API int cb_kv_deviation_select_workspace_size(int64_t* bytes);
+
+/*
+ * K-deviation score and recompute selection of a single-rank check layer in
+ * one launch: cb_kv_deviation's scores (bit-identical, written to `scores`)
+ * and cb_select_topk's ascending index set of base_mask[i] != 0 united with
+ * the k largest non-base scores (out_index, at most out_capacity entries).
+ * Replaces the deviation expression and `_select`
+ * (cacheblend_vllm/ascend.py:534-543, 757-796) when no TP all-reduce sits
+ * between them.  8-CTA clusters score the tokens and histogram the top 11
+ * bits of the non-base scores into `workspace`; the cluster that finishes
+ * last (a ticket in the workspace) runs the remaining radix passes and the
+ * ordered compaction.  `workspace` (16-byte aligned device memory,
+ * cb_kv_deviation_select_workspace_size bytes) must be zero before its first
+ * use; every call leaves it zero again, and calls sharing one workspace must
+ * not overlap on the GPU.  Rows that are not 16-byte aligned, more than
+ * 327,680 tokens, or a NULL workspace fall back to the two launches
+ * (cb_kv_deviation, then cb_select_topk) with the same results.
+ */
+CB_API int cb_kv_deviation_select(const void* fresh, int64_t fresh_row_stride, const void* cached,
+                                  int64_t cached_row_stride, int64_t cached_rows,
+                                  const int64_t* abs_index, int64_t abs_offset,
+                                  int64_t num_tokens, int64_t width, int dtype,
+                                  const uint8_t* base_mask, int64_t k, float* scores,
+                                  int64_t* out_index, int64_t out_capacity, void* workspace,
+                                  int64_t workspace_bytes, void* stream);
+
+/*
  * Workspace bytes cb_blend_attention needs (dense per-KV-head query rows, the
  * transposed values, row positions and tile bounds).  Same shape limits as
  * Sparse-Q: head_size 128, bf16 or fp16, (q heads / KV heads) dividing 128.

@@ -21,7 +21,7 @@ LIB_PATH = Path(
     os.environ.get("CACHEBLEND_B200_LIB")
     or Path(__file__).resolve().parent / "_lib" / "libcacheblend_b200.so"
 )
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 CB_OK = 0
 CB_ERR_INVALID = -1
@@ -101,6 +101,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_ptr, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i32, _ptr, _ptr],
     ),
     "cb_select_topk": (_i32, [_ptr, _ptr, _i64, _i64, _ptr, _i64, _ptr]),
+    "cb_kv_deviation_select_workspace_size": (_i32, [_ptr]),
+    "cb_kv_deviation_select": (
+        _i32,
+        [_ptr, _i64, _ptr, _i64, _i64, _ptr, _i64, _i64, _i64, _i32, _ptr, _i64, _ptr, _ptr, _i64,
+         _ptr, _i64, _ptr],
+    ),
     "cb_blend_attention_workspace_size": (_i32, [_i64, _i64, _i64, _i64, _i64, _i32, _ptr]),
     "cb_blend_attention": (
         _i32,

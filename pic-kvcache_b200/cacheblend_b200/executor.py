@@ -37,7 +37,8 @@ import torch
 from .attention import attention_supported, attention_workspace_bytes, blend_attention
 from .config import CacheBlendConfig
 from .rope import validate_rope_support
-from .selection import kv_deviation, select_tokens, selection_overlap, sparse_q_scores
+from .selection import (deviation_select, kv_deviation, select_tokens, selection_overlap,
+                        sparse_q_scores, tp_world_size)
 from .trace import PipelineTracer
 from .types import BlendPlan
 
@@ -244,8 +245,12 @@ class Qwen3BlendExecutor:
         choice = _Choice()
         by_deviation = by_query = None
         if strategy in ("kv_deviation", "compare"):
-            deviation = kv_deviation(rows.k, cached_k, rows.absolute)
-            by_deviation = self._select(deviation, gaps, layer_id)
+            ratio = self.config.ratio_for_layer(layer_id)
+            if self.config.tp_global_selection and tp_world_size(self.tp_group) > 1:
+                deviation = kv_deviation(rows.k, cached_k, rows.absolute)
+                by_deviation = self._select(deviation, gaps, layer_id)  # all-reduce, then select
+            else:  # this rank's scores alone: score and select in one launch
+                by_deviation, _ = deviation_select(rows.k, cached_k, gaps, ratio, rows.absolute)
             choice.before_attention = by_deviation
         if strategy in ("sparse_q", "compare"):
             attn = layer.self_attn.attn

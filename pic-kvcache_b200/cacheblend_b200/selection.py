@@ -8,6 +8,8 @@
 * ``select_tokens`` -- optional TP all-reduce of the scores (every rank then
   runs the same deterministic kernel, so the reference's rank-0 broadcast is
   unnecessary) and ``cb_select_topk``: ascending indices of base ∪ top-k.
+* ``deviation_select`` -- both in one launch (``cb_kv_deviation_select``) when
+  no all-reduce sits between them (one rank, or per-rank selection).
 * ``sparse_q_masks`` -- query set, forced set and tail fallback of
   ``_sparse_q_scores`` (ascend.py:652-673); these depend only on the plan's
   gap mask, so they are computed on the host without a device round trip.
@@ -125,6 +127,81 @@ def select_from_scores(
         _native.stream_handle(stream),
     )
     return out
+
+
+_FUSED_WORKSPACES: dict[torch.device, torch.Tensor] = {}
+
+
+def _fused_workspace(device: torch.device) -> torch.Tensor:
+    """The per-device workspace of cb_kv_deviation_select (zeroed once; every call
+    leaves it zero again).  Calls on one device are stream-ordered by the caller."""
+    workspace = _FUSED_WORKSPACES.get(device)
+    if workspace is None:
+        size = ctypes.c_int64(0)
+        _native.call("cb_kv_deviation_select_workspace_size", ctypes.addressof(size))
+        workspace = torch.zeros(size.value, dtype=torch.uint8, device=device)
+        _FUSED_WORKSPACES[device] = workspace
+    return workspace
+
+
+def deviation_select(
+    fresh_key: torch.Tensor,
+    cached_key: torch.Tensor,
+    gap_mask: torch.Tensor | np.ndarray,
+    ratio: float,
+    absolute_indices: torch.Tensor | None = None,
+    absolute_offset: int = 0,
+    stream: torch.cuda.Stream | None = None,
+    base_mask_device: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """K-deviation scores and ``_select`` of one rank in a single launch
+    (cb_kv_deviation_select): (ascending int64 indices, fp32 scores).  The budget
+    comes from the host gap mask (ascend.py:775-786), so nothing is read back.
+    ``base_mask_device``: the gap mask already on the device as uint8 (no upload;
+    what a CUDA-graph capture needs)."""
+    _native.require_cuda(fresh_key, cached_key)
+    fresh = fresh_key.reshape(fresh_key.shape[0], -1)
+    cached = cached_key.reshape(cached_key.shape[0], -1)
+    if fresh.shape[1] != cached.shape[1]:
+        raise ValueError("fresh and cached keys must have the same row width")
+    if fresh.dtype != cached.dtype:
+        raise ValueError("fresh and cached keys must have the same dtype")
+    if fresh.stride(1) != 1:
+        fresh = fresh.contiguous()
+    if cached.stride(1) != 1:
+        cached = cached.contiguous()
+    gaps = _as_host_mask(gap_mask, "gap_mask")
+    tokens = fresh.shape[0]
+    if gaps.shape[0] != tokens:
+        raise ValueError("gap mask must match the fresh key rows")
+    gap_count = int(gaps.sum())
+    k = recompute_budget(tokens, gap_count, gap_count, ratio)
+    device = fresh.device
+    scores = torch.empty(tokens, dtype=torch.float32, device=device)
+    selected = torch.empty(gap_count + k, dtype=torch.long, device=device)
+    if tokens == 0:
+        return selected, scores
+    index_ptr = 0
+    if absolute_indices is not None:
+        absolute_indices = absolute_indices.to(device=device, dtype=torch.long).contiguous()
+        if absolute_indices.numel() != tokens:
+            raise ValueError("one absolute index per fresh key row is required")
+        index_ptr = absolute_indices.data_ptr()
+    if base_mask_device is None:
+        base = _upload(gaps.astype(np.uint8), device)
+    else:
+        if base_mask_device.dtype != torch.uint8 or base_mask_device.numel() != tokens:
+            raise ValueError("base mask must be a uint8 vector shaped like the fresh rows")
+        base = base_mask_device
+    workspace = _fused_workspace(device)
+    esize = fresh.element_size()
+    _native.call(
+        "cb_kv_deviation_select", fresh.data_ptr(), fresh.stride(0) * esize, cached.data_ptr(),
+        cached.stride(0) * esize, cached.shape[0], index_ptr, absolute_offset, tokens, fresh.shape[1],
+        _native.dtype_code(fresh.dtype), base.data_ptr(), k, scores.data_ptr(), selected.data_ptr(),
+        selected.numel(), workspace.data_ptr(), workspace.numel(), _native.stream_handle(stream),
+    )
+    return selected, scores
 
 
 def tp_all_reduce(scores: torch.Tensor, tp_group) -> torch.Tensor:

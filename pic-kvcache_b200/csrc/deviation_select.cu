@@ -45,26 +45,33 @@ __device__ __forceinline__ void acc_vec16(const uint4& fv, const uint4& cv, floa
   }
 }
 
-template <typename T, bool VEC>
-__global__ void __launch_bounds__(256) deviation_kernel(const char* __restrict__ fresh,
-                                                        int64_t fresh_stride,
-                                                        const char* __restrict__ cached,
-                                                        int64_t cached_stride,
-                                                        int64_t cached_rows,
-                                                        const int64_t* __restrict__ abs_index,
-                                                        int64_t abs_offset, int64_t n, int width,
-                                                        float* __restrict__ scores) {
+// Deviation operands of one launch.
+struct DevArgs {
+  const char* fresh;
+  int64_t fresh_stride;
+  const char* cached;
+  int64_t cached_stride;
+  int64_t cached_rows;
+  const int64_t* abs_index;
+  int64_t abs_offset;
+  int64_t n;
+};
+
+// Scores every token this warp owns (tokens warp, warp + nwarps, ...): one warp
+// per token, the fixed association order above; `sink(i, score)` runs on lane 0.
+// A row whose cached index falls outside the cached rows scores NaN, unread.
+template <typename T, bool VEC, typename Sink>
+__device__ __forceinline__ void score_rows(const DevArgs& a, int width, int64_t warp, int64_t nwarps,
+                                           Sink&& sink) {
   const int lane = threadIdx.x & 31;
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t i = warp; i < n; i += nwarps) {
-    const int64_t ai = abs_index ? __ldg(abs_index + i) : abs_offset + i;
-    if (ai < 0 || ai >= cached_rows) {  // never read outside the cached rows
-      if (lane == 0) scores[i] = __int_as_float(0x7fc00000);
+  for (int64_t i = warp; i < a.n; i += nwarps) {
+    const int64_t ai = a.abs_index ? __ldg(a.abs_index + i) : a.abs_offset + i;
+    if (ai < 0 || ai >= a.cached_rows) {  // never read outside the cached rows
+      if (lane == 0) sink(i, __int_as_float(0x7fc00000));
       continue;
     }
-    const char* f = fresh + i * fresh_stride;
-    const char* c = cached + ai * cached_stride;
+    const char* f = a.fresh + i * a.fresh_stride;
+    const char* c = a.cached + ai * a.cached_stride;
     float s = 0.0f;
     if (VEC) {
       const int units = width * static_cast<int>(sizeof(T)) / 16;
@@ -90,48 +97,40 @@ __global__ void __launch_bounds__(256) deviation_kernel(const char* __restrict__
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-    if (lane == 0) scores[i] = s;
+    if (lane == 0) sink(i, s);
   }
 }
 
 // Rows of at most 32 16-byte units (up to two 128-dim bf16 heads per rank):
 // 32 / units tokens share a warp, one unit per lane, and each lane keeps four
-// tokens' loads in flight.  Same association order as deviation_kernel: a
-// lane's unit sum with fmaf, then the xor butterfly; the butterfly steps of
-// offset >= units that deviation_kernel also takes only add lanes holding
-// +0.0 to a sum of squares (>= 0), so skipping them changes no bit.
-template <typename T>
-__global__ void __launch_bounds__(256) deviation_small_kernel(const char* __restrict__ fresh,
-                                                              int64_t fresh_stride,
-                                                              const char* __restrict__ cached,
-                                                              int64_t cached_stride,
-                                                              int64_t cached_rows,
-                                                              const int64_t* __restrict__ abs_index,
-                                                              int64_t abs_offset, int64_t n,
-                                                              int units_log2,
-                                                              float* __restrict__ scores) {
+// tokens' loads in flight.  Same association order as score_rows: a lane's
+// unit sum with fmaf, then the xor butterfly; the butterfly steps of offset >=
+// units that score_rows also takes only add lanes holding +0.0 to a sum of
+// squares (>= 0), so skipping them changes no bit.  `sink` runs on the lane
+// holding unit 0 of each token.
+template <typename T, typename Sink>
+__device__ __forceinline__ void score_small_rows(const DevArgs& a, int units_log2, int64_t warp,
+                                                 int64_t nwarps, Sink&& sink) {
   constexpr int R = 4;  // token groups per warp per iteration
   const int lane = threadIdx.x & 31;
   const int units = 1 << units_log2;
   const int per_warp = 32 >> units_log2;     // tokens per warp instruction
   const int sub = lane >> units_log2;        // this lane's token within the group
   const int q = lane & (units - 1);          // this lane's unit
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int64_t step = nwarps * per_warp * R;
-  for (int64_t base = warp * per_warp * R; base < n; base += step) {
+  for (int64_t base = warp * per_warp * R; base < a.n; base += step) {
     uint4 fv[R], cv[R];
     bool ok[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int64_t i = base + r * per_warp + sub;
       ok[r] = false;
-      if (i < n) {
-        const int64_t ai = abs_index ? __ldg(abs_index + i) : abs_offset + i;
-        ok[r] = ai >= 0 && ai < cached_rows;  // never read outside the cached rows
+      if (i < a.n) {
+        const int64_t ai = a.abs_index ? __ldg(a.abs_index + i) : a.abs_offset + i;
+        ok[r] = ai >= 0 && ai < a.cached_rows;  // never read outside the cached rows
         if (ok[r]) {
-          fv[r] = ld_stream(reinterpret_cast<const uint4*>(fresh + i * fresh_stride) + q);
-          cv[r] = ld_stream(reinterpret_cast<const uint4*>(cached + ai * cached_stride) + q);
+          fv[r] = ld_stream(reinterpret_cast<const uint4*>(a.fresh + i * a.fresh_stride) + q);
+          cv[r] = ld_stream(reinterpret_cast<const uint4*>(a.cached + ai * a.cached_stride) + q);
         }
       }
     }
@@ -141,9 +140,24 @@ __global__ void __launch_bounds__(256) deviation_small_kernel(const char* __rest
       if (ok[r]) acc_vec16<T>(fv[r], cv[r], v);
       for (int o = units >> 1; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
       const int64_t i = base + r * per_warp + sub;
-      if (q == 0 && i < n) scores[i] = ok[r] ? v : __int_as_float(0x7fc00000);
+      if (q == 0 && i < a.n) sink(i, ok[r] ? v : __int_as_float(0x7fc00000));
     }
   }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) deviation_kernel(DevArgs a, int width, float* __restrict__ scores) {
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  score_rows<T, VEC>(a, width, warp, nwarps, [&](int64_t i, float v) { scores[i] = v; });
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) deviation_small_kernel(DevArgs a, int units_log2,
+                                                              float* __restrict__ scores) {
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  score_small_rows<T>(a, units_log2, warp, nwarps, [&](int64_t i, float v) { scores[i] = v; });
 }
 
 // Order-preserving key: larger float -> larger key.// Order-preserving key: larger float -> larger key.  NaN (either sign) is
@@ -343,12 +357,35 @@ __device__ __forceinline__ void find_digit(const uint32_t* hist, int64_t krem, u
   }
 }
 
-__global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
-    const float* __restrict__ scores, const uint8_t* __restrict__ base, int64_t n, int64_t k,
-    int64_t* __restrict__ out, int64_t cap, int slice) {
-  cg::cluster_group cluster = cg::this_cluster();
+// Radix passes still to run: the digit at bits [shift, shift + width).
+struct RadixPass {
+  int shift;
+  int width;
+};
+// four 8-bit digits over the whole 32-bit key
+struct FullPasses {
+  static constexpr int kCount = 4;
+  static __device__ __forceinline__ RadixPass at(int p) { return RadixPass{24 - 8 * p, 8}; }
+};
+// the bits below the 11-bit first digit the fused kernel takes from its global histogram
+struct TailPasses {
+  static constexpr int kCount = 3;
+  static __device__ __forceinline__ RadixPass at(int p) {
+    return p == 0 ? RadixPass{13, 8} : (p == 1 ? RadixPass{5, 8} : RadixPass{0, 5});
+  }
+};
+
+// The selection by one cluster of 8 CTAs (shared by select_cluster_kernel and
+// the fused deviation select): this CTA's slice of order keys and base flags in
+// shared memory, the remaining radix passes merged into rank 0's histogram
+// through DSMEM, then the ordered compaction.  `prefix`, `pmask`, `krem`: the
+// digits already fixed and the rank still sought among keys with that prefix.
+template <typename Passes>
+__device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const float* scores,
+                                               const uint8_t* base, int64_t n, int64_t k,
+                                               int64_t* out, int64_t cap, int slice, uint32_t* dyn,
+                                               uint32_t prefix, uint32_t pmask, int64_t krem) {
   const int rank = static_cast<int>(cluster.block_rank());
-  extern __shared__ __align__(16) uint32_t dyn[];
   uint32_t* keys = dyn;
   uint8_t* flags = reinterpret_cast<uint8_t*>(keys + slice);
   // rank 0's copy is the cluster histogram, double-buffered by pass parity:
@@ -365,14 +402,15 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
   const int64_t hi = lo + slice < n ? lo + slice : n;
   const int m = hi > lo ? static_cast<int>(hi - lo) : 0;
   for (int i = tid; i < m; i += kSelThreads) {
-    keys[i] = order_key(scores[lo + i]);
+    keys[i] = order_key(__ldcg(scores + lo + i));  // L2: other CTAs may have just written them
     flags[i] = base[lo + i] != 0;
   }
-  uint32_t prefix = 0, pmask = 0;
-  int64_t krem = k;
   if (k > 0) {
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
+#pragma unroll 1
+    for (int pass = 0; pass < Passes::kCount; ++pass) {
+      const RadixPass digit = Passes::at(pass);
+      const int shift = digit.shift;
+      const uint32_t digit_mask = (1u << digit.width) - 1u;
       uint32_t* root_hist = cluster.map_shared_rank(&hist[pass & 1][0], 0);
       if (tid < 256) {
         local[tid] = 0;
@@ -385,7 +423,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
       cluster.sync();
       for (int i = tid; i < m; i += kSelThreads) {
         const uint32_t key = keys[i];
-        if (!flags[i] && (key & pmask) == prefix) atomicAdd(&local[(key >> shift) & 255u], 1u);
+        if (!flags[i] && (key & pmask) == prefix) atomicAdd(&local[(key >> shift) & digit_mask], 1u);
       }
       __syncthreads();
       if (tid < 256 && local[tid]) atomicAdd(&root_hist[tid], local[tid]);
@@ -393,7 +431,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
       if (tid < 32) find_digit(root_hist, krem, &s_digit, &s_above);
       __syncthreads();
       prefix |= s_digit << shift;
-      pmask |= 255u << shift;
+      pmask |= digit_mask << shift;
       krem -= s_above;
       __syncthreads();  // all threads read s_digit before the next pass resets it
     }
@@ -443,6 +481,123 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
       ++eq_before;
     }
   }
+}
+
+__global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
+    const float* __restrict__ scores, const uint8_t* __restrict__ base, int64_t n, int64_t k,
+    int64_t* __restrict__ out, int64_t cap, int slice) {
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) uint32_t dyn[];
+  cluster_select<FullPasses>(cluster, scores, base, n, k, out, cap, slice, dyn, 0u, 0u, k);
+}
+
+// ---- fused deviation + selection ---------------------------------------------
+// One launch of 8-CTA clusters for the K-deviation and the selection of a
+// single-rank check layer (ascend.py:534-543 then 757-796).  Every CTA scores
+// its tokens (score_rows / score_small_rows: bit-identical scores) and counts
+// the non-base scores' top 11 key bits in a 2048-bin shared histogram, which it
+// adds into the caller's workspace.  A cluster that has finished fences, and
+// its rank 0 takes a ticket; the cluster holding the last ticket selects: the
+// first digit from the global histogram, the three radix passes over the
+// remaining 21 bits and the ordered compaction of cluster_select.  No CTA waits
+// for another cluster, so nothing spins; the last cluster leaves the histogram
+// and the ticket zeroed for the next call.
+constexpr int kWideBits = 11;
+constexpr int kWideBins = 1 << kWideBits;
+// keys per CTA: 5 bytes each in dynamic shared memory, beside the 8 KiB histogram
+constexpr int kFusedMaxSlice = 40 * 1024;
+
+struct FusedWorkspace {
+  uint32_t hist[kWideBins];
+  uint32_t ticket;
+};
+
+// First (11-bit) digit: warp 0, lane L owns bins 2047 - 64L down to 1984 - 64L.
+__device__ __forceinline__ void find_wide_digit(const uint32_t* hist, int64_t krem, uint32_t* s_digit,
+                                                int64_t* s_above) {
+  const int lane = threadIdx.x;
+  constexpr int kPer = kWideBins / 32;
+  uint32_t sum = 0;
+  for (int j = 0; j < kPer; ++j) sum += __ldcg(hist + kWideBins - 1 - kPer * lane - j);
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const uint32_t above = incl - sum;
+  if ((int64_t)above < krem && (int64_t)incl >= krem) {
+    uint32_t run = above;
+    for (int j = 0; j < kPer; ++j) {
+      const uint32_t count = __ldcg(hist + kWideBins - 1 - kPer * lane - j);
+      if ((int64_t)(run + count) >= krem) {
+        *s_digit = kWideBins - 1 - kPer * lane - j;
+        *s_above = run;
+        break;
+      }
+      run += count;
+    }
+  }
+}
+
+template <typename T, bool SMALL>
+__global__ void __launch_bounds__(kSelThreads, 1) deviation_select_kernel(
+    DevArgs a, int width_or_units_log2, const uint8_t* __restrict__ base, int64_t k,
+    float* __restrict__ scores, int64_t* __restrict__ out, int64_t cap, int slice,
+    FusedWorkspace* __restrict__ ws) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  extern __shared__ __align__(16) uint32_t dyn[];
+  __shared__ uint32_t wide[kWideBins];
+  __shared__ int s_last;
+  __shared__ uint32_t s_digit;
+  __shared__ int64_t s_above;
+  const int tid = threadIdx.x;
+  for (int b = tid; b < kWideBins; b += kSelThreads) wide[b] = 0;
+  __syncthreads();
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + tid) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  auto sink = [&](int64_t i, float v) {
+    scores[i] = v;
+    if (!base[i]) atomicAdd(&wide[order_key(v) >> (32 - kWideBits)], 1u);
+  };
+  if (SMALL)
+    score_small_rows<T>(a, width_or_units_log2, warp, nwarps, sink);
+  else
+    score_rows<T, true>(a, width_or_units_log2, warp, nwarps, sink);
+  __syncthreads();
+  for (int b = tid; b < kWideBins; b += kSelThreads)
+    if (wide[b]) atomicAdd(&ws->hist[b], wide[b]);
+  __threadfence();  // scores and counts visible device-wide before the ticket
+  cluster.sync();
+  if (rank == 0 && tid == 0) {
+    const uint32_t clusters = gridDim.x / kClusterCtas;
+    const int last = atomicAdd(&ws->ticket, 1u) == clusters - 1;
+    for (int r = 0; r < kClusterCtas; ++r) *cluster.map_shared_rank(&s_last, r) = last;
+  }
+  cluster.sync();
+  if (!s_last) return;
+  __threadfence();
+  uint32_t prefix = 0, pmask = 0;
+  int64_t krem = k;
+  if (k > 0) {
+    if (tid == 0) {
+      s_digit = 0;
+      s_above = 0;
+    }
+    __syncthreads();
+    if (tid < 32) find_wide_digit(ws->hist, k, &s_digit, &s_above);
+    __syncthreads();
+    prefix = s_digit << (32 - kWideBits);
+    pmask = (uint32_t)(kWideBins - 1) << (32 - kWideBits);
+    krem = k - s_above;
+  }
+  cluster.sync();  // every CTA of this cluster has read the histogram: clear it for the next call
+  if (rank == 0) {
+    for (int b = tid; b < kWideBins; b += kSelThreads) ws->hist[b] = 0;
+    if (tid == 0) ws->ticket = 0;
+  }
+  cluster_select<TailPasses>(cluster, scores, base, a.n, k, out, cap, slice, dyn, prefix, pmask, krem);
 }
 
 // |A n B| of two strictly ascending index lists (the two selections of the
@@ -509,23 +664,17 @@ extern "C" int cb_kv_deviation(const void* fresh, int64_t fresh_row_stride, cons
     const int64_t small_blocks = (num_tokens + per_block - 1) / per_block;
     small_grid = static_cast<int>(small_blocks < kSmCount * 8 ? small_blocks : kSmCount * 8);
   }
-#define CB_DEV_LAUNCH(T)                                                                      \
-  do {                                                                                        \
-    if (small)                                                                                \
-      deviation_small_kernel<T><<<small_grid, 256, 0, s>>>(f, fresh_row_stride, c,            \
-                                                           cached_row_stride, cached_rows,    \
-                                                           abs_index, abs_offset, num_tokens, \
-                                                           units_log2, scores);               \
-    else if (vec)                                                                             \
-      deviation_kernel<T, true><<<grid, 256, 0, s>>>(f, fresh_row_stride, c,                  \
-                                                     cached_row_stride, cached_rows, abs_index,\
-                                                     abs_offset, num_tokens, w, scores);      \
-    else                                                                                      \
-      deviation_kernel<T, false><<<grid, 256, 0, s>>>(f, fresh_row_stride, c,                 \
-                                                      cached_row_stride, cached_rows,         \
-                                                      abs_index, abs_offset, num_tokens, w,   \
-                                                      scores);                                \
+#define CB_DEV_LAUNCH(T)                                                                   \
+  do {                                                                                     \
+    if (small)                                                                             \
+      deviation_small_kernel<T><<<small_grid, 256, 0, s>>>(args, units_log2, scores);      \
+    else if (vec)                                                                          \
+      deviation_kernel<T, true><<<grid, 256, 0, s>>>(args, w, scores);                     \
+    else                                                                                   \
+      deviation_kernel<T, false><<<grid, 256, 0, s>>>(args, w, scores);                    \
   } while (0)
+  const DevArgs args{f, fresh_row_stride, c, cached_row_stride, cached_rows, abs_index, abs_offset,
+                     num_tokens};
   switch (dtype) {
     case CB_DTYPE_BF16:
       CB_DEV_LAUNCH(__nv_bfloat16);
@@ -595,4 +744,99 @@ extern "C" int cb_sorted_overlap(const int64_t* a, int64_t na, const int64_t* b,
   sorted_overlap_kernel<<<grid, 256, 0, s>>>(a, na, b, nb,
                                              reinterpret_cast<unsigned long long*>(count));
   return launch_status("cb_sorted_overlap");
+}
+
+extern "C" int cb_kv_deviation_select_workspace_size(int64_t* bytes) {
+  CB_REQUIRE(bytes != nullptr, "null output");
+  *bytes = static_cast<int64_t>(sizeof(FusedWorkspace));
+  return CB_OK;
+}
+
+extern "C" int cb_kv_deviation_select(const void* fresh, int64_t fresh_row_stride, const void* cached,
+                                      int64_t cached_row_stride, int64_t cached_rows,
+                                      const int64_t* abs_index, int64_t abs_offset,
+                                      int64_t num_tokens, int64_t width, int dtype,
+                                      const uint8_t* base_mask, int64_t k, float* scores,
+                                      int64_t* out_index, int64_t out_capacity, void* workspace,
+                                      int64_t workspace_bytes, void* stream) {
+  CB_BIND(stream, scores);
+  const int esize = dtype_bytes(dtype);
+  CB_REQUIRE(esize > 0, "unsupported dtype %d", dtype);
+  CB_REQUIRE(num_tokens >= 0 && width > 0 && width < (int64_t(1) << 24), "bad shape");
+  CB_REQUIRE(k >= 0 && k <= num_tokens && out_capacity >= 0, "bad n/k");
+  if (num_tokens == 0) return CB_OK;
+  CB_REQUIRE(fresh && cached && scores && base_mask && out_index, "null pointer argument");
+  CB_REQUIRE(cached_rows >= 0, "negative cached_rows");
+  const uint64_t acc = reinterpret_cast<uint64_t>(fresh) | reinterpret_cast<uint64_t>(cached) |
+                       (uint64_t)fresh_row_stride | (uint64_t)cached_row_stride |
+                       (uint64_t)(width * esize);
+  const bool vec = vector_bytes(acc) >= 16;
+  const bool fits = num_tokens <= (int64_t)kClusterCtas * kFusedMaxSlice;
+  if (!vec || !fits || workspace == nullptr) {
+    // unaligned rows or more scores than one cluster holds: the two launches
+    int rc = cb_kv_deviation(fresh, fresh_row_stride, cached, cached_row_stride, cached_rows, abs_index,
+                             abs_offset, num_tokens, width, dtype, scores, stream);
+    if (rc != CB_OK) return rc;
+    return cb_select_topk(scores, base_mask, num_tokens, k, out_index, out_capacity, stream);
+  }
+  CB_REQUIRE(workspace_bytes >= (int64_t)sizeof(FusedWorkspace), "workspace too small: %lld < %zu bytes",
+             (long long)workspace_bytes, sizeof(FusedWorkspace));
+  CB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, "workspace must be 16-byte aligned");
+  const int64_t units = width * esize / 16;
+  int units_log2 = 0;
+  while ((int64_t(1) << units_log2) < units) ++units_log2;
+  const bool small = units <= 32 && (int64_t(1) << units_log2) == units;
+  const int slice = static_cast<int>((num_tokens + kClusterCtas - 1) / kClusterCtas);
+  const size_t dyn = ((size_t)slice * 5 + 15) / 16 * 16;
+  // clusters: as many as run at once (one 1024-thread CTA per SM), at most one
+  // per 64 tokens' worth of warps
+  int clusters = 16;
+  const int64_t by_work = (num_tokens + 8 * 32 * 4 - 1) / (8 * 32 * 4);
+  if (by_work < clusters) clusters = static_cast<int>(by_work < 1 ? 1 : by_work);
+  const DevArgs args{static_cast<const char*>(fresh), fresh_row_stride, static_cast<const char*>(cached),
+                     cached_row_stride, cached_rows, abs_index, abs_offset, num_tokens};
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(clusters * kClusterCtas, 1, 1);
+  config.blockDim = dim3(kSelThreads, 1, 1);
+  config.dynamicSmemBytes = dyn;
+  config.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  const int wl = small ? units_log2 : static_cast<int>(width);
+  auto* ws = static_cast<FusedWorkspace*>(workspace);
+  cudaError_t e = cudaSuccess;
+  int rc = CB_OK;
+#define CB_FUSED_LAUNCH(T)                                                                       \
+  do {                                                                                          \
+    const void* fn = small ? reinterpret_cast<const void*>(deviation_select_kernel<T, true>)     \
+                           : reinterpret_cast<const void*>(deviation_select_kernel<T, false>);   \
+    rc = ensure_dynamic_smem(fn, dyn);                                                          \
+    if (rc != CB_OK) return rc;                                                                 \
+    e = small ? cudaLaunchKernelEx(&config, deviation_select_kernel<T, true>, args, wl, base_mask, \
+                                   k, scores, out_index, out_capacity, slice, ws)               \
+              : cudaLaunchKernelEx(&config, deviation_select_kernel<T, false>, args, wl, base_mask,\
+                                   k, scores, out_index, out_capacity, slice, ws);              \
+  } while (0)
+  switch (dtype) {
+    case CB_DTYPE_BF16:
+      CB_FUSED_LAUNCH(__nv_bfloat16);
+      break;
+    case CB_DTYPE_FP16:
+      CB_FUSED_LAUNCH(__half);
+      break;
+    default:
+      CB_FUSED_LAUNCH(float);
+      break;
+  }
+#undef CB_FUSED_LAUNCH
+  if (e != cudaSuccess) {
+    set_error("cb_kv_deviation_select cluster launch failed: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return launch_status("cb_kv_deviation_select");
 }

@@ -456,6 +456,70 @@ __global__ void __launch_bounds__(kThreads, 1)
   teardown(sh, warp);
 }
 
+#ifndef CB_SQ_PASS2_PIPELINE
+#define CB_SQ_PASS2_PIPELINE 0
+#endif
+
+// Pass 2's work on 4 * J rows of one key (this lane's): scores v[] (fp32 bits
+// from TMEM), the rows' negated log2-sum-exp and positions from the side slot.
+// Adds exp2(round_T(s) * scale * log2e - lse) into acc; rows past the key's
+// position add 0 when the tile is not `full`.
+template <typename T, int J, int N>
+__device__ __forceinline__ void key_mass_rows(const uint32_t (&v)[N], const float4* nlse4,
+                                              const int4* pos4, bool full, int key, float2 scale2,
+                                              float2 (&acc)[4]) {
+  static_assert(N == 4 * J, "four rows per step");
+  if (full) {
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const float4 l4 = nlse4[j];
+      const float2 y0 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j], v[4 * j + 1])), scale2,
+                                   make_float2(l4.x, l4.y));
+      const float2 y1 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j + 2], v[4 * j + 3])), scale2,
+                                   make_float2(l4.z, l4.w));
+      acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], exp2_pair(y0, (kPolyPass2 >> ((2 * j) & 15)) & 1u));
+      acc[(2 * j + 1) & 3] =
+          __fadd2_rn(acc[(2 * j + 1) & 3], exp2_pair(y1, (kPolyPass2 >> ((2 * j + 1) & 15)) & 1u));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const float4 l4 = nlse4[j];
+      const int4 p4 = pos4[j];
+      const float2 y0 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j], v[4 * j + 1])), scale2,
+                                   make_float2(l4.x, l4.y));
+      const float2 y1 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j + 2], v[4 * j + 3])), scale2,
+                                   make_float2(l4.z, l4.w));
+      const float2 e0 = make_float2(key <= p4.x ? ex2(y0.x) : 0.0f, key <= p4.y ? ex2(y0.y) : 0.0f);
+      const float2 e1 = make_float2(key <= p4.z ? ex2(y1.x) : 0.0f, key <= p4.w ? ex2(y1.y) : 0.0f);
+      acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], e0);
+      acc[(2 * j + 1) & 3] = __fadd2_rn(acc[(2 * j + 1) & 3], e1);
+    }
+  }
+}
+
+// 16 TMEM columns of this warp's 32 lanes into registers (completes at the next wait).
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(addr));
+}
+
+// tcgen05.wait::ld, naming the registers of the load it completes as in/out
+// operands so that no use of them is scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld_holding(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
+                 "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]),
+                 "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
+
 // ============================================================ pass 2: key mass
 // items: key tiles kt ascending (earlier keys are seen by more queries).
 template <typename T>
@@ -599,6 +663,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float* nlse = side + q * 2 * kTile;  // -lse of each row
           const int* pos = reinterpret_cast<const int*>(side + q * 2 * kTile + kTile);
           const bool full = key <= tile_min[qt];  // every row of the tile sees this key
+#if CB_SQ_PASS2_PIPELINE
+          // 16-row chunks, the TMEM load of chunk c + 1 in flight while chunk c computes
+          uint32_t va[16], vb[16];
+          tmem_ld16(addr, va);
+#pragma unroll
+          for (int chunk = 0; chunk < 8; ++chunk) {
+            uint32_t(&v)[16] = (chunk & 1) ? vb : va;
+            uint32_t(&next)[16] = (chunk & 1) ? va : vb;
+            tmem_wait_ld_holding(v);
+            if (chunk < 7) {
+              tmem_ld16(addr + (chunk + 1) * 16, next);
+            } else {  // TMEM no longer needed: hand the accumulator back to the MMA
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
+            }
+            const float4* nlse4 = reinterpret_cast<const float4*>(nlse + chunk * 16);
+            const int4* pos4 = reinterpret_cast<const int4*>(pos + chunk * 16);
+            key_mass_rows<T, 4>(v, nlse4, pos4, full, key, scale2, acc);
+          }
+          __syncwarp();  // lse / positions of this slot read: release it
+          if (lane == 0) mbar_arrive(&sh.side_empty[q]);
+#else
 #pragma unroll
           for (int quarter = 0; quarter < 4; ++quarter) {
             uint32_t v[32];  // 32 rows of this key: one TMEM load, few live registers
@@ -611,38 +698,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float4* nlse4 = reinterpret_cast<const float4*>(nlse + quarter * 32);
             const int4* pos4 = reinterpret_cast<const int4*>(pos + quarter * 32);
-            if (full) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 l4 = nlse4[j];
-                const float2 y0 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j], v[4 * j + 1])), scale2,
-                                             make_float2(l4.x, l4.y));
-                const float2 y1 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j + 2], v[4 * j + 3])), scale2,
-                                             make_float2(l4.z, l4.w));
-                acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], exp2_pair(y0, (kPolyPass2 >> (2 * j)) & 1u));
-                acc[(2 * j + 1) & 3] =
-                    __fadd2_rn(acc[(2 * j + 1) & 3], exp2_pair(y1, (kPolyPass2 >> (2 * j + 1)) & 1u));
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 l4 = nlse4[j];
-                const int4 p4 = pos4[j];
-                const float2 y0 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j], v[4 * j + 1])), scale2,
-                                             make_float2(l4.x, l4.y));
-                const float2 y1 = __ffma2_rn(unpack<T>(pack_round<T>(v[4 * j + 2], v[4 * j + 3])), scale2,
-                                             make_float2(l4.z, l4.w));
-                const float2 e0 = make_float2(key <= p4.x ? ex2(y0.x) : 0.0f, key <= p4.y ? ex2(y0.y) : 0.0f);
-                const float2 e1 = make_float2(key <= p4.z ? ex2(y1.x) : 0.0f, key <= p4.w ? ex2(y1.y) : 0.0f);
-                acc[(2 * j) & 3] = __fadd2_rn(acc[(2 * j) & 3], e0);
-                acc[(2 * j + 1) & 3] = __fadd2_rn(acc[(2 * j + 1) & 3], e1);
-              }
-            }
+            key_mass_rows<T, 8>(v, nlse4, pos4, full, key, scale2, acc);
             if (quarter == 3) {  // lse / positions of this slot read: release it
               __syncwarp();
               if (lane == 0) mbar_arrive(&sh.side_empty[q]);
             }
           }
+#endif
         }
       }
       const float2 a03 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
