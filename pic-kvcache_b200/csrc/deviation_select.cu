@@ -17,6 +17,10 @@
 // (<= 4 B x active tokens) and L2-resident, so the select is latency-bound.
 #include <cooperative_groups.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "cb_common.cuh"
 
 namespace cb {
@@ -746,6 +750,54 @@ extern "C" int cb_sorted_overlap(const int64_t* a, int64_t na, const int64_t* b,
   return launch_status("cb_sorted_overlap");
 }
 
+namespace {
+// Clusters of deviation_select_kernel the current device runs at once (queried
+// once per context, kernel and shared-memory size; 16 if the query fails).
+int resident_clusters(bool small, int dtype, size_t dyn) {
+  static std::mutex lock;
+  static std::map<std::tuple<void*, const void*, size_t>, int> known;
+  const void* fn = nullptr;
+  switch (dtype) {
+    case CB_DTYPE_BF16:
+      fn = small ? (const void*)deviation_select_kernel<__nv_bfloat16, true>
+                 : (const void*)deviation_select_kernel<__nv_bfloat16, false>;
+      break;
+    case CB_DTYPE_FP16:
+      fn = small ? (const void*)deviation_select_kernel<__half, true>
+                 : (const void*)deviation_select_kernel<__half, false>;
+      break;
+    default:
+      fn = small ? (const void*)deviation_select_kernel<float, true>
+                 : (const void*)deviation_select_kernel<float, false>;
+      break;
+  }
+  void* context = nullptr;
+  if (current_context(&context) != CB_OK) return 16;
+  std::lock_guard<std::mutex> guard(lock);
+  const auto key = std::make_tuple(context, fn, dyn);
+  const auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(kClusterCtas, 1, 1);
+  config.blockDim = dim3(kSelThreads, 1, 1);
+  config.dynamicSmemBytes = dyn;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  int count = 0;
+  if (cudaOccupancyMaxActiveClusters(&count, fn, &config) != cudaSuccess || count <= 0) {
+    cudaGetLastError();  // a failed query leaves no sticky error behind
+    count = 16;
+  }
+  known[key] = count;
+  return count;
+}
+}  // namespace
+
 extern "C" int cb_kv_deviation_select_workspace_size(int64_t* bytes) {
   CB_REQUIRE(bytes != nullptr, "null output");
   *bytes = static_cast<int64_t>(sizeof(FusedWorkspace));
@@ -788,9 +840,19 @@ extern "C" int cb_kv_deviation_select(const void* fresh, int64_t fresh_row_strid
   const bool small = units <= 32 && (int64_t(1) << units_log2) == units;
   const int slice = static_cast<int>((num_tokens + kClusterCtas - 1) / kClusterCtas);
   const size_t dyn = ((size_t)slice * 5 + 15) / 16 * 16;
-  // clusters: as many as run at once (one 1024-thread CTA per SM), at most one
-  // per 64 tokens' worth of warps
-  int clusters = 16;
+  // clusters: as many as the GPU runs at once (one 1024-thread CTA per SM,
+  // eight SMs of one GPC per cluster), fewer for short inputs
+  {
+    const void* fns[3][2] = {
+        {(const void*)deviation_select_kernel<__nv_bfloat16, false>,
+         (const void*)deviation_select_kernel<__nv_bfloat16, true>},
+        {(const void*)deviation_select_kernel<__half, false>, (const void*)deviation_select_kernel<__half, true>},
+        {(const void*)deviation_select_kernel<float, false>, (const void*)deviation_select_kernel<float, true>}};
+    const int row = dtype == CB_DTYPE_BF16 ? 0 : (dtype == CB_DTYPE_FP16 ? 1 : 2);
+    const int rc0 = ensure_dynamic_smem(fns[row][small ? 1 : 0], dyn);
+    if (rc0 != CB_OK) return rc0;
+  }
+  int clusters = resident_clusters(small, dtype, dyn);
   const int64_t by_work = (num_tokens + 8 * 32 * 4 - 1) / (8 * 32 * 4);
   if (by_work < clusters) clusters = static_cast<int>(by_work < 1 ? 1 : by_work);
   const DevArgs args{static_cast<const char*>(fresh), fresh_row_stride, static_cast<const char*>(cached),
