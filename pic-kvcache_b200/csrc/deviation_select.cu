@@ -409,6 +409,9 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
     keys[i] = order_key(__ldcg(scores + lo + i));  // L2: other CTAs may have just written them
     flags[i] = base[lo + i] != 0;
   }
+  // the passes and the compaction read entries other threads loaded (with k == 0
+  // no pass runs, so this barrier is the only one before the compaction)
+  __syncthreads();
   if (k > 0) {
 #pragma unroll 1
     for (int pass = 0; pass < Passes::kCount; ++pass) {

@@ -456,10 +456,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   teardown(sh, warp);
 }
 
-#ifndef CB_SQ_PASS2_PIPELINE
-#define CB_SQ_PASS2_PIPELINE 0
-#endif
-
 // Pass 2's work on 4 * J rows of one key (this lane's): scores v[] (fp32 bits
 // from TMEM), the rows' negated log2-sum-exp and positions from the side slot.
 // Adds exp2(round_T(s) * scale * log2e - lse) into acc; rows past the key's
@@ -496,28 +492,6 @@ __device__ __forceinline__ void key_mass_rows(const uint32_t (&v)[N], const floa
       acc[(2 * j + 1) & 3] = __fadd2_rn(acc[(2 * j + 1) & 3], e1);
     }
   }
-}
-
-// 16 TMEM columns of this warp's 32 lanes into registers (completes at the next wait).
-__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-        "=r"(v[14]), "=r"(v[15])
-      : "r"(addr));
-}
-
-// tcgen05.wait::ld, naming the registers of the load it completes as in/out
-// operands so that no use of them is scheduled before the wait.
-__device__ __forceinline__ void tmem_wait_ld_holding(uint32_t (&v)[16]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
-                 "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]),
-                 "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
-               :
-               : "memory");
 }
 
 // ============================================================ pass 2: key mass
@@ -663,29 +637,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float* nlse = side + q * 2 * kTile;  // -lse of each row
           const int* pos = reinterpret_cast<const int*>(side + q * 2 * kTile + kTile);
           const bool full = key <= tile_min[qt];  // every row of the tile sees this key
-#if CB_SQ_PASS2_PIPELINE
-          // 16-row chunks, the TMEM load of chunk c + 1 in flight while chunk c computes
-          uint32_t va[16], vb[16];
-          tmem_ld16(addr, va);
-#pragma unroll
-          for (int chunk = 0; chunk < 8; ++chunk) {
-            uint32_t(&v)[16] = (chunk & 1) ? vb : va;
-            uint32_t(&next)[16] = (chunk & 1) ? va : vb;
-            tmem_wait_ld_holding(v);
-            if (chunk < 7) {
-              tmem_ld16(addr + (chunk + 1) * 16, next);
-            } else {  // TMEM no longer needed: hand the accumulator back to the MMA
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&sh.t_empty[tb]);
-            }
-            const float4* nlse4 = reinterpret_cast<const float4*>(nlse + chunk * 16);
-            const int4* pos4 = reinterpret_cast<const int4*>(pos + chunk * 16);
-            key_mass_rows<T, 4>(v, nlse4, pos4, full, key, scale2, acc);
-          }
-          __syncwarp();  // lse / positions of this slot read: release it
-          if (lane == 0) mbar_arrive(&sh.side_empty[q]);
-#else
 #pragma unroll
           for (int quarter = 0; quarter < 4; ++quarter) {
             uint32_t v[32];  // 32 rows of this key: one TMEM load, few live registers
@@ -704,7 +655,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) mbar_arrive(&sh.side_empty[q]);
             }
           }
-#endif
         }
       }
       const float2 a03 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));

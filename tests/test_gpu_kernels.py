@@ -304,11 +304,15 @@ def test_select_special_values(cuda):
     assert got.tolist() == [0, 4, 6, 7]
 
 
-def test_select_all_base_and_empty_budget(cuda):
-    scores = torch.rand(100, device=cuda)
-    base = torch.ones(100, dtype=torch.uint8, device=cuda)
-    assert select_from_scores(scores, base, 0, 100).cpu().tolist() == list(range(100))
-    assert recompute_budget(100, 100, 100, 0.5) == 0
+@pytest.mark.parametrize("n", [100, 20_000, 300_000])
+def test_select_all_base_and_empty_budget(cuda, n):
+    """k = 0 (every token a gap): the base set alone, also when each cluster CTA
+    holds more keys than it has threads (its compaction then reads entries
+    other threads loaded)."""
+    scores = torch.rand(n, device=cuda)
+    base = torch.ones(n, dtype=torch.uint8, device=cuda)
+    assert np.array_equal(select_from_scores(scores, base, 0, n).cpu().numpy(), np.arange(n))
+    assert recompute_budget(n, n, n, 0.5) == 0
 
 
 def test_select_reference_known_answers(cuda):
