@@ -251,9 +251,10 @@ class DevicePath:
         self.selected = torch.empty(gaps + self.k, dtype=torch.long, device=dev)
         # fresh K for the check layer = cached hits + noise, prepared once
         self.fresh = None
-        # one rank: the check layer's deviation and select run as one fused launch
-        # (cb_kv_deviation_select); with TP the score all-reduce sits between them
-        self.fused = tp_group is None
+        # the check layer's deviation and select: two launches (with TP the score all-reduce
+        # sits between them); CACHEBLEND_B200_FUSED_SELECT=1 times the single fused launch
+        # (cb_kv_deviation_select) on one rank instead
+        self.fused = tp_group is None and os.environ.get("CACHEBLEND_B200_FUSED_SELECT") == "1"
         self.fused_workspace = None
         if self.fused:
             size = ctypes.c_int64(0)
@@ -514,7 +515,7 @@ def e2e_step(wl: Workload, load_stream, tp_group=None) -> tuple[torch.Tensor, in
             k_plane = buf[0].reshape(plan.allocation_end, -1)
             if not hasattr(wl, "e2e_fresh"):
                 wl.e2e_fresh = (k_plane[plan.apc_prefix_tokens:].float() + wl.fresh_noise).to(torch.bfloat16)
-            if tp_group is None:  # one rank: deviation and select in one launch
+            if tp_group is None and os.environ.get("CACHEBLEND_B200_FUSED_SELECT") == "1":
                 selected, _ = deviation_select(wl.e2e_fresh, k_plane, wl.gap_mask, shape.ratio,
                                                absolute_offset=plan.apc_prefix_tokens)
             else:
@@ -1432,6 +1433,7 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
     shard = args.tp_shard if args.tp_shard and world == 1 else world
     wl = Workload(shape, shard, rank, device, host_store=e2e_on)
     path = DevicePath(wl, tp_group=group)
+    path_fused = path.fused
     stream = torch.cuda.Stream(device)
     # warm-up (also builds the check-layer fresh K)
     with torch.cuda.stream(stream):
@@ -1536,7 +1538,7 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
         "config": workload_config(shape, span, shape.kv_heads // shard, world, shard),
-        "gpu_launches": (2 * shape.layers + 2) * steps,
+        "gpu_launches": (2 * shape.layers + (1 if path_fused else 2)) * steps,
         "launch": "eager, one stream" if args.no_graph else (
             ("cuda-graph" if world == 1 else "two cuda-graphs around the NCCL all-reduce")
             + (", loads on a side stream beside the commits" if 2 * shape.kv_heads // shard * 128 < 2048

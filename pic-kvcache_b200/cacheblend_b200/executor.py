@@ -47,6 +47,10 @@ from .types import BlendPlan
 # which is what the reference computes on a CUDA device).
 _FUSED_ATTENTION = os.environ.get("CACHEBLEND_B200_ATTENTION", "").lower() == "fused"
 
+# CACHEBLEND_B200_FUSED_SELECT=1: K-deviation and selection of a one-rank check layer as one
+# launch (cb_kv_deviation_select) instead of two (measured slower on B200 so far: off by default)
+_FUSED_SELECT = os.environ.get("CACHEBLEND_B200_FUSED_SELECT", "") == "1"
+
 _EMBEDDING_HOOKS = ("get_input_embeddings", "embed_input_ids")
 
 
@@ -246,11 +250,12 @@ class Qwen3BlendExecutor:
         by_deviation = by_query = None
         if strategy in ("kv_deviation", "compare"):
             ratio = self.config.ratio_for_layer(layer_id)
-            if self.config.tp_global_selection and tp_world_size(self.tp_group) > 1:
-                deviation = kv_deviation(rows.k, cached_k, rows.absolute)
-                by_deviation = self._select(deviation, gaps, layer_id)  # all-reduce, then select
-            else:  # this rank's scores alone: score and select in one launch
+            if _FUSED_SELECT and not (self.config.tp_global_selection and tp_world_size(self.tp_group) > 1):
+                # this rank's scores alone: score and select in one launch
                 by_deviation, _ = deviation_select(rows.k, cached_k, gaps, ratio, rows.absolute)
+            else:
+                deviation = kv_deviation(rows.k, cached_k, rows.absolute)
+                by_deviation = self._select(deviation, gaps, layer_id)  # all-reduce (TP), then select
             choice.before_attention = by_deviation
         if strategy in ("sparse_q", "compare"):
             attn = layer.self_attn.attn

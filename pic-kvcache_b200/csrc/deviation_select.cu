@@ -519,13 +519,15 @@ struct FusedWorkspace {
   uint32_t ticket;
 };
 
-// First (11-bit) digit: warp 0, lane L owns bins 2047 - 64L down to 1984 - 64L.
+// First (11-bit) digit from the histogram staged in shared memory: warp 0,
+// lane L owns bins 2047 - 64L down to 1984 - 64L.
 __device__ __forceinline__ void find_wide_digit(const uint32_t* hist, int64_t krem, uint32_t* s_digit,
                                                 int64_t* s_above) {
   const int lane = threadIdx.x;
   constexpr int kPer = kWideBins / 32;
   uint32_t sum = 0;
-  for (int j = 0; j < kPer; ++j) sum += __ldcg(hist + kWideBins - 1 - kPer * lane - j);
+#pragma unroll 16
+  for (int j = 0; j < kPer; ++j) sum += hist[kWideBins - 1 - kPer * lane - j];
   uint32_t incl = sum;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -536,7 +538,7 @@ __device__ __forceinline__ void find_wide_digit(const uint32_t* hist, int64_t kr
   if ((int64_t)above < krem && (int64_t)incl >= krem) {
     uint32_t run = above;
     for (int j = 0; j < kPer; ++j) {
-      const uint32_t count = __ldcg(hist + kWideBins - 1 - kPer * lane - j);
+      const uint32_t count = hist[kWideBins - 1 - kPer * lane - j];
       if ((int64_t)(run + count) >= krem) {
         *s_digit = kWideBins - 1 - kPer * lane - j;
         *s_above = run;
@@ -588,12 +590,14 @@ __global__ void __launch_bounds__(kSelThreads, 1) deviation_select_kernel(
   uint32_t prefix = 0, pmask = 0;
   int64_t krem = k;
   if (k > 0) {
+    // the device-wide histogram into shared memory (the CTA's own counts are flushed)
+    for (int b = tid; b < kWideBins; b += kSelThreads) wide[b] = __ldcg(ws->hist + b);
     if (tid == 0) {
       s_digit = 0;
       s_above = 0;
     }
     __syncthreads();
-    if (tid < 32) find_wide_digit(ws->hist, k, &s_digit, &s_above);
+    if (tid < 32) find_wide_digit(wide, k, &s_digit, &s_above);
     __syncthreads();
     prefix = s_digit << (32 - kWideBits);
     pmask = (uint32_t)(kWideBins - 1) << (32 - kWideBits);
