@@ -179,7 +179,11 @@ class PagedBlendLoader:
         segments = self.plan.segments
         if not segments:
             return None, False
-        hosts = [self.store.get_layer(self.request_id, seg, layer_id) for seg in segments]
+        get_layers = getattr(self.store, "get_layers", None)
+        if get_layers is not None:  # one lock acquisition for the layer's segments
+            hosts = get_layers(self.request_id, segments, layer_id)
+        else:
+            hosts = [self.store.get_layer(self.request_id, seg, layer_id) for seg in segments]
         for host, seg in zip(hosts, segments, strict=True):
             self._check_host(host, paged, seg.length)
         zero_copy = self.mode == "zerocopy" and all(host.is_pinned() for host in hosts)
@@ -234,7 +238,8 @@ class PagedBlendLoader:
             hit_buffer = torch.empty(total, dtype=torch.uint8, device=paged.device)
             self._hit_buffers[parity] = hit_buffer
             self._copy_tables[parity] = None
-        runs: list[list] = []  # [first piece, dst offset, bytes, next src ptr]
+        runs: list[list] = []  # [first piece, dst offset, bytes, next src ptr, storage ptr]
+        pinned: dict[int, bool] = {}  # per host storage: pinned (queried once per storage)
         offset = 0
         for host in hosts:
             pieces = [host] if host.is_contiguous() else [host[0], host[1]]
@@ -243,17 +248,18 @@ class PagedBlendLoader:
                     piece = piece.contiguous()
                 nbytes = piece.numel() * piece.element_size()
                 ptr = piece.data_ptr()
+                storage = piece.untyped_storage().data_ptr()
                 last = runs[-1] if runs else None
-                if (
-                    last is not None
-                    and last[3] == ptr
-                    and piece.is_pinned()
-                    and last[0].untyped_storage().data_ptr() == piece.untyped_storage().data_ptr()
-                ):
-                    last[2] += nbytes
-                    last[3] += nbytes
-                else:
-                    runs.append([piece, offset, nbytes, ptr + nbytes])
+                if last is not None and last[3] == ptr and last[4] == storage:
+                    is_pinned = pinned.get(storage)
+                    if is_pinned is None:
+                        is_pinned = pinned[storage] = piece.is_pinned()
+                    if is_pinned:
+                        last[2] += nbytes
+                        last[3] += nbytes
+                        offset += nbytes
+                        continue
+                runs.append([piece, offset, nbytes, ptr + nbytes, storage])
                 offset += nbytes
         load_stream = torch.cuda.current_stream()
         copy_stream = _copy_stream(paged.device) if self._load_stream is not None else load_stream
@@ -262,7 +268,7 @@ class PagedBlendLoader:
             if free is not None:
                 copy_stream.wait_event(free)
         with torch.cuda.stream(copy_stream):
-            for piece, dst_offset, nbytes, _ in runs:
+            for piece, dst_offset, nbytes, _, _ in runs:
                 src = byte_span(piece, nbytes)
                 hit_buffer[dst_offset : dst_offset + nbytes].copy_(src, non_blocking=True)
                 self._host_refs.append(src)

@@ -74,7 +74,9 @@ class LocalPinnedCPUStore:
         # do not rescan every in-flight entry on each publication
         self._committed: OrderedDict[SegmentId, _Entry] = OrderedDict()
         self._bytes = 0
-        self._request_pins: dict[str, tuple[SegmentId, ...]] = {}
+        # per request, its pinned segment ids in pin order (a dict: O(1) membership for the
+        # loader's per-layer lookups, insertion order for release)
+        self._request_pins: dict[str, dict[SegmentId, None]] = {}
         self._lock = threading.RLock()
         self.arena = None  # PinnedArena once attached
 
@@ -325,7 +327,7 @@ class LocalPinnedCPUStore:
                 self._touch(seg.segment_id, entry)
                 kept.append(seg)
             if kept:
-                self._request_pins[request_id] = tuple(seg.segment_id for seg in kept)
+                self._request_pins[request_id] = dict.fromkeys(seg.segment_id for seg in kept)
             return tuple(kept)
 
     def release(self, request_id: str) -> None:
@@ -338,16 +340,29 @@ class LocalPinnedCPUStore:
 
     def get_layer(self, request_id: str, segment: BlendSegment, layer_id: int) -> torch.Tensor:
         with self._lock:
-            if segment.segment_id not in self._request_pins.get(request_id, ()):
-                raise RuntimeError(f"segment {segment.segment_id} is not pinned by {request_id}")
-            entry = self._entries.get(segment.segment_id)
-            if entry is None or not entry.committed:
-                raise KeyError(segment.segment_id)
-            tensor = entry.layers.get(layer_id)
-            if tensor is None:
-                raise KeyError(f"layer {layer_id} is not stored for {segment.segment_id}")
-            self._touch(segment.segment_id, entry)
-            return tensor
+            return self._pinned_layer(self._request_pins.get(request_id, {}), request_id, segment,
+                                      layer_id)
+
+    def get_layers(self, request_id: str, segments, layer_id: int) -> list[torch.Tensor]:
+        """``get_layer`` for every segment in order, under one lock acquisition: the same
+        checks, errors and LRU touches as the calls one by one (the loader's per-layer lookup)."""
+        with self._lock:
+            pins = self._request_pins.get(request_id, {})
+            return [self._pinned_layer(pins, request_id, seg, layer_id) for seg in segments]
+
+    def _pinned_layer(self, pins: dict, request_id: str, segment: BlendSegment,
+                      layer_id: int) -> torch.Tensor:
+        sid = segment.segment_id
+        if sid not in pins:
+            raise RuntimeError(f"segment {sid} is not pinned by {request_id}")
+        entry = self._entries.get(sid)
+        if entry is None or not entry.committed:
+            raise KeyError(sid)
+        tensor = entry.layers.get(layer_id)
+        if tensor is None:
+            raise KeyError(f"layer {layer_id} is not stored for {sid}")
+        self._touch(sid, entry)
+        return tensor
 
     def clear(self) -> None:
         with self._lock:

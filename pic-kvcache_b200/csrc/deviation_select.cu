@@ -428,20 +428,9 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
         s_above = 0;
       }
       cluster.sync();
-      // warp-aggregated counts: lanes holding the same digit add once (the high
-      // digits of similar scores are nearly constant, and 4 K atomics on one
-      // shared word serialise)
-      const int lane = tid & 31;
-      for (int i0 = tid - lane; i0 < m; i0 += kSelThreads) {
-        const int i = i0 + lane;
-        const uint32_t key = i < m ? keys[i] : 0u;
-        const bool take = i < m && !flags[i] && (key & pmask) == prefix;
-        const unsigned voting = __ballot_sync(0xffffffffu, take);
-        if (take) {
-          const uint32_t digit = (key >> shift) & digit_mask;
-          const unsigned peers = __match_any_sync(voting, digit);
-          if (lane == __ffs(peers) - 1) atomicAdd(&local[digit], static_cast<uint32_t>(__popc(peers)));
-        }
+      for (int i = tid; i < m; i += kSelThreads) {
+        const uint32_t key = keys[i];
+        if (!flags[i] && (key & pmask) == prefix) atomicAdd(&local[(key >> shift) & digit_mask], 1u);
       }
       __syncthreads();
       if (tid < 256 && local[tid]) atomicAdd(&root_hist[tid], local[tid]);
