@@ -392,10 +392,12 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
   const int rank = static_cast<int>(cluster.block_rank());
   uint32_t* keys = dyn;
   uint8_t* flags = reinterpret_cast<uint8_t*>(keys + slice);
-  // rank 0's copy is the cluster histogram, double-buffered by pass parity:
-  // buffer p&1 is zeroed at the start of pass p, and its last readers (pass
-  // p-2) finished before the cluster barrier that opened pass p-1.
-  __shared__ uint32_t hist[2][256];
+  // rank 0's copy is the cluster histogram, triple-buffered by pass: buffer
+  // p % 3 receives pass p's counts.  Rank 0 zeroes buffer (p + 1) % 3 while it
+  // counts pass p: that buffer was last read by pass p - 2's digit search,
+  // which every CTA finished before the barrier of pass p - 1, and it is first
+  // added to after the barrier of pass p.  So one cluster barrier per pass.
+  __shared__ uint32_t hist[3][256];
   __shared__ uint32_t local[256];
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t totals[2];    // this CTA's (selected, tied) counts
@@ -409,31 +411,37 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
     keys[i] = order_key(__ldcg(scores + lo + i));  // L2: other CTAs may have just written them
     flags[i] = base[lo + i] != 0;
   }
+  if (tid < 256) {
+    local[tid] = 0;
+    if (rank == 0) hist[0][tid] = 0;
+  }
   // the passes and the compaction read entries other threads loaded (with k == 0
-  // no pass runs, so this barrier is the only one before the compaction)
-  __syncthreads();
+  // no pass runs), and every CTA's first adds must follow rank 0's zeroing
+  if (k > 0)
+    cluster.sync();
+  else
+    __syncthreads();
   if (k > 0) {
 #pragma unroll 1
     for (int pass = 0; pass < Passes::kCount; ++pass) {
       const RadixPass digit = Passes::at(pass);
       const int shift = digit.shift;
       const uint32_t digit_mask = (1u << digit.width) - 1u;
-      uint32_t* root_hist = cluster.map_shared_rank(&hist[pass & 1][0], 0);
-      if (tid < 256) {
-        local[tid] = 0;
-        if (rank == 0) hist[pass & 1][tid] = 0;
-      }
+      uint32_t* root_hist = cluster.map_shared_rank(&hist[pass % 3][0], 0);
+      if (rank == 0 && tid < 256) hist[(pass + 1) % 3][tid] = 0;
       if (tid == 0) {
         s_digit = 0;  // see select_topk_kernel: degrades safely if k > #candidates
         s_above = 0;
       }
-      cluster.sync();
       for (int i = tid; i < m; i += kSelThreads) {
         const uint32_t key = keys[i];
         if (!flags[i] && (key & pmask) == prefix) atomicAdd(&local[(key >> shift) & digit_mask], 1u);
       }
       __syncthreads();
-      if (tid < 256 && local[tid]) atomicAdd(&root_hist[tid], local[tid]);
+      if (tid < 256) {
+        if (local[tid]) atomicAdd(&root_hist[tid], local[tid]);
+        local[tid] = 0;  // this thread's own bin: ready for the next pass
+      }
       cluster.sync();
       if (tid < 32) find_digit(root_hist, krem, &s_digit, &s_above);
       __syncthreads();
