@@ -255,6 +255,13 @@ class DevicePath:
         # sits between them); CACHEBLEND_B200_FUSED_SELECT=1 times the single fused launch
         # (cb_kv_deviation_select) on one rank instead
         self.fused = tp_group is None and os.environ.get("CACHEBLEND_B200_FUSED_SELECT") == "1"
+        # with TP the score reduction runs inside the select kernel over NVLink peer memory
+        # (cb_select_topk_peer); CACHEBLEND_B200_PEER_SELECT=0 puts the NCCL all-reduce back
+        self.peer = None
+        if tp_group is not None and os.environ.get("CACHEBLEND_B200_PEER_SELECT", "1") != "0":
+            from cacheblend_b200.peer_exchange import PeerScoreExchange
+
+            self.peer = PeerScoreExchange(tp_group, wl.act, dev)
         self.fused_workspace = None
         if self.fused:
             size = ctypes.c_int64(0)
@@ -301,7 +308,7 @@ class DevicePath:
         if self.fused:
             return self.deviation_select(buf, stream)
         self.deviation(buf, stream)
-        if self.tp_group is not None:
+        if self.tp_group is not None and self.peer is None:
             torch.distributed.all_reduce(self.scores, group=self.tp_group)
         return self.select(stream)
 
@@ -358,10 +365,14 @@ class DevicePath:
     def select(self, stream) -> torch.Tensor:
         wl = self.wl
         ev = self._ev("select", stream)
-        self.native.call(
-            "cb_select_topk", self.scores.data_ptr(), self.base_mask.data_ptr(), wl.act, self.k,
-            self.selected.data_ptr(), self.selected.numel(), stream.cuda_stream,
-        )
+        if self.peer is not None:
+            self.peer.select(self.scores, self.base_mask, self.k, self.selected.numel(), stream,
+                             out=self.selected)
+        else:
+            self.native.call(
+                "cb_select_topk", self.scores.data_ptr(), self.base_mask.data_ptr(), wl.act, self.k,
+                self.selected.data_ptr(), self.selected.numel(), stream.cuda_stream,
+            )
         self._ev_end("select", ev, stream)
         return self.selected
 
@@ -431,7 +442,7 @@ class DevicePath:
                     self.deviation_select(self.staging[layer % 2], main)
                 else:
                     self.deviation(self.staging[layer % 2], main)
-                    if part == "until":
+                    if part == "until" and self.peer is None:
                         break
                     self.select(main)
             self.commit(layer, self.staging[layer % 2], main)
@@ -442,11 +453,12 @@ class DevicePath:
 
     def capture(self, stream) -> None:
         """CUDA graphs of the pipelined step (no per-launch host work while timing): one
-        graph on a single rank; with TP, two graphs around the eager NCCL all-reduce."""
+        graph on a single rank or with the peer-memory select; with the NCCL all-reduce,
+        two graphs around it."""
         assert self.fresh is not None and not self.timing
         torch.cuda.synchronize(self.wl.device)
         graphs = []
-        for part in (["all"] if self.tp_group is None else ["until", "after"]):
+        for part in (["all"] if self.tp_group is None or self.peer is not None else ["until", "after"]):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 self._pipelined(stream, part)
@@ -456,7 +468,15 @@ class DevicePath:
     def release(self) -> None:
         self.graphs = []
 
-    def kernel_graph_us(self, stream, reps: int = 20) -> dict[str, float]:
+    def close(self) -> None:
+        """Free the peer exchange (every rank together)."""
+        self.graphs = []
+        if self.peer is not None:
+            self.peer.check()
+            self.peer.close()
+            self.peer = None
+
+    def kernel_graph_us(self, stream, reps: int = 20, sync=None) -> dict[str, float]:
         """Average launch duration of each kernel, back to back as in the step: one step's
         36 loads (resp. 36 commit scatters, or ten deviation / select launches) captured
         in a graph, replayed ``reps`` times between two CUDA events on the launching stream."""
@@ -481,6 +501,8 @@ class DevicePath:
         out = {}
         for name, (count, launch) in kinds.items():
             torch.cuda.synchronize(self.wl.device)
+            if sync is not None:
+                sync()  # TP: the ranks start each kind together (the peer select waits on the others)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
                 launch()
@@ -520,7 +542,8 @@ def e2e_step(wl: Workload, load_stream, tp_group=None) -> tuple[torch.Tensor, in
                                                absolute_offset=plan.apc_prefix_tokens)
             else:
                 scores = kv_deviation(wl.e2e_fresh, k_plane, absolute_offset=plan.apc_prefix_tokens)
-                selected = select_tokens(scores, wl.gap_mask, shape.ratio, tp_group=tp_group)
+                selected = select_tokens(scores, wl.gap_mask, shape.ratio, tp_group=tp_group,
+                                         peer_exchange=getattr(wl, "peer", None))
         loader.commit(layer, buf)
     host = selected.to("cpu")  # device -> host read of the step's result
     return host, host.numel() * host.element_size()
@@ -1482,7 +1505,7 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
                  for name, evs in path.events.items()}
     eager_ms = dict(kernel_ms)
     if not args.no_graph:
-        for name, us in path.kernel_graph_us(stream).items():
+        for name, us in path.kernel_graph_us(stream, sync=lambda: barrier(world)).items():
             kernel_ms[name] = us / 1e3
     totals = {name: (kernel_ms[name] or 0) * len(path.events[name]) for name in kernel_ms}
     dominant = max(totals, key=totals.get)
@@ -1516,13 +1539,22 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
         torch.cuda.synchronize(device)
         barrier(world)
         us = max_over_ranks(a0.elapsed_time(a1), world, device) * 1e3 / 50
-        allreduce = {"avg_us": us, "bytes": path.scores.numel() * 4, "share_of_step": us / (ms_per_step * 1e3),
+        allreduce = {"avg_us": us, "bytes": path.scores.numel() * 4,
                      "timing": "50 back-to-back NCCL all-reduces of the step's fp32 score vector, max over ranks"}
+        if path.peer is None:
+            allreduce["share_of_step"] = us / (ms_per_step * 1e3)
+        else:
+            allreduce["on_step"] = ("no: the select kernel sums the ranks' scores over NVLink peer memory "
+                                    "(cb_select_topk_peer); kernels.select includes that exchange")
 
     # ---- e2e: public API with host buffers (H2D of reused chunks inside the step)
     e2e = None
     if e2e_on:
+        wl.peer = path.peer
         e2e = run_e2e(args, wl, device, world, group, span)
+        wl.peer = None
+    peer_on = path.peer is not None
+    path.close()
     del path, wl
     torch.cuda.empty_cache()
 
@@ -1540,7 +1572,7 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
         "config": workload_config(shape, span, shape.kv_heads // shard, world, shard),
         "gpu_launches": (2 * shape.layers + (1 if path_fused else 2)) * steps,
         "launch": "eager, one stream" if args.no_graph else (
-            ("cuda-graph" if world == 1 else "two cuda-graphs around the NCCL all-reduce")
+            ("cuda-graph" if world == 1 or peer_on else "two cuda-graphs around the NCCL all-reduce")
             + (", loads on a side stream beside the commits" if 2 * shape.kv_heads // shard * 128 < 2048
                else "")),
         "kernel_timing": ("CUDA events around each launch in an eager pass of the same steps"
@@ -1548,6 +1580,9 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
                              "as a CUDA graph between two events (deviation / select: ten launches over "
                              "four rotating input sets, 512 MiB, so each reads its inputs from HBM)")),
         "roofline": roofline, "kernels": per_kernel, "e2e": e2e, "allreduce": allreduce,
+        "score_reduction": None if world == 1 else (
+            "inside the select kernel: NVLink peer stores + bounded flag waits (cb_select_topk_peer)"
+            if peer_on else "NCCL all-reduce between two graphs"),
         "clocks": clocks.summary(), "cpu_baseline": cpu,
     }
 

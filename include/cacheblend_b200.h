@@ -245,6 +245,54 @@ CB_API int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t
                    int64_t* out_index, int64_t out_capacity, void* stream);
 
 /*
+ * Tensor-parallel selection with the score reduction done over NVLink peer
+ * memory: the TP all-reduce of the partial scores and `_select`
+ * (cacheblend_vllm/ascend.py:764-770 tensor_model_parallel_all_reduce, then
+ * 771-796) in one launch of one 8-CTA cluster per rank, replacing the NCCL
+ * all-reduce + cb_select_topk pair.  Every rank owns an exchange buffer
+ * (cb_peer_select_buffer_size bytes for its world size and the largest token
+ * count it will select over) that every rank maps: the owner creates it with
+ * cb_peer_buffer_create (zeroed; the 64-byte CUDA IPC handle goes to the other
+ * ranks), the others open it with cb_peer_buffer_open.  `buffers` is a HOST
+ * array of `world` device addresses, indexed by rank (this rank's own buffer
+ * and the opened mappings of the others').  Each call stores this rank's
+ * partial scores into every rank's buffer, waits (bounded, 2 s) for every
+ * rank's scores of the same call, sums them in rank order (rank 0 first: the
+ * same fp32 sum on every rank, so every rank selects the same tokens), writes
+ * the sum to `summed` (may be NULL) and selects exactly like cb_select_topk.
+ * All ranks size their buffers for the same world and max_tokens and make
+ * the same sequence of calls with the same n, k and base mask, on streams that
+ * run them in call order; n <= max_tokens <= 360,448.  `device`: the CUDA
+ * device the buffer lives on (create) or is mapped into (open, close).
+ * A wait that gives up stores 5 in *device_error (if not NULL): that call's
+ * result is wrong, later calls are right again once the late rank catches up.
+ * cb_peer_buffer_reset zeroes the call counters (all ranks, at a quiescent
+ * point, e.g. after an error); close opened mappings before the owners
+ * destroy their buffers.
+ */
+#define CB_IPC_HANDLE_BYTES 64
+CB_API int cb_peer_select_buffer_size(int world, int64_t max_tokens, int64_t* bytes);
+CB_API int cb_peer_buffer_create(int device, int64_t bytes, void** buffer, void* ipc_handle);
+CB_API int cb_peer_buffer_open(int device, const void* ipc_handle, void** buffer);
+CB_API int cb_peer_buffer_close(int device, void* buffer);
+CB_API int cb_peer_buffer_destroy(int device, void* buffer);
+CB_API int cb_peer_buffer_reset(void* buffer, int world, int64_t max_tokens, void* stream);
+CB_API int cb_select_topk_peer(const float* partial, const uint8_t* base_mask, int64_t n, int64_t k,
+                               int64_t* out_index, int64_t out_capacity, const uint64_t* buffers,
+                               int rank, int world, int64_t max_tokens, float* summed,
+                               int32_t* device_error, void* stream);
+/*
+ * The same exchange with every rank played by one cooperative launch on one
+ * GPU (cluster r is rank r; `buffers` are all local): partial is
+ * [world][n] fp32, out_index [world][out_capacity], summed [world][n].  The
+ * single-GPU check of the multi-rank protocol.
+ */
+CB_API int cb_select_topk_peer_all_ranks(const float* partial, const uint8_t* base_mask, int64_t n,
+                                         int64_t k, int64_t* out_index, int64_t out_capacity,
+                                         const uint64_t* buffers, int world, int64_t max_tokens,
+                                         float* summed, int32_t* device_error, void* stream);
+
+/*
  * Bytes of the workspace cb_kv_deviation_select needs (a 2048-bin histogram
  * and a completion ticket).
  */

@@ -37,6 +37,7 @@ import torch
 from .attention import attention_supported, attention_workspace_bytes, blend_attention
 from .config import CacheBlendConfig
 from .rope import validate_rope_support
+from .peer_exchange import MAX_PEERS, MAX_TOKENS, PeerScoreExchange
 from .selection import (deviation_select, kv_deviation, select_tokens, selection_overlap,
                         sparse_q_scores, tp_world_size)
 from .trace import PipelineTracer
@@ -50,6 +51,9 @@ _FUSED_ATTENTION = os.environ.get("CACHEBLEND_B200_ATTENTION", "").lower() == "f
 # CACHEBLEND_B200_FUSED_SELECT=1: K-deviation and selection of a one-rank check layer as one
 # launch (cb_kv_deviation_select) instead of two (measured slower on B200 so far: off by default)
 _FUSED_SELECT = os.environ.get("CACHEBLEND_B200_FUSED_SELECT", "") == "1"
+# With TP the score all-reduce runs inside the select kernel over NVLink peer memory
+# (cb_select_topk_peer); CACHEBLEND_B200_PEER_SELECT=0 puts vLLM's NCCL all-reduce back.
+_PEER_SELECT = os.environ.get("CACHEBLEND_B200_PEER_SELECT", "1") != "0"
 
 _EMBEDDING_HOOKS = ("get_input_embeddings", "embed_input_ids")
 
@@ -166,6 +170,19 @@ class Qwen3BlendExecutor:
         self.block_size = block_size
         self.layers = layers
         self.tp_group = _tensor_parallel_group()
+        self._peer: PeerScoreExchange | None = None  # made by the first TP selection
+
+    def _peer_exchange(self, tokens: int, device: torch.device) -> PeerScoreExchange | None:
+        """The TP group's peer-memory score exchange when this selection can use it.  Every
+        rank reaches the same decision (same request, same token count), and the exchange
+        is created collectively by the first selection that needs it."""
+        world = tp_world_size(self.tp_group)
+        if not (_PEER_SELECT and self.config.tp_global_selection and 1 < world <= MAX_PEERS
+                and tokens <= MAX_TOKENS and device.type == "cuda"):
+            return None
+        if self._peer is None:
+            self._peer = PeerScoreExchange(self.tp_group, MAX_TOKENS, device)
+        return self._peer
 
     # ------------------------------------------------------------------ request
     def run(self, request_id: str, tokens: list[int], plan: BlendPlan, loader) -> None:
@@ -284,7 +301,8 @@ class Qwen3BlendExecutor:
                 forced_mask=None) -> torch.Tensor:
         """TP-summed, budgeted top-k united with the gap (and forced) rows (ascend.py:757-796)."""
         return select_tokens(scores, gaps, self.config.ratio_for_layer(layer_id), forced_mask,
-                             tp_group=self.tp_group, global_selection=self.config.tp_global_selection)
+                             tp_group=self.tp_group, global_selection=self.config.tp_global_selection,
+                             peer_exchange=self._peer_exchange(scores.numel(), scores.device))
 
     def _stage_and_attend(self, layer, rows: _Rows, staging: torch.Tensor,
                           state: BlendExecutionState) -> torch.Tensor:

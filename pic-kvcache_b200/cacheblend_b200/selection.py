@@ -8,6 +8,8 @@
 * ``select_tokens`` -- optional TP all-reduce of the scores (every rank then
   runs the same deterministic kernel, so the reference's rank-0 broadcast is
   unnecessary) and ``cb_select_topk``: ascending indices of base ∪ top-k.
+  With a ``PeerScoreExchange`` the all-reduce runs inside the select kernel
+  over NVLink peer memory (``cb_select_topk_peer``).
 * ``deviation_select`` -- both in one launch (``cb_kv_deviation_select``) when
   no all-reduce sits between them (one rank, or per-rank selection).
 * ``sparse_q_masks`` -- query set, forced set and tail fallback of
@@ -232,9 +234,15 @@ def select_tokens(
     tp_group=None,
     global_selection: bool = True,
     base_mask_device: torch.Tensor | None = None,
+    peer_exchange=None,
 ) -> torch.Tensor:
-    """Full ``_select``: TP reduction, budget, masked top-k, ascending union."""
-    if global_selection and tp_world_size(tp_group) > 1:
+    """Full ``_select``: TP reduction, budget, masked top-k, ascending union.
+
+    With a ``peer_exchange`` (``PeerScoreExchange`` of the TP group) the
+    reduction runs inside the select kernel over NVLink peer memory instead of
+    a NCCL all-reduce; ``scores`` are then this rank's partial scores."""
+    use_peer = peer_exchange is not None and global_selection
+    if global_selection and tp_world_size(tp_group) > 1 and not use_peer:
         scores = tp_all_reduce(scores, tp_group)
     gaps = _as_host_mask(gap_mask, "gap_mask")
     base = gaps.copy()
@@ -250,6 +258,8 @@ def select_tokens(
     k = recompute_budget(active, int(gaps.sum()), base_count, ratio)
     if base_mask_device is None:
         base_mask_device = _upload(base.astype(np.uint8), scores.device)
+    if use_peer:
+        return peer_exchange.select(scores.contiguous(), base_mask_device, k, base_count + k)
     return select_from_scores(scores.contiguous(), base_mask_device, k, base_count + k)
 
 

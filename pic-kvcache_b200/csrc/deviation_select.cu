@@ -21,6 +21,9 @@
 #include <mutex>
 #include <tuple>
 
+#include <string.h>
+
+#include "cb_async.cuh"
 #include "cb_common.cuh"
 
 namespace cb {
@@ -388,7 +391,8 @@ template <typename Passes>
 __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const float* scores,
                                                const uint8_t* base, int64_t n, int64_t k,
                                                int64_t* out, int64_t cap, int slice, uint32_t* dyn,
-                                               uint32_t prefix, uint32_t pmask, int64_t krem) {
+                                               uint32_t prefix, uint32_t pmask, int64_t krem,
+                                               bool keys_ready = false) {
   const int rank = static_cast<int>(cluster.block_rank());
   uint32_t* keys = dyn;
   uint8_t* flags = reinterpret_cast<uint8_t*>(keys + slice);
@@ -407,9 +411,11 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
   const int64_t lo = (int64_t)rank * slice;
   const int64_t hi = lo + slice < n ? lo + slice : n;
   const int m = hi > lo ? static_cast<int>(hi - lo) : 0;
-  for (int i = tid; i < m; i += kSelThreads) {
-    keys[i] = order_key(__ldcg(scores + lo + i));  // L2: other CTAs may have just written them
-    flags[i] = base[lo + i] != 0;
+  if (!keys_ready) {  // else the caller filled keys[0, m) and flags[0, m)
+    for (int i = tid; i < m; i += kSelThreads) {
+      keys[i] = order_key(__ldcg(scores + lo + i));  // L2: other CTAs may have just written them
+      flags[i] = base[lo + i] != 0;
+    }
   }
   if (tid < 256) {
     local[tid] = 0;
@@ -617,6 +623,130 @@ __global__ void __launch_bounds__(kSelThreads, 1) deviation_select_kernel(
     if (tid == 0) ws->ticket = 0;
   }
   cluster_select<TailPasses>(cluster, scores, base, a.n, k, out, cap, slice, dyn, prefix, pmask, krem);
+}
+
+// ---- TP selection with the score reduction over peer memory -------------------
+// `_select` after the TP all-reduce (ascend.py:764-796) with the reduction done
+// in this kernel over NVLink instead of by a separate NCCL collective.  Every
+// rank owns an exchange buffer that all ranks map (CUDA IPC):
+//   recv  [2][world][capacity] fp32   one row per sending rank, double-buffered by call parity
+//   flags [kMaxPeers][8] u32          [r][c]: calls of rank r whose slice c has landed here
+//   count [8] u32                     this rank's finished calls, per cluster CTA
+// Cluster CTA c owns tokens [c * slice, (c + 1) * slice): it stores its slice
+// of the local partial scores into row `rank` of every rank's receive buffer
+// (plain stores through the peer mapping), fences at system scope, bumps
+// flag [rank][c] on every rank, waits (bounded) until every rank has bumped
+// its own flags [*][c] to this call's number, then sums the rows in rank
+// order -- the same fp32 order on every rank, so every rank selects the same
+// tokens -- and runs the radix passes and compaction of cluster_select.
+//
+// A rank runs at most one call ahead of another: its call e + 1 waits for the
+// other's bump of call e + 1, which the other makes only after its call e has
+// read its rows.  So the rows of call e + 2 (same parity as e) never land while
+// call e reads them, and two receive buffers suffice.  A wait that gives up
+// records code 5 and the call goes on with whatever rows are there (its result
+// is wrong, the error word says so); the flags stay consistent, because the
+// late rank still makes its bump, so the next calls are right again.
+//
+// `emulated`: one launch plays every rank on one GPU (cluster w is rank w, all
+// buffers local, partial / out / summed are [world] x their per-rank size); a
+// cooperative launch, so that every cluster is resident while the others wait.
+constexpr int kMaxPeers = 8;
+constexpr int kPeerError = 5;
+
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void add_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+struct PeerArgs {
+  uint64_t base[kMaxPeers];  // each rank's exchange buffer as mapped in this process
+  int rank;
+  int world;
+  int emulated;
+  int64_t capacity;          // fp32 entries per receive row (a multiple of 4)
+  int64_t flags_offset;      // bytes from a buffer's start to its flags
+};
+
+__host__ __device__ inline int64_t peer_flags_offset(int world, int64_t capacity) {
+  return (int64_t)2 * world * capacity * 4;
+}
+
+__device__ __forceinline__ uint32_t* peer_flags(const PeerArgs& p, int r) {
+  return reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(p.base[r]) + p.flags_offset);
+}
+
+__global__ void __launch_bounds__(kSelThreads, 1) select_peer_kernel(
+    const float* __restrict__ partial, const uint8_t* __restrict__ base, int64_t n, int64_t k,
+    int64_t* __restrict__ out, int64_t cap, int slice, PeerArgs peers, float* __restrict__ summed,
+    int32_t* __restrict__ error) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = static_cast<int>(cluster.block_rank());
+  const int me = peers.emulated ? static_cast<int>(blockIdx.x) / kClusterCtas : peers.rank;
+  if (peers.emulated) {
+    partial += (int64_t)me * n;
+    out += (int64_t)me * cap;
+    if (summed != nullptr) summed += (int64_t)me * n;
+  }
+  extern __shared__ __align__(16) uint32_t dyn[];
+  uint32_t* keys = dyn;
+  uint8_t* flags_smem = reinterpret_cast<uint8_t*>(keys + slice);
+  __shared__ uint32_t s_epoch;
+  const int tid = threadIdx.x;
+  const int world = peers.world;
+  const int64_t lo = (int64_t)crank * slice;
+  const int64_t hi = lo + slice < n ? lo + slice : n;
+  const int m = hi > lo ? static_cast<int>(hi - lo) : 0;
+  uint32_t* my_flags = peer_flags(peers, me);
+  uint32_t* my_count = my_flags + kMaxPeers * kClusterCtas;
+  if (tid == 0) s_epoch = my_count[crank] + 1u;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int64_t parity = epoch & 1u;
+  // this CTA's slice of the partial scores into row `me` of every receive buffer,
+  // in 16-byte stores where both sides are aligned (slice and capacity are
+  // multiples of 4 and the buffers 256-byte aligned, so that rests on `partial`)
+  for (int r = 0; r < world; ++r) {
+    float* row = reinterpret_cast<float*>(peers.base[r]) + (parity * world + me) * peers.capacity + lo;
+    const bool vec = ((reinterpret_cast<uintptr_t>(partial + lo) | reinterpret_cast<uintptr_t>(row)) & 15) == 0;
+    const int m4 = vec ? m >> 2 : 0;
+    const float4* src = reinterpret_cast<const float4*>(partial + lo);
+    for (int i = tid; i < m4; i += kSelThreads) reinterpret_cast<float4*>(row)[i] = src[i];
+    for (int i = 4 * m4 + tid; i < m; i += kSelThreads) row[i] = partial[lo + i];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    for (int r = 0; r < world; ++r) add_release_sys(peer_flags(peers, r) + me * kClusterCtas + crank, 1u);
+  }
+  // every rank's slice `crank` of this call has landed here
+  if (tid < world) {
+    const uint32_t* flag = my_flags + tid * kClusterCtas + crank;
+    const uint64_t start = async::global_ns();
+    while (load_acquire_sys(flag) < epoch) {
+      if (async::global_ns() - start > async::kTimeoutNs) {
+        if (error != nullptr) atomicCAS(error, 0, kPeerError);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+  const float* rows = reinterpret_cast<const float*>(peers.base[me]) + parity * world * peers.capacity + lo;
+  for (int i = tid; i < m; i += kSelThreads) {
+    float v = __ldcg(rows + i);
+    for (int r = 1; r < world; ++r) v += __ldcg(rows + r * peers.capacity + i);
+    if (summed != nullptr) summed[lo + i] = v;
+    keys[i] = order_key(v);
+    flags_smem[i] = base[lo + i] != 0;
+  }
+  if (tid == 0) my_count[crank] = epoch;
+  cluster_select<FullPasses>(cluster, nullptr, base, n, k, out, cap, slice, dyn, 0u, 0u, k, true);
 }
 
 // |A n B| of two strictly ascending index lists (the two selections of the
@@ -916,4 +1046,179 @@ extern "C" int cb_kv_deviation_select(const void* fresh, int64_t fresh_row_strid
     return CB_ERR_CUDA;
   }
   return launch_status("cb_kv_deviation_select");
+}
+
+// ---- peer exchange buffers (CUDA IPC) and the TP select ----------------------
+namespace {
+int64_t peer_row_capacity(int64_t n) { return (n + 3) / 4 * 4; }
+int64_t peer_buffer_bytes(int world, int64_t capacity) {
+  return peer_flags_offset(world, capacity) + (int64_t)(kMaxPeers + 1) * kClusterCtas * 4;
+}
+// Makes `device` current for this library's runtime on the calling thread.
+int use_device(int device, const char* name) {
+  clear_error();
+  const cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) {
+    set_error("%s: cudaSetDevice(%d): %s", name, device, cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return CB_OK;
+}
+}  // namespace
+
+extern "C" int cb_peer_select_buffer_size(int world, int64_t max_tokens, int64_t* bytes) {
+  CB_REQUIRE(bytes != nullptr, "null output");
+  CB_REQUIRE(world >= 1 && world <= kMaxPeers, "world size %d outside [1, %d]", world, kMaxPeers);
+  CB_REQUIRE(max_tokens >= 0 && max_tokens <= (int64_t)kClusterCtas * kMaxSlice,
+             "max_tokens %lld outside [0, %lld]", (long long)max_tokens,
+             (long long)((int64_t)kClusterCtas * kMaxSlice));
+  *bytes = peer_buffer_bytes(world, peer_row_capacity(max_tokens));
+  return CB_OK;
+}
+
+extern "C" int cb_peer_buffer_create(int device, int64_t bytes, void** buffer, void* ipc_handle) {
+  CB_REQUIRE(bytes > 0 && buffer != nullptr, "bad buffer request");
+  const int rc = use_device(device, "cb_peer_buffer_create");
+  if (rc != CB_OK) return rc;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e == cudaSuccess) e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (e == cudaSuccess && ipc_handle != nullptr) {
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e == cudaSuccess) memcpy(ipc_handle, &h, sizeof(h));
+  }
+  if (e != cudaSuccess) {
+    if (p != nullptr) cudaFree(p);
+    set_error("cb_peer_buffer_create: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  *buffer = p;
+  return CB_OK;
+}
+
+extern "C" int cb_peer_buffer_open(int device, const void* ipc_handle, void** buffer) {
+  CB_REQUIRE(ipc_handle != nullptr && buffer != nullptr, "null argument");
+  const int rc = use_device(device, "cb_peer_buffer_open");
+  if (rc != CB_OK) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_error("cb_peer_buffer_open: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  *buffer = p;
+  return CB_OK;
+}
+
+extern "C" int cb_peer_buffer_close(int device, void* buffer) {
+  CB_REQUIRE(buffer != nullptr, "null buffer");
+  const int rc = use_device(device, "cb_peer_buffer_close");
+  if (rc != CB_OK) return rc;
+  const cudaError_t e = cudaIpcCloseMemHandle(buffer);
+  if (e != cudaSuccess) {
+    set_error("cb_peer_buffer_close: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return CB_OK;
+}
+
+extern "C" int cb_peer_buffer_destroy(int device, void* buffer) {
+  CB_REQUIRE(buffer != nullptr, "null buffer");
+  const int rc = use_device(device, "cb_peer_buffer_destroy");
+  if (rc != CB_OK) return rc;
+  const cudaError_t e = cudaFree(buffer);
+  if (e != cudaSuccess) {
+    set_error("cb_peer_buffer_destroy: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return CB_OK;
+}
+
+extern "C" int cb_peer_buffer_reset(void* buffer, int world, int64_t max_tokens, void* stream) {
+  CB_REQUIRE(buffer != nullptr, "null buffer");
+  CB_REQUIRE(world >= 1 && world <= kMaxPeers && max_tokens >= 0, "bad world / max_tokens");
+  CB_BIND(stream, buffer);
+  const int64_t off = peer_flags_offset(world, peer_row_capacity(max_tokens));
+  const cudaError_t e = cudaMemsetAsync(static_cast<char*>(buffer) + off, 0,
+                                        (size_t)(kMaxPeers + 1) * kClusterCtas * 4,
+                                        reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("cb_peer_buffer_reset: %s", cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return CB_OK;
+}
+
+namespace {
+int launch_select_peer(const float* partial, const uint8_t* base_mask, int64_t n, int64_t k,
+                       int64_t* out_index, int64_t out_capacity, const uint64_t* buffers, int rank,
+                       int world, int emulated, int64_t max_tokens, float* summed, int32_t* device_error,
+                       void* stream, const char* name) {
+  clear_error();
+  CB_REQUIRE(world >= 1 && world <= kMaxPeers, "world size %d outside [1, %d]", world, kMaxPeers);
+  CB_REQUIRE(emulated || (rank >= 0 && rank < world), "rank %d outside [0, %d)", rank, world);
+  CB_REQUIRE(buffers != nullptr && buffers[emulated ? 0 : rank] != 0, "null buffer table or own buffer");
+  // this rank's own exchange buffer names the device (the scores may be empty)
+  CB_BIND(stream, reinterpret_cast<const void*>(buffers[emulated ? 0 : rank]));
+  CB_REQUIRE(n >= 0 && n <= max_tokens && max_tokens <= (int64_t)kClusterCtas * kMaxSlice,
+             "n %lld outside [0, max_tokens %lld]", (long long)n, (long long)max_tokens);
+  CB_REQUIRE(k >= 0 && k <= n && out_capacity >= 0, "bad n/k");
+  CB_REQUIRE(n == 0 || (partial && base_mask), "null score or mask pointer");
+  CB_REQUIRE(out_capacity == 0 || out_index, "null output pointer");
+  PeerArgs args = {};
+  for (int r = 0; r < world; ++r) {
+    CB_REQUIRE(buffers[r] != 0 && (buffers[r] & 255) == 0, "exchange buffer %d null or unaligned", r);
+    args.base[r] = buffers[r];
+  }
+  args.rank = emulated ? 0 : rank;
+  args.world = world;
+  args.emulated = emulated;
+  args.capacity = peer_row_capacity(max_tokens);
+  args.flags_offset = peer_flags_offset(world, args.capacity);
+  // every call exchanges, also with n == 0: the ranks' call counts stay in step
+  const int slice = static_cast<int>(peer_row_capacity((n + kClusterCtas - 1) / kClusterCtas));
+  const size_t dyn = ((size_t)(slice > 0 ? slice : 4) * 5 + 15) / 16 * 16;
+  const int rc = ensure_dynamic_smem(reinterpret_cast<const void*>(select_peer_kernel), dyn);
+  if (rc != CB_OK) return rc;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3((emulated ? world : 1) * kClusterCtas, 1, 1);
+  config.blockDim = dim3(kSelThreads, 1, 1);
+  config.dynamicSmemBytes = dyn;
+  config.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  config.attrs = attr;
+  config.numAttrs = emulated ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&config, select_peer_kernel, partial, base_mask, n, k, out_index,
+                                           out_capacity, slice > 0 ? slice : 4, args, summed, device_error);
+  if (e != cudaSuccess) {
+    set_error("%s launch failed: %s", name, cudaGetErrorString(e));
+    return CB_ERR_CUDA;
+  }
+  return launch_status(name);
+}
+}  // namespace
+
+extern "C" int cb_select_topk_peer(const float* partial, const uint8_t* base_mask, int64_t n, int64_t k,
+                                   int64_t* out_index, int64_t out_capacity, const uint64_t* buffers,
+                                   int rank, int world, int64_t max_tokens, float* summed,
+                                   int32_t* device_error, void* stream) {
+  return launch_select_peer(partial, base_mask, n, k, out_index, out_capacity, buffers, rank, world, 0,
+                            max_tokens, summed, device_error, stream, "cb_select_topk_peer");
+}
+
+extern "C" int cb_select_topk_peer_all_ranks(const float* partial, const uint8_t* base_mask, int64_t n,
+                                             int64_t k, int64_t* out_index, int64_t out_capacity,
+                                             const uint64_t* buffers, int world, int64_t max_tokens,
+                                             float* summed, int32_t* device_error, void* stream) {
+  return launch_select_peer(partial, base_mask, n, k, out_index, out_capacity, buffers, 0, world, 1,
+                            max_tokens, summed, device_error, stream, "cb_select_topk_peer_all_ranks");
 }

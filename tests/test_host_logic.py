@@ -201,3 +201,30 @@ def test_fingerprints_match_reference_vectors():
     assert [content_hash([7]), content_hash([-1, 0, 1]), content_hash([])] == gold["small"].tolist()
     records = TokenRangeMatcher(256).make_records("m", 0, tokens.tolist(), 16)
     assert [r.segment_id.content_hash for r in records] == gold["chunks"].tolist()
+
+
+def test_select_tokens_routes_tp_reduction_through_the_peer_exchange():
+    """With a peer exchange the TP reduction happens inside its select kernel: no
+    all-reduce call, the partial scores and the reference budget go to the exchange."""
+    from cacheblend_b200.selection import select_tokens
+
+    class NoAllReduce:
+        world_size = 2
+
+        def all_reduce(self, tensor):
+            raise AssertionError("the NCCL all-reduce must not run beside the peer exchange")
+
+    class Exchange:
+        def select(self, scores, base, k, capacity):
+            self.args = (scores, base, k, capacity)
+            return torch.arange(capacity)
+
+    gaps = np.zeros(100, dtype=bool)
+    gaps[:10] = True
+    partial = torch.rand(100)
+    exchange = Exchange()
+    out = select_tokens(partial, gaps, 0.2, tp_group=NoAllReduce(), peer_exchange=exchange,
+                        base_mask_device=torch.from_numpy(gaps.astype(np.uint8)))
+    scores, base, k, capacity = exchange.args
+    assert scores is partial and k == recompute_budget(100, 10, 10, 0.2) == 18 and capacity == 28
+    assert out.numel() == 28
