@@ -262,7 +262,7 @@ CB_API int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t
  * the sum to `summed` (may be NULL) and selects exactly like cb_select_topk.
  * All ranks size their buffers for the same world and max_tokens and make
  * the same sequence of calls with the same n, k and base mask, on streams that
- * run them in call order; n <= max_tokens <= 360,448.  `device`: the CUDA
+ * run them in call order; n <= max_tokens <= 344,064.  `device`: the CUDA
  * device the buffer lives on (create) or is mapped into (open, close).
  * A wait that gives up stores 5 in *device_error (if not NULL): that call's
  * result is wrong, later calls are right again once the late rank catches up.

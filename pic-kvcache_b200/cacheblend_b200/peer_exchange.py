@@ -27,7 +27,7 @@ from . import _native
 
 IPC_HANDLE_BYTES = 64
 MAX_PEERS = 8
-MAX_TOKENS = 8 * 44 * 1024  # one 8-CTA cluster's shared memory holds the scores' order keys
+MAX_TOKENS = 8 * 42 * 1024  # one 8-CTA cluster's shared memory holds the scores' order keys
 DEVICE_ERROR_PEER_WAIT = 5
 
 

@@ -1075,6 +1075,14 @@ bool use_vector_path(uint64_t addr_acc, int esize, int head_size, int rotary_dim
 #ifndef CB_LOAD_VARIANT
 #define CB_LOAD_VARIANT 0
 #endif
+// CB_LOAD_CTAS > 0 overrides the bulk kernel's CTAs per SM, CB_FLAT_BLOCKS > 0
+// the flat kernel's 256-thread blocks per SM (tuning sweeps only).
+#ifndef CB_LOAD_CTAS
+#define CB_LOAD_CTAS 0
+#endif
+#ifndef CB_FLAT_BLOCKS
+#define CB_FLAT_BLOCKS 0
+#endif
 
 template <typename T, bool NEOX, int S, int LAG>
 int launch_bulk_variant(const LoadArgs& a, int tile_bytes, int ctas_per_sm, int row_bytes,
@@ -1082,6 +1090,7 @@ int launch_bulk_variant(const LoadArgs& a, int tile_bytes, int ctas_per_sm, int 
   int rows = tile_bytes / (row_bytes + cs_bytes);
   if (rows > tma::kMaxRows) rows = tma::kMaxRows;
   const int64_t tiles = 2 * ((a.alloc_end + rows - 1) / rows);
+  if (CB_LOAD_CTAS > 0) ctas_per_sm = CB_LOAD_CTAS;
   const int64_t cap = static_cast<int64_t>(kSmCount) * ctas_per_sm;
   const int grid = static_cast<int>(tiles < cap ? tiles : cap);
   auto kernel = tma::blend_load_bulk_kernel<T, NEOX, S, LAG>;
@@ -1143,7 +1152,8 @@ int dispatch_load(const LoadArgs& a, bool vec, bool neox, int64_t max_ctas, int3
   if (vec && max_ctas <= 0 && flat_ok && (row_bytes < 1024 || CB_LOAD_VARIANT == 9)) {
     // device-memory sources, rows under 1 KiB: one thread per 16-byte item
     const int64_t blocks = (flat_items + 255) / 256;
-    const int grid = static_cast<int>(blocks < kSmCount * 8 ? blocks : kSmCount * 8);
+    const int64_t cap = (int64_t)kSmCount * (CB_FLAT_BLOCKS > 0 ? CB_FLAT_BLOCKS : 8);
+    const int grid = static_cast<int>(blocks < cap ? blocks : cap);
     if (neox)
       tma::blend_load_flat_kernel<T, true><<<grid, 256, 0, s>>>(a);
     else

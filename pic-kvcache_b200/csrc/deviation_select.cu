@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(kSelThreads) select_topk_kernel(
 // ranks, again read through DSMEM.  Scores cross HBM/L2 once.
 namespace cg = cooperative_groups;
 constexpr int kClusterCtas = 8;
-constexpr int kMaxSlice = 44 * 1024;  // keys per CTA: 5 bytes each in shared memory
+constexpr int kMaxSlice = 42 * 1024;  // keys per CTA: 5 bytes each in shared memory
 
 __device__ __forceinline__ void find_digit(const uint32_t* hist, int64_t krem, uint32_t* s_digit,
                                            int64_t* s_above) {
@@ -382,11 +382,29 @@ struct TailPasses {
   }
 };
 
-// The selection by one cluster of 8 CTAs (shared by select_cluster_kernel and
-// the fused deviation select): this CTA's slice of order keys and base flags in
-// shared memory, the remaining radix passes merged into rank 0's histogram
-// through DSMEM, then the ordered compaction.  `prefix`, `pmask`, `krem`: the
-// digits already fixed and the rank still sought among keys with that prefix.
+// Cluster barrier halves (PTX barrier.cluster): `arrive` at kernel start and
+// `wait` just before the first access to another CTA's shared memory, which
+// must not come before that CTA has started.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// The selection by one cluster of 8 CTAs (shared by select_cluster_kernel, the
+// fused deviation select and the peer-exchange select): this CTA's slice of
+// order keys and base flags in shared memory, the remaining radix passes, then
+// the ordered compaction.  `prefix`, `pmask`, `krem`: the digits already fixed
+// and the rank still sought among keys with that prefix.
+//
+// Every CTA pushes its local histogram of a pass into slot [its rank] of every
+// CTA's inbox (DSMEM stores, 16-bit counts: a slice holds < 65,536 keys), so
+// after the pass's one cluster barrier each CTA merges and searches its own
+// copy from local shared memory.  The inbox is double-buffered by pass: pass
+// p + 2 writes buffer p % 2 only after the barrier of pass p + 1, which every
+// CTA reaches after merging pass p.  The compaction's per-CTA totals travel
+// the same way, so the last barrier is the totals' one.  The caller must have
+// made the cluster barrier's arrive (cluster_arrive_relaxed) once, and must not
+// have waited on it: the first wait here completes it.
 template <typename Passes>
 __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const float* scores,
                                                const uint8_t* base, int64_t n, int64_t k,
@@ -396,15 +414,11 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
   const int rank = static_cast<int>(cluster.block_rank());
   uint32_t* keys = dyn;
   uint8_t* flags = reinterpret_cast<uint8_t*>(keys + slice);
-  // rank 0's copy is the cluster histogram, triple-buffered by pass: buffer
-  // p % 3 receives pass p's counts.  Rank 0 zeroes buffer (p + 1) % 3 while it
-  // counts pass p: that buffer was last read by pass p - 2's digit search,
-  // which every CTA finished before the barrier of pass p - 1, and it is first
-  // added to after the barrier of pass p.  So one cluster barrier per pass.
-  __shared__ uint32_t hist[3][256];
+  __shared__ uint32_t inbox[2][kClusterCtas][128];  // 256 16-bit counts per CTA, packed in pairs
   __shared__ uint32_t local[256];
+  __shared__ uint32_t merged[256];
+  __shared__ uint32_t all_totals[kClusterCtas][2];  // every CTA's (selected, tied) counts
   __shared__ int64_t warp_sums[32];
-  __shared__ int64_t totals[2];    // this CTA's (selected, tied) counts
   __shared__ uint32_t s_digit;
   __shared__ int64_t s_above;
   const int tid = threadIdx.x;
@@ -417,24 +431,15 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
       flags[i] = base[lo + i] != 0;
     }
   }
-  if (tid < 256) {
-    local[tid] = 0;
-    if (rank == 0) hist[0][tid] = 0;
-  }
-  // the passes and the compaction read entries other threads loaded (with k == 0
-  // no pass runs), and every CTA's first adds must follow rank 0's zeroing
-  if (k > 0)
-    cluster.sync();
-  else
-    __syncthreads();
+  if (tid < 256) local[tid] = 0;
+  __syncthreads();
+  bool waited = false;
   if (k > 0) {
 #pragma unroll 1
     for (int pass = 0; pass < Passes::kCount; ++pass) {
       const RadixPass digit = Passes::at(pass);
       const int shift = digit.shift;
       const uint32_t digit_mask = (1u << digit.width) - 1u;
-      uint32_t* root_hist = cluster.map_shared_rank(&hist[pass % 3][0], 0);
-      if (rank == 0 && tid < 256) hist[(pass + 1) % 3][tid] = 0;
       if (tid == 0) {
         s_digit = 0;  // see select_topk_kernel: degrades safely if k > #candidates
         s_above = 0;
@@ -444,12 +449,26 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
         if (!flags[i] && (key & pmask) == prefix) atomicAdd(&local[(key >> shift) & digit_mask], 1u);
       }
       __syncthreads();
-      if (tid < 256) {
-        if (local[tid]) atomicAdd(&root_hist[tid], local[tid]);
-        local[tid] = 0;  // this thread's own bin: ready for the next pass
+      if (!waited) {
+        cluster_wait();  // every CTA has started: its shared memory may be written
+        waited = true;
+      }
+      if (tid < 128) {
+        const uint32_t pair = local[2 * tid] | (local[2 * tid + 1] << 16);
+        local[2 * tid] = 0;  // this thread's own bins: ready for the next pass
+        local[2 * tid + 1] = 0;
+#pragma unroll
+        for (int r = 0; r < kClusterCtas; ++r) *cluster.map_shared_rank(&inbox[pass & 1][rank][tid], r) = pair;
       }
       cluster.sync();
-      if (tid < 32) find_digit(root_hist, krem, &s_digit, &s_above);
+      if (tid < 256) {
+        uint32_t sum = 0;
+#pragma unroll
+        for (int r = 0; r < kClusterCtas; ++r) sum += (inbox[pass & 1][r][tid >> 1] >> ((tid & 1) * 16)) & 0xffffu;
+        merged[tid] = sum;
+      }
+      __syncthreads();
+      if (tid < 32) find_digit(merged, krem, &s_digit, &s_above);
       __syncthreads();
       prefix |= s_digit << shift;
       pmask |= digit_mask << shift;
@@ -457,6 +476,7 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
       __syncthreads();  // all threads read s_digit before the next pass resets it
     }
   }
+  if (!waited) cluster_wait();
   const uint32_t thr = prefix;
   const int64_t k_eq = k > 0 ? krem : 0;
   const bool any = k > 0;
@@ -474,23 +494,22 @@ __device__ __forceinline__ void cluster_select(cg::cluster_group& cluster, const
         ++c_eq;
     }
   }
-  int64_t sel_total, eq_total;
-  int64_t sel_before = block_exclusive_scan(c_sel, warp_sums, sel_total);
-  int64_t eq_before = block_exclusive_scan(c_eq, warp_sums, eq_total);
-  if (tid == 0) {
-    totals[0] = sel_total;
-    totals[1] = eq_total;
+  // one scan of both counts: (selected << 32) | tied, neither passes 2^32 in a slice
+  int64_t total;
+  const int64_t before = block_exclusive_scan((c_sel << 32) | c_eq, warp_sums, total);
+  if (tid < kClusterCtas) {
+    uint32_t* slot = cluster.map_shared_rank(&all_totals[rank][0], tid);
+    slot[0] = static_cast<uint32_t>(total >> 32);
+    slot[1] = static_cast<uint32_t>(total & 0xffffffff);
   }
-  cluster.sync();
+  cluster.sync();  // the last access to another CTA's shared memory came before this
   int64_t sel_off = 0, eq_off = 0;
   for (int r = 0; r < rank; ++r) {
-    const int64_t* other = cluster.map_shared_rank(totals, r);
-    sel_off += other[0];
-    eq_off += other[1];
+    sel_off += all_totals[r][0];
+    eq_off += all_totals[r][1];
   }
-  cluster.sync();  // no CTA may leave while a peer still reads its totals
-  sel_before += sel_off;
-  eq_before += eq_off;
+  int64_t sel_before = (before >> 32) + sel_off;
+  int64_t eq_before = (before & 0xffffffff) + eq_off;
   for (int i = a0; i < a1; ++i) {
     const int64_t index = lo + i;
     if (flags[i] || (any && keys[i] > thr)) {
@@ -508,6 +527,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_cluster_kernel(
     const float* __restrict__ scores, const uint8_t* __restrict__ base, int64_t n, int64_t k,
     int64_t* __restrict__ out, int64_t cap, int slice) {
   cg::cluster_group cluster = cg::this_cluster();
+  cluster_arrive_relaxed();
   extern __shared__ __align__(16) uint32_t dyn[];
   cluster_select<FullPasses>(cluster, scores, base, n, k, out, cap, slice, dyn, 0u, 0u, k);
 }
@@ -622,6 +642,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) deviation_select_kernel(
     for (int b = tid; b < kWideBins; b += kSelThreads) ws->hist[b] = 0;
     if (tid == 0) ws->ticket = 0;
   }
+  cluster_arrive_relaxed();  // cluster_select's first wait pairs with it
   cluster_select<TailPasses>(cluster, scores, base, a.n, k, out, cap, slice, dyn, prefix, pmask, krem);
 }
 
@@ -660,8 +681,8 @@ __device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-__device__ __forceinline__ void add_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void add_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 struct PeerArgs {
@@ -686,6 +707,7 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_peer_kernel(
     int64_t* __restrict__ out, int64_t cap, int slice, PeerArgs peers, float* __restrict__ summed,
     int32_t* __restrict__ error) {
   cg::cluster_group cluster = cg::this_cluster();
+  cluster_arrive_relaxed();  // cluster_select's first wait pairs with it
   const int crank = static_cast<int>(cluster.block_rank());
   const int me = peers.emulated ? static_cast<int>(blockIdx.x) / kClusterCtas : peers.rank;
   if (peers.emulated) {
@@ -719,10 +741,14 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_peer_kernel(
     for (int i = tid; i < m4; i += kSelThreads) reinterpret_cast<float4*>(row)[i] = src[i];
     for (int i = 4 * m4 + tid; i < m; i += kSelThreads) row[i] = partial[lo + i];
   }
+  // Release: the block barrier orders every thread's stores before warp 0's
+  // system-scope fence, and each flag bump follows that fence (one fence for
+  // all ranks' flags; a release on every bump would wait out the NVLink round
+  // trip of the bump before it).
   __syncthreads();
-  if (tid == 0) {
+  if (tid < 32) {
     __threadfence_system();
-    for (int r = 0; r < world; ++r) add_release_sys(peer_flags(peers, r) + me * kClusterCtas + crank, 1u);
+    if (tid < world) add_relaxed_sys(peer_flags(peers, tid) + me * kClusterCtas + crank, 1u);
   }
   // every rank's slice `crank` of this call has landed here
   if (tid < world) {

@@ -147,7 +147,13 @@ struct Policy {
 
 inline Policy pick_policy(int64_t row_bytes) {
   Policy p{8 * 1024, 4};                                  // rows of 2 KiB and more
-  if (row_bytes < 1024) p = Policy{4 * 1024, 8};          // e.g. one 128-dim head
+  // e.g. one or two 128-dim heads.  5 CTAs per SM, not the 8 that are fastest
+  // for a scatter alone (7.1 vs 8.4 us at one head): the loader runs the next
+  // layer's load beside each commit on another stream, and with 5 the two
+  // kernels share the SMs -- the pipelined load + commit step of a 32,768-token
+  // request measured 0.470 vs 0.538 ms at one head and 0.951 vs 1.016 ms at
+  // two (B200; 3, 4 and 6 CTAs were slower than 5, and at 1 KiB rows 6 stays).
+  if (row_bytes < 1024) p = Policy{4 * 1024, 5};
   else if (row_bytes < 2048) p = Policy{8 * 1024, 6};     // e.g. four heads
   if (CB_RUN_UNIT_KB > 0) p.unit_bytes = CB_RUN_UNIT_KB * 1024;
   if (CB_RUN_CTAS > 0) p.ctas_per_sm = CB_RUN_CTAS;

@@ -285,7 +285,7 @@ def test_select_golden(golden, cuda, case):
     assert np.array_equal(out.cpu().numpy(), golden[f"sel_{case}_out"])
 
 
-@pytest.mark.parametrize("n", [1, 2, 7, 31, 1024, 1025, 32768, 65535, 98303, 400_000])
+@pytest.mark.parametrize("n", [1, 2, 7, 31, 1024, 1025, 32768, 65535, 98303, 344_064, 344_065, 400_000])
 def test_select_vs_oracle_random_with_ties(cuda, n):
     rng = np.random.default_rng(n)
     scores = rng.integers(0, max(4, n // 8), size=n).astype(np.float32)  # many ties

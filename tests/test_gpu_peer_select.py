@@ -103,7 +103,7 @@ def test_abi_rejects_bad_arguments(cuda):
     lib = _native.load_library()
     size = ctypes.c_int64(0)
     assert lib.cb_peer_select_buffer_size(9, 100, ctypes.byref(size)) == _native.CB_ERR_INVALID
-    assert lib.cb_peer_select_buffer_size(2, 8 * 44 * 1024 + 1, ctypes.byref(size)) == _native.CB_ERR_INVALID
+    assert lib.cb_peer_select_buffer_size(2, 8 * 42 * 1024 + 1, ctypes.byref(size)) == _native.CB_ERR_INVALID
     assert lib.cb_peer_select_buffer_size(2, 100, ctypes.byref(size)) == 0 and size.value > 0
     scores = torch.zeros(100, device=cuda)
     base = torch.zeros(100, dtype=torch.uint8, device=cuda)
