@@ -324,8 +324,8 @@ CB_API int cb_kv_deviation_select(const void* fresh, int64_t fresh_row_stride, c
                                   int64_t workspace_bytes, void* stream);
 
 /*
- * Workspace bytes cb_blend_attention needs (dense per-KV-head query rows, the
- * transposed values, row positions and tile bounds).  Same shape limits as
+ * Workspace bytes cb_blend_attention needs (row positions, tile bounds and the
+ * rows' log2-sum-exps).  Same shape limits as
  * Sparse-Q: head_size 128, bf16 or fp16, (q heads / KV heads) dividing 128.
  */
 CB_API int cb_blend_attention_workspace_size(int64_t num_queries, int64_t num_keys,
@@ -341,9 +341,14 @@ CB_API int cb_blend_attention_workspace_size(int64_t num_queries, int64_t num_ke
  * value [num_keys][num_kv_heads][head_size] (staging rows = positions),
  * query head h attends KV head h / (num_q_heads / num_kv_heads):
  *   w = T(T(q . k) * scale), p = softmax over keys k <= pos of w (fp32),
- *   out = T(sum_k p v).
- * exact_rounding = 0 computes w = (q . k) * scale in fp32 instead (the
- * reference's fused attention kernel, ascend.py:814-830); it needs scale > 0.
+ *   out = T(sum_k T(p) v).
+ * exact_rounding = 1 follows that order: one launch computes each row's
+ * log2-sum-exp of w, a second rounds the normalized p to T before P V.
+ * exact_rounding = 2 keeps the roundings of w in one launch (flash order: the
+ * unnormalized exp2 values rounded to T, O divided by the row sum at the end;
+ * within one T ulp per probability).  exact_rounding = 0 computes
+ * w = (q . k) * scale in fp32, flash order (the reference's fused attention
+ * kernel, ascend.py:814-830); it needs scale > 0.
  * Strides in bytes, rows and heads 16-byte aligned, heads contiguous within a
  * row.  On the tensor cores: QK^T and PV with tcgen05.mma, accumulators in
  * TMEM, operands staged by TMA; device_error (optional) receives a code if a

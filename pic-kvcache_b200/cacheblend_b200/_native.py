@@ -21,7 +21,7 @@ LIB_PATH = Path(
     os.environ.get("CACHEBLEND_B200_LIB")
     or Path(__file__).resolve().parent / "_lib" / "libcacheblend_b200.so"
 )
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 CB_OK = 0
 CB_ERR_INVALID = -1

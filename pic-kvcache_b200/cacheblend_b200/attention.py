@@ -16,6 +16,10 @@ import torch
 from . import _native
 
 
+# exact_rounding argument -> the C ABI's mode code
+_MODES = {True: 1, "reference": 1, "flash": 2, False: 0, "fused": 0}
+
+
 def attention_supported(query: torch.Tensor, key: torch.Tensor) -> bool:
     """Shapes cb_blend_attention takes: head size 128, bf16 / fp16, query heads
     a multiple of KV heads with the group count dividing 128."""
@@ -44,14 +48,25 @@ def blend_attention(
     workspace: torch.Tensor | None = None,
     device_error: torch.Tensor | None = None,
     stream: torch.cuda.Stream | None = None,
-    exact_rounding: bool = True,
+    exact_rounding: bool | str = True,
 ) -> torch.Tensor:
     """out [Nq, Hq, D] for query [Nq, Hq, D] at ``query_positions`` (each in [0, Nk)),
     key / value [Nk, Hkv, D] (rows = positions).
 
-    ``exact_rounding`` keeps the einsum path's roundings (element-type logits, element-type
-    logit * scale); False computes fp32 logits * scale like the reference's fused attention
-    kernel (ascend.py:814-830) and flash attention, about a fifth faster."""
+    ``exact_rounding``:
+
+    * True / ``"reference"`` -- the einsum path's roundings in its order (element-type
+      logits, element-type logit * scale, the normalized probabilities rounded to the
+      element type before P V): a row log2-sum-exp launch, then the products.
+    * ``"flash"`` -- the same logit roundings in one launch with the unnormalized
+      probabilities rounded and the row sum divided at the end (within one element-type
+      ulp per probability of the reference).
+    * False / ``"fused"`` -- fp32 logits * scale like the reference's fused attention
+      kernel (ascend.py:814-830) and flash attention, in one launch."""
+    mode = _MODES.get(exact_rounding if isinstance(exact_rounding, str) else bool(exact_rounding))
+    if mode is None:
+        raise ValueError(f"exact_rounding must be True, False, 'reference', 'flash' or 'fused', "
+                         f"not {exact_rounding!r}")
     _native.require_cuda(query, key, value)
     if query.ndim != 3 or key.ndim != 3 or value.shape != key.shape:
         raise ValueError("query must be [tokens, q_heads, head]; key and value [keys, kv_heads, head]")
@@ -77,7 +92,7 @@ def blend_attention(
         "cb_blend_attention", query.data_ptr(), query.stride(0) * esize, key.data_ptr(),
         key.stride(0) * esize, value.data_ptr(), value.stride(0) * esize, num_keys, num_q_heads,
         num_kv_heads, head_size, _native.dtype_code(query.dtype), positions.data_ptr(), num_queries,
-        float(scale), int(bool(exact_rounding)), out.data_ptr(), out.stride(0) * esize,
+        float(scale), mode, out.data_ptr(), out.stride(0) * esize,
         workspace.data_ptr(), workspace.numel(),
         0 if device_error is None else device_error.data_ptr(), _native.stream_handle(stream),
     )

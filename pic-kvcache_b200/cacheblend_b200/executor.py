@@ -44,9 +44,12 @@ from .trace import PipelineTracer
 from .types import BlendPlan
 
 # CACHEBLEND_B200_ATTENTION=fused: fp32 logits like the reference's fused NPU attention
-# (ascend.py:814-830) instead of the einsum path's element-type roundings (the default,
-# which is what the reference computes on a CUDA device).
-_FUSED_ATTENTION = os.environ.get("CACHEBLEND_B200_ATTENTION", "").lower() == "fused"
+# (ascend.py:814-830); =flash: the einsum path's roundings with flash-order normalization
+# (one launch); default: the einsum path's roundings in its own order, which is what the
+# reference computes on a CUDA device.
+_ATTENTION_MODE = os.environ.get("CACHEBLEND_B200_ATTENTION", "").lower() or "reference"
+if _ATTENTION_MODE not in ("reference", "flash", "fused"):
+    raise ValueError(f"CACHEBLEND_B200_ATTENTION must be reference, flash or fused, not {_ATTENTION_MODE!r}")
 
 # CACHEBLEND_B200_FUSED_SELECT=1: K-deviation and selection of a one-rank check layer as one
 # launch (cb_kv_deviation_select) instead of two (measured slower on B200 so far: off by default)
@@ -335,7 +338,8 @@ class Qwen3BlendExecutor:
                 scratch = torch.empty(need, dtype=torch.uint8, device=query.device)
                 self._attention_scratch = scratch
             return blend_attention(query, key, value, positions, scale, workspace=scratch,
-                                   exact_rounding=not _FUSED_ATTENTION or scale <= 0)
+                                   exact_rounding="reference" if scale <= 0 and _ATTENTION_MODE == "fused"
+                                   else _ATTENTION_MODE)
         reuse = self.config.cache_attention_mask and state.important_indices is not None
         visible = state.attention_mask if reuse else None
         if visible is None:

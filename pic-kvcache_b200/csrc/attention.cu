@@ -9,9 +9,17 @@
 //   p   = softmax over k <= pos_q of w           (fp32; keys k > pos_q get 0)
 //   out = round_T(sum_k p * v)                   (fp32 accumulation)
 // The reference rounds the normalized probabilities to T before the second
-// product; here the unnormalized exp2 values are rounded to T and the sum is
-// divided at the end (flash-attention order), a difference within one T ulp
-// per probability.
+// product.  Three modes:
+//   kNormalized (exact_rounding = 1, the reference's order): two launches over
+//     the same tiles.  The first (kRowLse) computes S and each row's
+//     log2-sum-exp of w only; the second computes S again and rounds
+//     p = 2^(w log2e - lse2) -- the normalized probability -- to T before P V,
+//     with no rescaling and no final division.
+//   kFlash (exact_rounding = 2): one launch, the unnormalized exp2 values are
+//     rounded to T and O is divided by the row sum at the end (flash-attention
+//     order), within one T ulp per probability of the reference.
+//   kFused (exact_rounding = 0): fp32 logits times the scale, flash order, as
+//     the reference's fused NPU kernel computes them.
 //
 // Layout: rows = (query, group) pairs of one KV head, r = qi * groups + g, in
 // 128-row tiles (one 4-D TMA box over the query tensor: 64 dims x groups x 1
@@ -85,6 +93,7 @@ struct Params {
   float scale;
   const int32_t* row_pos;   // [rows_pad]: position of each row, -1 for padding
   const int32_t* pair_max;  // [q_pairs]: largest position among a pair's rows
+  float* lse;               // [num_kv_heads][rows_pad]: -(log2-sum-exp of w log2e) per row (kRowLse out, kNormalized in)
   char* out;
   int64_t out_token_stride;  // bytes
   int32_t* error;
@@ -160,11 +169,16 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
-// EXACT: the reference einsum path's roundings (T logits, T logit * scale);
-// otherwise fused semantics: fp32 logits times scale, as the reference's fused
-// attention kernel (npu_fused_infer_attention_score, ascend.py:814-830) and
-// flash attention compute them.
-template <typename T, bool EXACT>
+// Modes of attention_kernel.  All but kFused apply the reference einsum path's
+// roundings (T logits, T logit * scale); kFused computes fp32 logits times the
+// scale, as the reference's fused attention kernel (npu_fused_infer_attention_score,
+// ascend.py:814-830) and flash attention do.
+constexpr int kFused = 0;
+constexpr int kFlash = 1;       // online max / sum, P unnormalized, O divided at the end
+constexpr int kRowLse = 2;      // S only: each row's log2-sum-exp into Params::lse
+constexpr int kNormalized = 3;  // P = the normalized probabilities from Params::lse
+
+template <typename T, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap q_map,
                      const __grid_constant__ CUtensorMap k_map,
@@ -180,6 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* v_buf = k_buf + kKStages * kTileBytes;         // one V tile
   unsigned char* p_buf = v_buf + kTileBytes;                    // kPair P tiles
   const int items = c.num_kv_heads * c.q_pairs;
+  constexpr bool EXACT = MODE != kFused;
+  constexpr bool LSE_ONLY = MODE == kRowLse;  // no V, no P, no O
 
   if (threadIdx.x == 0) {
     mbar_init(&sh.q_full, 1);
@@ -256,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------ V loads
     // V(t) may land only after P V of tile t-1 has read the previous one;
     // it is needed after S(t+1), so its latency hides behind those products.
-    if (lane == 0) {
+    if (lane == 0 && !LSE_ONLY) {
       int t = 0;
       int v_armed = -1;
       bool ok = true;
@@ -317,14 +333,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!ok) break;
           umma_commit(&sh.k_empty[s]);
-          if (kt > 0 && !issue_pv(t - 1, kt == 1)) {
+          if (!LSE_ONLY && kt > 0 && !issue_pv(t - 1, kt == 1)) {
             ok = false;
             break;
           }
         }
         if (!ok) break;
         umma_commit(&sh.q_empty);  // every S of this item issued: Q may be replaced
-        if (!issue_pv(t - 1, kt_end == 0)) {
+        if (!LSE_ONLY && !issue_pv(t - 1, kt_end == 0)) {
           ok = false;
           break;
         }
@@ -354,6 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kt_end = max(c.pair_max[qp], 0) / kTile;
       float m_used = -INFINITY;  // log2-domain max the exponentials are taken against
       float l = 0.0f;
+      // kNormalized: -(log2-sum-exp) of the row, so p = 2^(w log2e + neg_lse) is normalized
+      const float neg_lse = MODE == kNormalized ? c.lse[static_cast<int64_t>(h) * c.rows_pad + r] : 0.0f;
       for (int kt = 0; kt <= kt_end; ++kt, ++t) {
         if (!wait_warp(&sh.s_full[x], t & 1)) { ok = false; break; }
         tc_fence_after();
@@ -385,43 +403,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (2 * j + 1 >= valid) w[j].y = -INFINITY;
           }
         }
-        float mx[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 64; ++j) mx[j & 3] = max3(mx[j & 3], w[j].x, w[j].y);
-        // log2-domain tile max: w times a positive multiplier (log2e, or scale * log2e
-        // when the scale is folded in), and rounding is monotonic, so max(w) * mul =
-        // max(w * mul)
+        // log2-domain multiplier: log2e, or scale * log2e when the scale is folded in
         const float mul = EXACT ? kLog2e : c.scale * kLog2e;
-        const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * mul;
-        const bool grow = tile_max > m_used + kRescaleLog2 || (m_used == -INFINITY && tile_max > -INFINITY);
-        // the P buffer is free and O settled once the previous tile's P V is done
-        if (kt > 0 && !wait_warp(&sh.pv_done[x], (t - 1) & 1)) { ok = false; break; }
-        if (__any_sync(0xffffffffu, grow)) {
-          const float m_new = grow ? tile_max : m_used;
-          const float corr = grow ? (m_used == -INFINITY ? 0.0f : ex2(m_used - m_new)) : 1.0f;
-          if (kt > 0) {  // O holds earlier tiles of this item: rescale its rows
-            tc_fence_after();
+        float2 nm;  // the exponent offset of this tile's p
+        if constexpr (MODE == kNormalized) {
+          nm = make_float2(neg_lse, neg_lse);
+        } else {
+          float mx[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t o[32];
-              tmem_ld32(o_tmem + q * 32, o);
-              tmem_wait_ld();
+          for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * corr);
-              tmem_st32(o_tmem + q * 32, o);
+          for (int j = 0; j < 64; ++j) mx[j & 3] = max3(mx[j & 3], w[j].x, w[j].y);
+          // w times a positive multiplier, and rounding is monotonic, so
+          // max(w) * mul = max(w * mul)
+          const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * mul;
+          const bool grow =
+              tile_max > m_used + kRescaleLog2 || (m_used == -INFINITY && tile_max > -INFINITY);
+          // the P buffer is free and O settled once the previous tile's P V is done
+          if (!LSE_ONLY && kt > 0 && !wait_warp(&sh.pv_done[x], (t - 1) & 1)) { ok = false; break; }
+          if (__any_sync(0xffffffffu, grow)) {
+            const float m_new = grow ? tile_max : m_used;
+            const float corr = grow ? (m_used == -INFINITY ? 0.0f : ex2(m_used - m_new)) : 1.0f;
+            if (!LSE_ONLY && kt > 0) {  // O holds earlier tiles of this item: rescale its rows
+              tc_fence_after();
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint32_t o[32];
+                tmem_ld32(o_tmem + q * 32, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * corr);
+                tmem_st32(o_tmem + q * 32, o);
+              }
+              tmem_wait_st();
             }
-            tmem_wait_st();
+            l *= corr;
+            m_used = m_new;
           }
-          l *= corr;
-          m_used = m_new;
+          // a padding row keeps m_used = -inf: its p are exact zeros
+          const float base_m = m_used == -INFINITY ? 0.0f : m_used;
+          nm = make_float2(-base_m, -base_m);
         }
-        // p = 2^(w mul - m_used) rounded to T into the SW128 P tile; the sum in fp32
-        // (a padding row keeps m_used = -inf: its p are exact zeros)
-        const float base_m = m_used == -INFINITY ? 0.0f : m_used;
+        if (MODE == kNormalized && kt > 0 && !wait_warp(&sh.pv_done[x], (t - 1) & 1)) { ok = false; break; }
+        // p = 2^(w mul + offset): rounded to T into the SW128 P tile (not in kRowLse);
+        // the sum in fp32 (not in kNormalized)
         const float2 l2e = make_float2(mul, mul);
-        const float2 nm = make_float2(-base_m, -base_m);
         float2 sm[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) sm[i] = make_float2(0.0f, 0.0f);
@@ -432,32 +458,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 4; ++e) {
             const float2 xe = __ffma2_rn(w[c16 * 4 + e], l2e, nm);
             const float2 pe = make_float2(ex2(xe.x), ex2(xe.y));
-            sm[e] = __fadd2_rn(sm[e], pe);
-            packed[e] = pack2<T>(pe.x, pe.y);
+            if constexpr (MODE != kNormalized) sm[e] = __fadd2_rn(sm[e], pe);
+            if constexpr (!LSE_ONLY) packed[e] = pack2<T>(pe.x, pe.y);
           }
-          const int half = c16 >> 3;
-          const int chunk = c16 & 7;
-          unsigned char* dst = my_p + half * kHalfBytes + row_in_tile * 128 +
-                               ((chunk ^ (row_in_tile & 7)) * 16);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          if constexpr (!LSE_ONLY) {
+            const int half = c16 >> 3;
+            const int chunk = c16 & 7;
+            unsigned char* dst = my_p + half * kHalfBytes + row_in_tile * 128 +
+                                 ((chunk ^ (row_in_tile & 7)) * 16);
+            *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          }
         }
-        const float2 s01 = __fadd2_rn(sm[0], sm[1]);
-        const float2 s23 = __fadd2_rn(sm[2], sm[3]);
-        const float2 st = __fadd2_rn(s01, s23);
-        l += st.x + st.y;
-        fence_async_smem();  // generic-proxy P writes -> the MMA's async-proxy reads
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.p_full[x]);
+        if constexpr (MODE != kNormalized) {
+          const float2 s01 = __fadd2_rn(sm[0], sm[1]);
+          const float2 s23 = __fadd2_rn(sm[2], sm[3]);
+          const float2 st = __fadd2_rn(s01, s23);
+          l += st.x + st.y;
+        }
+        if constexpr (!LSE_ONLY) {
+          fence_async_smem();  // generic-proxy P writes -> the MMA's async-proxy reads
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.p_full[x]);
+        }
       }
       if (!ok) break;
+      if constexpr (LSE_ONLY) {
+        // -(m + log2 l); a padding row (no key) stores 0 and is never read
+        c.lse[static_cast<int64_t>(h) * c.rows_pad + r] = l > 0.0f ? -(m_used + lg2(l)) : 0.0f;
+        continue;
+      }
       // O of this item complete once the last P V is done
       if (!wait_warp(&sh.pv_done[x], (t - 1) & 1)) { ok = false; break; }
       tc_fence_after();
       const int64_t qi = static_cast<int64_t>(r) / c.groups;
       const int g = r - static_cast<int>(qi) * c.groups;
       const bool store = qi < c.num_queries && pos >= 0;
-      const float inv = store && l > 0.0f ? 1.0f / l : 0.0f;
+      // kNormalized: P was normalized, O is the output; else divide by the row sum
+      const float inv = !store ? 0.0f : (MODE == kNormalized ? 1.0f : (l > 0.0f ? 1.0f / l : 0.0f));
       T* dst = reinterpret_cast<T*>(c.out + qi * c.out_token_stride) +
                static_cast<int64_t>(h * c.groups + g) * kHead;
 #pragma unroll
@@ -525,7 +563,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const int64_t* __restrict__ p
 
 // ---------------------------------------------------------------- host side
 struct Workspace {
-  size_t row_pos, pair_max, total;
+  size_t row_pos, pair_max, lse, total;
   int64_t rows_pad;
 };
 
@@ -540,6 +578,8 @@ Workspace layout(int64_t num_queries, int64_t num_keys, int64_t num_q_heads, int
   off = align_up(off + (size_t)w.rows_pad * 4, 256);
   w.pair_max = off;
   off = align_up(off + (size_t)(w.rows_pad / kPairRows) * 4, 256);
+  w.lse = off;  // the normalized mode's row log2-sum-exps
+  off = align_up(off + (size_t)num_kv_heads * w.rows_pad * 4, 256);
   w.total = off;
   return w;
 }
@@ -646,19 +686,42 @@ extern "C" int cb_blend_attention(const void* query, int64_t query_token_stride,
   c.scale = scale;
   c.row_pos = reinterpret_cast<const int32_t*>(ws + w.row_pos);
   c.pair_max = reinterpret_cast<const int32_t*>(ws + w.pair_max);
+  c.lse = reinterpret_cast<float*>(ws + w.lse);
   c.out = static_cast<char*>(out);
   c.out_token_stride = out_token_stride;
   c.error = device_error;
   const int grid = static_cast<int>(std::min<int64_t>(num_kv_heads * c.q_pairs, kSmCount));
+  CB_REQUIRE(exact_rounding >= 0 && exact_rounding <= 2, "exact_rounding must be 0, 1 or 2 (got %d)",
+             exact_rounding);
   CB_REQUIRE(exact_rounding || scale > 0.0f,
              "the fused-logit mode needs a positive scale (got %g)", static_cast<double>(scale));
-  auto kernel = dtype == CB_DTYPE_BF16
-                    ? (exact_rounding ? att::attention_kernel<__nv_bfloat16, true>
-                                      : att::attention_kernel<__nv_bfloat16, false>)
-                    : (exact_rounding ? att::attention_kernel<__half, true>
-                                      : att::attention_kernel<__half, false>);
-  rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), att::kDynSmem);
-  if (rc != CB_OK) return rc;
-  kernel<<<grid, att::kThreads, att::kDynSmem, s>>>(q_map, k_map, v_map, c);
-  return launch_status("cb_blend_attention");
+  const bool bf16 = dtype == CB_DTYPE_BF16;
+  // exact_rounding 1: the row log2-sum-exps, then the products with normalized P
+  const int modes[2] = {exact_rounding == 1 ? att::kRowLse : (exact_rounding == 2 ? att::kFlash : att::kFused),
+                        exact_rounding == 1 ? att::kNormalized : -1};
+  for (int mode : modes) {
+    if (mode < 0) break;
+    void (*kernel)(CUtensorMap, CUtensorMap, CUtensorMap, att::Params) = nullptr;
+    switch (mode) {
+      case att::kFused:
+        kernel = bf16 ? att::attention_kernel<__nv_bfloat16, att::kFused> : att::attention_kernel<__half, att::kFused>;
+        break;
+      case att::kFlash:
+        kernel = bf16 ? att::attention_kernel<__nv_bfloat16, att::kFlash> : att::attention_kernel<__half, att::kFlash>;
+        break;
+      case att::kRowLse:
+        kernel = bf16 ? att::attention_kernel<__nv_bfloat16, att::kRowLse> : att::attention_kernel<__half, att::kRowLse>;
+        break;
+      default:
+        kernel = bf16 ? att::attention_kernel<__nv_bfloat16, att::kNormalized>
+                      : att::attention_kernel<__half, att::kNormalized>;
+        break;
+    }
+    rc = ensure_dynamic_smem(reinterpret_cast<const void*>(kernel), att::kDynSmem);
+    if (rc != CB_OK) return rc;
+    kernel<<<grid, att::kThreads, att::kDynSmem, s>>>(q_map, k_map, v_map, c);
+    rc = launch_status("cb_blend_attention");
+    if (rc != CB_OK) return rc;
+  }
+  return CB_OK;
 }
