@@ -910,11 +910,19 @@ def sparse_q_bench(args, world: int, rank: int, local: int, steps: int, cpu: boo
     scale = 128 ** -0.5
     flops = float(sum(2 * 128 * cfg["q_heads"] * (int(p) + 1) for p in positions)) / world
 
+    # with TP the key masses are summed inside the select kernel over NVLink peer memory,
+    # as the executor does (CACHEBLEND_B200_PEER_SELECT=0: NCCL all-reduce, then select)
+    peer = None
+    if world > 1 and os.environ.get("CACHEBLEND_B200_PEER_SELECT", "1") != "0":
+        from cacheblend_b200.peer_exchange import PeerScoreExchange
+
+        peer = PeerScoreExchange(torch.distributed.group.WORLD, ctx, device)
+
     def step():
         mass = sparse_q_key_mass(query, key, rows, positions, scale, workspace=workspace, device_error=error)
-        if world > 1:
+        if world > 1 and peer is None:
             torch.distributed.all_reduce(mass)
-        return select_tokens(mass, gaps, 0.15, forced)
+        return select_tokens(mass, gaps, 0.15, forced, peer_exchange=peer)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -930,6 +938,9 @@ def sparse_q_bench(args, world: int, rank: int, local: int, steps: int, cpu: boo
         torch.cuda.synchronize(device)
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world, device) / steps
+    if peer is not None:
+        peer.check()
+        peer.close()
     peaks = measured_peaks()
     peak = peaks["bf16_tflops"]
     achieved = flops / (ms / 1e3) / 1e12
@@ -950,7 +961,9 @@ def sparse_q_bench(args, world: int, rank: int, local: int, steps: int, cpu: boo
         "config": {"workload": cfg["name"], "keys": ctx, "queries": int(positions.size),
                    "q_heads_per_rank": hq, "kv_heads_per_rank": hkv,
                    "l2": "K and the sparse queries re-streamed per tile pair; 201 MiB of K, larger than L2"},
-        "gpu_launches": 4 * steps, "launch": "eager: query prep, row pass, key pass, select per step",
+        "gpu_launches": 4 * steps, "launch": "eager: query prep, row pass, key pass, select per step"
+                                             + ("" if peer is None else " (the select sums the ranks' "
+                                                                         "key masses over NVLink)"),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peaks["source"],
                      "flops_note": "one causal QK^T counted once (two passes run); timed over the step "
