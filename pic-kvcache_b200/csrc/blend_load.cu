@@ -1076,12 +1076,16 @@ bool use_vector_path(uint64_t addr_acc, int esize, int head_size, int rotary_dim
 #define CB_LOAD_VARIANT 0
 #endif
 // CB_LOAD_CTAS > 0 overrides the bulk kernel's CTAs per SM, CB_FLAT_BLOCKS > 0
-// the flat kernel's 256-thread blocks per SM (tuning sweeps only).
+// the flat kernel's 256-thread blocks per SM, CB_TMA_LOAD_CTAS > 0 the tile
+// kernel's CTAs per SM (tuning sweeps only).
 #ifndef CB_LOAD_CTAS
 #define CB_LOAD_CTAS 0
 #endif
 #ifndef CB_FLAT_BLOCKS
 #define CB_FLAT_BLOCKS 0
+#endif
+#ifndef CB_TMA_LOAD_CTAS
+#define CB_TMA_LOAD_CTAS 0
 #endif
 
 template <typename T, bool NEOX, int S, int LAG>
@@ -1124,7 +1128,7 @@ int launch_tma_load(const LoadArgs& a, int32_t* error, cudaStream_t s) {
   int rows = tma::kTileBytes / (row_bytes + cs_bytes);
   if (rows > tma::kMaxRows) rows = tma::kMaxRows;
   const int64_t tiles = 2 * ((a.alloc_end + rows - 1) / rows);
-  const int64_t cap = static_cast<int64_t>(kSmCount) * 3;
+  const int64_t cap = static_cast<int64_t>(kSmCount) * (CB_TMA_LOAD_CTAS > 0 ? CB_TMA_LOAD_CTAS : 3);
   const int grid = static_cast<int>(tiles < cap ? tiles : cap);
   // Staging rows back to back (the loader's [2, alloc_end, H, D] staging) and
   // rows below 2 KiB: every tile leaves shared memory as one bulk store.  For
