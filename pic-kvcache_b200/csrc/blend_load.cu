@@ -1087,6 +1087,10 @@ bool use_vector_path(uint64_t addr_acc, int esize, int head_size, int rotary_dim
 #ifndef CB_TMA_LOAD_CTAS
 #define CB_TMA_LOAD_CTAS 0
 #endif
+// CB_FLAT_BELOW: row bytes under which the flat kernel loads (tuning sweeps only)
+#ifndef CB_FLAT_BELOW
+#define CB_FLAT_BELOW 1024
+#endif
 
 template <typename T, bool NEOX, int S, int LAG>
 int launch_bulk_variant(const LoadArgs& a, int tile_bytes, int ctas_per_sm, int row_bytes,
@@ -1153,7 +1157,7 @@ int dispatch_load(const LoadArgs& a, bool vec, bool neox, int64_t max_ctas, int3
   const int64_t cs_bytes = 2 * (int64_t)a.rope.rotary_dim * (int64_t)sizeof(T);
   const int64_t flat_items = a.alloc_end * (2 * row_bytes / 16);
   const bool flat_ok = flat_items < (int64_t(1) << 31);
-  if (vec && max_ctas <= 0 && flat_ok && (row_bytes < 1024 || CB_LOAD_VARIANT == 9)) {
+  if (vec && max_ctas <= 0 && flat_ok && (row_bytes < CB_FLAT_BELOW || CB_LOAD_VARIANT == 9)) {
     // device-memory sources, rows under 1 KiB: one thread per 16-byte item
     const int64_t blocks = (flat_items + 255) / 256;
     const int64_t cap = (int64_t)kSmCount * (CB_FLAT_BLOCKS > 0 ? CB_FLAT_BLOCKS : 8);
