@@ -56,7 +56,9 @@ class PeerScoreExchange:
         self.buffer_bytes = size.value
         own = ctypes.c_void_p(0)
         handle = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
-        index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        index = self.device.index
+        if index is None:
+            index = torch.cuda.current_device() if self.device.type == "cuda" else 0
         self._index = index
         _native.call("cb_peer_buffer_create", index, self.buffer_bytes, ctypes.addressof(own),
                      ctypes.addressof(handle))
@@ -118,6 +120,10 @@ class PeerScoreExchange:
         )
         return selected
 
+    def _sync(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
     def check(self) -> None:
         """Raise if a call's wait for another rank gave up (synchronises the device)."""
         code = int(self.device_error.item())
@@ -128,11 +134,11 @@ class PeerScoreExchange:
         """Zero the call counters of every rank (all ranks call this together)."""
         import torch.distributed as dist
 
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=self._group)
         _native.call("cb_peer_buffer_reset", self._own, self.world, self.max_tokens, 0)
         self.device_error.zero_()
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=self._group)
 
     def close(self) -> None:
@@ -142,7 +148,7 @@ class PeerScoreExchange:
         if self._closed:
             return
         self._closed = True
-        torch.cuda.synchronize(self.device)
+        self._sync()
         dist.barrier(group=self._group)
         for mapped in self._opened:
             _native.call("cb_peer_buffer_close", self._index, mapped)

@@ -91,3 +91,67 @@ def test_bench_reference_arm_under_torchrun():
     assert line["cpu_baseline"]["kind"] == "port" and line["e2e"]["h2d_bytes_per_step"] == 0
     # the same workload description as the GPU arm prints
     assert line["config"]["workload"] == "qwen3-0.6b-cpu-plumbing" and line["config"]["parallelism"] == "tp2"
+
+
+def _peer_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+    """PeerScoreExchange's host protocol over two gloo ranks with the C ABI faked:
+    IPC handles swapped through the group, the address table in rank order (own
+    buffer at this rank, the others' mappings elsewhere), the select's arguments,
+    and the teardown order (unmap every peer, then free the own buffer)."""
+    import ctypes
+
+    sys.path[:0] = [str(REPO), str(REPO / "pic-kvcache_b200")]
+    from cacheblend_b200 import peer_exchange
+
+    calls, seen = [], {}
+
+    def fake_call(name, *args):
+        calls.append(name)
+        if name == "cb_peer_select_buffer_size":
+            ctypes.c_int64.from_address(args[2]).value = 4096
+        elif name == "cb_peer_buffer_create":
+            ctypes.c_uint64.from_address(args[2]).value = 0x10000 * (rank + 1)
+            (ctypes.c_uint8 * 64).from_address(args[3])[0] = rank + 1  # the "handle" names its owner
+        elif name == "cb_peer_buffer_open":
+            owner = (ctypes.c_uint8 * 64).from_address(args[1])[0] - 1
+            ctypes.c_uint64.from_address(args[2]).value = 0x1000000 * (owner + 1) + 0x100 * (rank + 1)
+        elif name == "cb_select_topk_peer":
+            _, _, n, k, _, cap, table, r, w, max_tokens = args[:10]
+            seen.update(n=n, k=k, cap=cap, rank=r, world=w, max_tokens=max_tokens,
+                        table=list((ctypes.c_uint64 * w).from_address(table)))
+        elif name in ("cb_peer_buffer_close", "cb_peer_buffer_destroy"):
+            calls[-1] = f"{name}:{args[1]:#x}"
+
+    peer_exchange._native.call = fake_call
+    peer_exchange._native.require_cuda = lambda *tensors: None
+    peer_exchange._native.stream_handle = lambda stream=None: 0
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        exchange = peer_exchange.PeerScoreExchange(dist.group.WORLD, 1000, "cpu")
+        selected = exchange.select(torch.zeros(1000), torch.zeros(1000, dtype=torch.uint8), 150, 170)
+        exchange.close()
+        exchange.close()  # idempotent
+        (Path(out_dir) / f"peer{rank}.json").write_text(json.dumps(
+            {"calls": calls, "seen": seen, "selected": int(selected.numel())}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_host_protocol(tmp_path):
+    world = 2
+    mp.start_processes(_peer_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    for rank in range(world):
+        got = json.loads((tmp_path / f"peer{rank}.json").read_text())
+        other = 1 - rank
+        mapped = 0x1000000 * (other + 1) + 0x100 * (rank + 1)
+        table = [0, 0]
+        table[rank] = 0x10000 * (rank + 1)
+        table[other] = mapped
+        assert got["seen"] == {"n": 1000, "k": 150, "cap": 170, "rank": rank, "world": world,
+                               "max_tokens": 1000, "table": table}
+        assert got["selected"] == 170
+        assert got["calls"] == ["cb_peer_select_buffer_size", "cb_peer_buffer_create", "cb_peer_buffer_open",
+                                "cb_select_topk_peer", f"cb_peer_buffer_close:{mapped:#x}",
+                                f"cb_peer_buffer_destroy:{0x10000 * (rank + 1):#x}"]
