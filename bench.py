@@ -219,6 +219,18 @@ class Workload:
         return tables
 
 
+def open_peer_exchange(group, max_tokens: int, device):
+    """The TP group's peer-memory score exchange, or None (every rank alike) when a rank
+    cannot create or map its buffer: the NCCL all-reduce then sums the scores."""
+    from cacheblend_b200.peer_exchange import PeerExchangeUnavailable, PeerScoreExchange
+
+    try:
+        return PeerScoreExchange(group, max_tokens, device)
+    except PeerExchangeUnavailable as error:
+        print(f"peer score exchange unavailable, using the NCCL all-reduce: {error}", file=sys.stderr)
+        return None
+
+
 class DevicePath:
     """The hot path straight through the C ABI with device-resident inputs."""
 
@@ -259,9 +271,7 @@ class DevicePath:
         # (cb_select_topk_peer); CACHEBLEND_B200_PEER_SELECT=0 puts the NCCL all-reduce back
         self.peer = None
         if tp_group is not None and os.environ.get("CACHEBLEND_B200_PEER_SELECT", "1") != "0":
-            from cacheblend_b200.peer_exchange import PeerScoreExchange
-
-            self.peer = PeerScoreExchange(tp_group, wl.act, dev)
+            self.peer = open_peer_exchange(tp_group, wl.act, dev)
         self.fused_workspace = None
         if self.fused:
             size = ctypes.c_int64(0)
@@ -914,9 +924,7 @@ def sparse_q_bench(args, world: int, rank: int, local: int, steps: int, cpu: boo
     # as the executor does (CACHEBLEND_B200_PEER_SELECT=0: NCCL all-reduce, then select)
     peer = None
     if world > 1 and os.environ.get("CACHEBLEND_B200_PEER_SELECT", "1") != "0":
-        from cacheblend_b200.peer_exchange import PeerScoreExchange
-
-        peer = PeerScoreExchange(torch.distributed.group.WORLD, ctx, device)
+        peer = open_peer_exchange(torch.distributed.group.WORLD, ctx, device)
 
     def step():
         mass = sparse_q_key_mass(query, key, rows, positions, scale, workspace=workspace, device_error=error)

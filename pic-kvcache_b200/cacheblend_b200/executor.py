@@ -37,7 +37,7 @@ import torch
 from .attention import attention_supported, attention_workspace_bytes, blend_attention
 from .config import CacheBlendConfig
 from .rope import validate_rope_support
-from .peer_exchange import MAX_PEERS, MAX_TOKENS, PeerScoreExchange
+from .peer_exchange import MAX_PEERS, MAX_TOKENS, PeerExchangeUnavailable, PeerScoreExchange
 from .selection import (deviation_select, kv_deviation, select_tokens, selection_overlap,
                         sparse_q_scores, tp_world_size)
 from .trace import PipelineTracer
@@ -174,6 +174,7 @@ class Qwen3BlendExecutor:
         self.layers = layers
         self.tp_group = _tensor_parallel_group()
         self._peer: PeerScoreExchange | None = None  # made by the first TP selection
+        self._peer_unavailable = False
 
     def _peer_exchange(self, tokens: int, device: torch.device) -> PeerScoreExchange | None:
         """The TP group's peer-memory score exchange when this selection can use it.  Every
@@ -181,10 +182,14 @@ class Qwen3BlendExecutor:
         is created collectively by the first selection that needs it."""
         world = tp_world_size(self.tp_group)
         if not (_PEER_SELECT and self.config.tp_global_selection and 1 < world <= MAX_PEERS
-                and tokens <= MAX_TOKENS and device.type == "cuda"):
+                and tokens <= MAX_TOKENS and device.type == "cuda") or self._peer_unavailable:
             return None
         if self._peer is None:
-            self._peer = PeerScoreExchange(self.tp_group, MAX_TOKENS, device)
+            try:
+                self._peer = PeerScoreExchange(self.tp_group, MAX_TOKENS, device)
+            except PeerExchangeUnavailable:
+                self._peer_unavailable = True  # every rank: vLLM's all-reduce from now on
+                return None
         return self._peer
 
     # ------------------------------------------------------------------ request

@@ -31,6 +31,10 @@ MAX_TOKENS = 8 * 42 * 1024  # one 8-CTA cluster's shared memory holds the scores
 DEVICE_ERROR_PEER_WAIT = 5
 
 
+class PeerExchangeUnavailable(RuntimeError):
+    """Some rank could not create or map an exchange buffer (raised on every rank)."""
+
+
 def _group_rank_world(group) -> tuple[int, int, object]:
     """(rank, world, torch process group) of a torch group or a vLLM GroupCoordinator."""
     import torch.distributed as dist
@@ -54,32 +58,61 @@ class PeerScoreExchange:
         size = ctypes.c_int64(0)
         _native.call("cb_peer_select_buffer_size", self.world, self.max_tokens, ctypes.addressof(size))
         self.buffer_bytes = size.value
-        own = ctypes.c_void_p(0)
-        handle = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
         index = self.device.index
         if index is None:
             index = torch.cuda.current_device() if self.device.type == "cuda" else 0
         self._index = index
-        _native.call("cb_peer_buffer_create", index, self.buffer_bytes, ctypes.addressof(own),
-                     ctypes.addressof(handle))
-        self._own = own.value
+        self._own = 0
+        self._opened: list[int] = []
+        self._closed = True
+        # Every rank learns whether every other rank mapped everything, so that all
+        # of them either use the exchange or raise PeerExchangeUnavailable together.
+        failure = ""
+        handle = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
+        try:
+            own = ctypes.c_void_p(0)
+            _native.call("cb_peer_buffer_create", index, self.buffer_bytes, ctypes.addressof(own),
+                         ctypes.addressof(handle))
+            self._own = own.value
+        except (RuntimeError, ValueError) as error:
+            failure = f"rank {self.rank}: {error}"
         handles: list = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=self._group)
+        dist.all_gather_object(handles, None if failure else bytes(handle), group=self._group)
         addresses = [0] * self.world
         addresses[self.rank] = self._own
-        self._opened: list[int] = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                continue
-            raw = (ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(h)
-            mapped = ctypes.c_void_p(0)
-            _native.call("cb_peer_buffer_open", index, ctypes.addressof(raw), ctypes.addressof(mapped))
-            addresses[r] = mapped.value
-            self._opened.append(mapped.value)
+        if not failure and all(h is not None for h in handles):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    continue
+                raw = (ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(h)
+                mapped = ctypes.c_void_p(0)
+                try:
+                    _native.call("cb_peer_buffer_open", index, ctypes.addressof(raw), ctypes.addressof(mapped))
+                except (RuntimeError, ValueError) as error:
+                    failure = f"rank {self.rank} mapping rank {r}: {error}"
+                    break
+                addresses[r] = mapped.value
+                self._opened.append(mapped.value)
+        elif not failure:
+            failure = "another rank could not create its exchange buffer"
+        failures: list = [None] * self.world
+        dist.all_gather_object(failures, failure, group=self._group)
+        if any(failures):
+            opened, self._opened = self._opened, []
+            for mapped in opened:
+                _native.call("cb_peer_buffer_close", self._index, mapped)
+            dist.barrier(group=self._group)  # every mapping of this rank's buffer is gone
+            self._release()
+            raise PeerExchangeUnavailable("; ".join(f for f in failures if f))
         self._addresses = (ctypes.c_uint64 * self.world)(*addresses)
         self.device_error = torch.zeros(1, dtype=torch.int32, device=self.device)
-        dist.barrier(group=self._group)  # every rank mapped every buffer before the first call
         self._closed = False
+
+    def _release(self) -> None:
+        """Free this rank's buffer once no rank maps it any more."""
+        if self._own:
+            _native.call("cb_peer_buffer_destroy", self._index, self._own)
+            self._own = 0
 
     def select(
         self,
@@ -150,10 +183,11 @@ class PeerScoreExchange:
         self._closed = True
         self._sync()
         dist.barrier(group=self._group)
-        for mapped in self._opened:
+        opened, self._opened = self._opened, []
+        for mapped in opened:
             _native.call("cb_peer_buffer_close", self._index, mapped)
-        dist.barrier(group=self._group)
-        _native.call("cb_peer_buffer_destroy", self._index, self._own)
+        dist.barrier(group=self._group)  # every rank unmapped this rank's buffer
+        self._release()
 
 
 class AllRanksExchange:

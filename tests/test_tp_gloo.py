@@ -93,7 +93,7 @@ def test_bench_reference_arm_under_torchrun():
     assert line["config"]["workload"] == "qwen3-0.6b-cpu-plumbing" and line["config"]["parallelism"] == "tp2"
 
 
-def _peer_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+def _peer_rank_main(rank: int, world: int, port: int, out_dir: str, fail_open_rank: int = -1) -> None:
     """PeerScoreExchange's host protocol over two gloo ranks with the C ABI faked:
     IPC handles swapped through the group, the address table in rank order (own
     buffer at this rank, the others' mappings elsewhere), the select's arguments,
@@ -113,6 +113,8 @@ def _peer_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
             ctypes.c_uint64.from_address(args[2]).value = 0x10000 * (rank + 1)
             (ctypes.c_uint8 * 64).from_address(args[3])[0] = rank + 1  # the "handle" names its owner
         elif name == "cb_peer_buffer_open":
+            if rank == fail_open_rank:
+                raise RuntimeError("cb_peer_buffer_open: peer access unsupported")
             owner = (ctypes.c_uint8 * 64).from_address(args[1])[0] - 1
             ctypes.c_uint64.from_address(args[2]).value = 0x1000000 * (owner + 1) + 0x100 * (rank + 1)
         elif name == "cb_select_topk_peer":
@@ -128,7 +130,11 @@ def _peer_rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        exchange = peer_exchange.PeerScoreExchange(dist.group.WORLD, 1000, "cpu")
+        try:
+            exchange = peer_exchange.PeerScoreExchange(dist.group.WORLD, 1000, "cpu")
+        except peer_exchange.PeerExchangeUnavailable as error:
+            (Path(out_dir) / f"peer{rank}.json").write_text(json.dumps({"calls": calls, "error": str(error)}))
+            return
         selected = exchange.select(torch.zeros(1000), torch.zeros(1000, dtype=torch.uint8), 150, 170)
         exchange.close()
         exchange.close()  # idempotent
@@ -155,3 +161,21 @@ def test_peer_exchange_host_protocol(tmp_path):
         assert got["calls"] == ["cb_peer_select_buffer_size", "cb_peer_buffer_create", "cb_peer_buffer_open",
                                 "cb_select_topk_peer", f"cb_peer_buffer_close:{mapped:#x}",
                                 f"cb_peer_buffer_destroy:{0x10000 * (rank + 1):#x}"]
+
+
+def test_peer_exchange_setup_failure_is_collective(tmp_path):
+    """A rank that cannot map a peer's buffer: every rank raises PeerExchangeUnavailable
+    (callers then fall back to the NCCL all-reduce together), mappings are closed before
+    any owner frees its buffer, and nothing is left allocated."""
+    world = 2
+    mp.start_processes(_peer_rank_main, args=(world, _free_port(), str(tmp_path), 1), nprocs=world,
+                       start_method="spawn", join=True)
+    rank0 = json.loads((tmp_path / "peer0.json").read_text())
+    rank1 = json.loads((tmp_path / "peer1.json").read_text())
+    for got in (rank0, rank1):
+        assert "rank 1 mapping rank 0" in got["error"]
+    mapped = 0x1000000 * 2 + 0x100 * 1  # rank 0's mapping of rank 1's buffer
+    assert rank0["calls"] == ["cb_peer_select_buffer_size", "cb_peer_buffer_create", "cb_peer_buffer_open",
+                              f"cb_peer_buffer_close:{mapped:#x}", f"cb_peer_buffer_destroy:{0x10000:#x}"]
+    assert rank1["calls"] == ["cb_peer_select_buffer_size", "cb_peer_buffer_create", "cb_peer_buffer_open",
+                              f"cb_peer_buffer_destroy:{0x20000:#x}"]
