@@ -730,37 +730,21 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_peer_kernel(
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const int64_t parity = epoch & 1u;
-  // This CTA's slice of the partial scores into row `me` of every receive buffer.
-  // The slice is staged in shared memory (the keys area, free until the sums)
-  // and leaves as one bulk copy per rank: the TMA engine keeps the NVLink writes
-  // in flight, where the SM's own stores would be bound by their round trips.
-  // Bulk copies need 16-byte aligned addresses and sizes: slice and capacity are
-  // multiples of 4 and the buffers 256-byte aligned, so only the last CTA's
-  // ragged tail (under four scores) goes out as plain stores.
-  float* stage = reinterpret_cast<float*>(keys);
-  for (int i = tid; i < m; i += kSelThreads) stage[i] = __ldcg(partial + lo + i);
-  async::fence_async_smem();  // generic writes -> the bulk copies' async-proxy reads
-  __syncthreads();
-  const int m_bulk = m & ~3;
-  if (tid == 0 && m_bulk > 0) {
-    for (int r = 0; r < world; ++r) {
-      float* row = reinterpret_cast<float*>(peers.base[r]) + (parity * world + me) * peers.capacity + lo;
-      async::bulk_store(row, stage, static_cast<uint32_t>(m_bulk) * 4u);
-    }
-    async::bulk_commit();
-    async::bulk_wait<0>();  // the writes are performed, and the stage may be reused
-    asm volatile("fence.proxy.async.global;" ::: "memory");  // async-proxy writes before the fence below
-  }
-  if (tid < (m - m_bulk) * world) {
-    const int r = tid / (m - m_bulk);
-    const int i = m_bulk + tid % (m - m_bulk);
+  // this CTA's slice of the partial scores into row `me` of every receive buffer,
+  // in 16-byte stores where both sides are aligned (slice and capacity are
+  // multiples of 4 and the buffers 256-byte aligned, so that rests on `partial`)
+  for (int r = 0; r < world; ++r) {
     float* row = reinterpret_cast<float*>(peers.base[r]) + (parity * world + me) * peers.capacity + lo;
-    row[i] = stage[i];
+    const bool vec = ((reinterpret_cast<uintptr_t>(partial + lo) | reinterpret_cast<uintptr_t>(row)) & 15) == 0;
+    const int m4 = vec ? m >> 2 : 0;
+    const float4* src = reinterpret_cast<const float4*>(partial + lo);
+    for (int i = tid; i < m4; i += kSelThreads) reinterpret_cast<float4*>(row)[i] = src[i];
+    for (int i = 4 * m4 + tid; i < m; i += kSelThreads) row[i] = partial[lo + i];
   }
-  // Release: the block barrier orders every thread's stores (and thread 0's
-  // completed bulk copies) before warp 0's system-scope fence, and each flag
-  // bump follows that fence (one fence for all ranks' flags; a release on every
-  // bump would wait out the NVLink round trip of the bump before it).
+  // Release: the block barrier orders every thread's stores before warp 0's
+  // system-scope fence, and each flag bump follows that fence (one fence for
+  // all ranks' flags; a release on every bump would wait out the NVLink round
+  // trip of the bump before it).
   __syncthreads();
   if (tid < 32) {
     __threadfence_system();
