@@ -228,3 +228,50 @@ def test_select_tokens_routes_tp_reduction_through_the_peer_exchange():
     scores, base, k, capacity = exchange.args
     assert scores is partial and k == recompute_budget(100, 10, 10, 0.2) == 18 and capacity == 28
     assert out.numel() == 28
+
+
+def test_executor_peer_exchange_decision(monkeypatch):
+    """The executor's TP selection uses the peer exchange only with global selection,
+    2-8 ranks, CUDA scores and at most MAX_TOKENS tokens; it creates the exchange once,
+    and after a collective setup failure it stays on the all-reduce for good."""
+    from cacheblend_b200 import executor as ex
+    from cacheblend_b200.peer_exchange import MAX_TOKENS, PeerExchangeUnavailable
+
+    made = []
+
+    class FakeExchange:
+        def __init__(self, group, max_tokens, device):
+            made.append((group, max_tokens, device))
+
+    class Group:
+        def __init__(self, world):
+            self.world_size = world
+
+    def runner(world, global_selection=True):
+        obj = object.__new__(ex.Qwen3BlendExecutor)
+        obj.config = CacheBlendConfig(tp_global_selection=global_selection)
+        obj.tp_group = Group(world)
+        obj._peer = None
+        obj._peer_unavailable = False
+        return obj
+
+    cuda = torch.device("cuda", 0)
+    monkeypatch.setattr(ex, "PeerScoreExchange", FakeExchange)
+    one = runner(2)
+    first = one._peer_exchange(1000, cuda)
+    assert isinstance(first, FakeExchange) and one._peer_exchange(5000, cuda) is first
+    assert made == [(one.tp_group, MAX_TOKENS, cuda)]
+    assert runner(1)._peer_exchange(1000, cuda) is None                      # no TP
+    assert runner(16)._peer_exchange(1000, cuda) is None                     # more ranks than flags
+    assert runner(2, global_selection=False)._peer_exchange(1000, cuda) is None
+    assert runner(2)._peer_exchange(MAX_TOKENS + 1, cuda) is None            # too many tokens
+    assert runner(2)._peer_exchange(1000, torch.device("cpu")) is None
+
+    def unavailable(group, max_tokens, device):
+        raise PeerExchangeUnavailable("rank 1 mapping rank 0: peer access unsupported")
+
+    monkeypatch.setattr(ex, "PeerScoreExchange", unavailable)
+    two = runner(2)
+    assert two._peer_exchange(1000, cuda) is None and two._peer_unavailable
+    monkeypatch.setattr(ex, "PeerScoreExchange", FakeExchange)
+    assert two._peer_exchange(1000, cuda) is None  # no second attempt
