@@ -1584,6 +1584,7 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
         e2e = run_e2e(args, wl, device, world, group, span)
         wl.peer = None
     peer_on = path.peer is not None
+    protocol = path.peer.protocol if peer_on else None
     path.close()
     del path, wl
     torch.cuda.empty_cache()
@@ -1611,7 +1612,7 @@ def deviation_bench(args, shape: Shape, world: int, rank: int, local: int, group
                              "four rotating input sets, 512 MiB, so each reads its inputs from HBM)")),
         "roofline": roofline, "kernels": per_kernel, "e2e": e2e, "allreduce": allreduce,
         "score_reduction": None if world == 1 else (
-            "inside the select kernel: NVLink peer stores + bounded flag waits (cb_select_topk_peer)"
+            f"inside the select kernel over NVLink peer memory (cb_select_topk_peer, {protocol} protocol)"
             if peer_on else "NCCL all-reduce between two graphs"),
         "clocks": clocks.summary(), "cpu_baseline": cpu,
     }

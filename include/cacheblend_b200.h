@@ -264,9 +264,13 @@ CB_API int cb_select_topk(const float* scores, const uint8_t* base_mask, int64_t
  * the same sequence of calls with the same n, k and base mask, on streams that
  * run them in call order; n <= max_tokens <= 344,064.  `device`: the CUDA
  * device the buffer lives on (create) or is mapped into (open, close).
- * A wait that gives up stores 5 in *device_error (if not NULL): that call's
- * result is wrong, later calls are right again once the late rank catches up.
- * cb_peer_buffer_reset zeroes the call counters (all ranks, at a quiescent
+ * `protocol` 0: the partial scores as fp32 rows, one system fence, then a
+ * flag per (rank, cluster CTA); 1 (low latency): every score as a 64-bit word
+ * carrying the call number, polled by the reader, with no fence or flag.  All
+ * ranks must use the same protocol for a call.  A wait that gives up stores 5
+ * in *device_error (if not NULL): that call's result is wrong, later calls are
+ * right again once the late rank catches up.
+ * cb_peer_buffer_reset zeroes the whole buffer (all ranks, at a quiescent
  * point, e.g. after an error); close opened mappings before the owners
  * destroy their buffers.
  */
@@ -279,7 +283,7 @@ CB_API int cb_peer_buffer_destroy(int device, void* buffer);
 CB_API int cb_peer_buffer_reset(void* buffer, int world, int64_t max_tokens, void* stream);
 CB_API int cb_select_topk_peer(const float* partial, const uint8_t* base_mask, int64_t n, int64_t k,
                                int64_t* out_index, int64_t out_capacity, const uint64_t* buffers,
-                               int rank, int world, int64_t max_tokens, float* summed,
+                               int rank, int world, int64_t max_tokens, int protocol, float* summed,
                                int32_t* device_error, void* stream);
 /*
  * The same exchange with every rank played by one cooperative launch on one
@@ -290,7 +294,8 @@ CB_API int cb_select_topk_peer(const float* partial, const uint8_t* base_mask, i
 CB_API int cb_select_topk_peer_all_ranks(const float* partial, const uint8_t* base_mask, int64_t n,
                                          int64_t k, int64_t* out_index, int64_t out_capacity,
                                          const uint64_t* buffers, int world, int64_t max_tokens,
-                                         float* summed, int32_t* device_error, void* stream);
+                                         int protocol, float* summed, int32_t* device_error,
+                                         void* stream);
 
 /*
  * Bytes of the workspace cb_kv_deviation_select needs (a 2048-bin histogram

@@ -21,7 +21,7 @@ LIB_PATH = Path(
     os.environ.get("CACHEBLEND_B200_LIB")
     or Path(__file__).resolve().parent / "_lib" / "libcacheblend_b200.so"
 )
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 CB_OK = 0
 CB_ERR_INVALID = -1
@@ -107,9 +107,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "cb_peer_buffer_close": (_i32, [_i32, _ptr]),
     "cb_peer_buffer_destroy": (_i32, [_i32, _ptr]),
     "cb_peer_buffer_reset": (_i32, [_ptr, _i32, _i64, _ptr]),
-    "cb_select_topk_peer": (_i32, [_ptr, _ptr, _i64, _i64, _ptr, _i64, _ptr, _i32, _i32, _i64, _ptr, _ptr, _ptr]),
+    "cb_select_topk_peer": (
+        _i32, [_ptr, _ptr, _i64, _i64, _ptr, _i64, _ptr, _i32, _i32, _i64, _i32, _ptr, _ptr, _ptr]),
     "cb_select_topk_peer_all_ranks": (
-        _i32, [_ptr, _ptr, _i64, _i64, _ptr, _i64, _ptr, _i32, _i64, _ptr, _ptr, _ptr]),
+        _i32, [_ptr, _ptr, _i64, _i64, _ptr, _i64, _ptr, _i32, _i64, _i32, _ptr, _ptr, _ptr]),
     "cb_kv_deviation_select_workspace_size": (_i32, [_ptr]),
     "cb_kv_deviation_select": (
         _i32,

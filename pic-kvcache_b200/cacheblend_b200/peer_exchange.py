@@ -27,12 +27,25 @@ from . import _native
 
 IPC_HANDLE_BYTES = 64
 MAX_PEERS = 8
+# exchange protocols of cb_select_topk_peer: fp32 rows + one fence + flags, or
+# 64-bit (call number, score) words polled by the reader
+PROTOCOLS = {"flags": 0, "low_latency": 1}
 MAX_TOKENS = 8 * 42 * 1024  # one 8-CTA cluster's shared memory holds the scores' order keys
 DEVICE_ERROR_PEER_WAIT = 5
 
 
 class PeerExchangeUnavailable(RuntimeError):
     """Some rank could not create or map an exchange buffer (raised on every rank)."""
+
+
+def default_protocol() -> str:
+    """CACHEBLEND_B200_PEER_PROTOCOL (flags | low_latency), flags by default."""
+    import os
+
+    name = os.environ.get("CACHEBLEND_B200_PEER_PROTOCOL", "flags")
+    if name not in PROTOCOLS:
+        raise ValueError(f"CACHEBLEND_B200_PEER_PROTOCOL must be one of {sorted(PROTOCOLS)}, not {name!r}")
+    return name
 
 
 def _group_rank_world(group) -> tuple[int, int, object]:
@@ -47,9 +60,13 @@ def _group_rank_world(group) -> tuple[int, int, object]:
 class PeerScoreExchange:
     """Exchange buffers of one TP group for selections over at most ``max_tokens`` tokens."""
 
-    def __init__(self, group, max_tokens: int, device: torch.device | int | str):
+    def __init__(self, group, max_tokens: int, device: torch.device | int | str,
+                 protocol: str | None = None):
         import torch.distributed as dist
 
+        self.protocol = default_protocol() if protocol is None else protocol
+        if self.protocol not in PROTOCOLS:
+            raise ValueError(f"protocol must be one of {sorted(PROTOCOLS)}, not {self.protocol!r}")
         self.device = torch.device(device)
         self.rank, self.world, self._group = _group_rank_world(group)
         if not 1 <= self.world <= MAX_PEERS:
@@ -148,7 +165,7 @@ class PeerScoreExchange:
         _native.call(
             "cb_select_topk_peer", partial.data_ptr(), base_mask_device.data_ptr(), n, k, selected.data_ptr(),
             capacity, ctypes.addressof(self._addresses), self.rank, self.world, self.max_tokens,
-            0 if summed is None else summed.data_ptr(), self.device_error.data_ptr(),
+            PROTOCOLS[self.protocol], 0 if summed is None else summed.data_ptr(), self.device_error.data_ptr(),
             _native.stream_handle(stream),
         )
         return selected
@@ -195,7 +212,11 @@ class AllRanksExchange:
     (``cb_select_topk_peer_all_ranks``; cluster r is rank r, every buffer local):
     the single-GPU check of the protocol, call after call."""
 
-    def __init__(self, world: int, max_tokens: int, device: torch.device | int | str):
+    def __init__(self, world: int, max_tokens: int, device: torch.device | int | str,
+                 protocol: str = "flags"):
+        if protocol not in PROTOCOLS:
+            raise ValueError(f"protocol must be one of {sorted(PROTOCOLS)}, not {protocol!r}")
+        self.protocol = protocol
         self.world = int(world)
         self.max_tokens = int(max_tokens)
         self.device = torch.device(device)
@@ -220,6 +241,6 @@ class AllRanksExchange:
         _native.call(
             "cb_select_topk_peer_all_ranks", partials.data_ptr(), base_mask_device.data_ptr(), n, k,
             selected.data_ptr(), capacity, ctypes.addressof(self._addresses), world, self.max_tokens,
-            summed.data_ptr(), self.device_error.data_ptr(), 0,
+            PROTOCOLS[self.protocol], summed.data_ptr(), self.device_error.data_ptr(), 0,
         )
         return selected, summed

@@ -128,7 +128,7 @@ int launch_status(const char* kernel) {
 
 }  // namespace cb
 
-extern "C" int cb_abi_version(void) { return 5; }
+extern "C" int cb_abi_version(void) { return 6; }
 
 extern "C" const char* cb_last_error(void) { return cb::g_last_error; }
 

@@ -685,17 +685,32 @@ __device__ __forceinline__ void add_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// 64-bit scalar accesses are single-copy atomic: a word carries a score and
+// the call number that wrote it, and a reader that sees the call number sees
+// the score stored with it.
+__device__ __forceinline__ void store_relaxed_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t load_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 struct PeerArgs {
   uint64_t base[kMaxPeers];  // each rank's exchange buffer as mapped in this process
   int rank;
   int world;
   int emulated;
-  int64_t capacity;          // fp32 entries per receive row (a multiple of 4)
+  int low_latency;           // 1: 64-bit (score, call) words, no fence or flags
+  int64_t capacity;          // entries per receive row (a multiple of 4)
   int64_t flags_offset;      // bytes from a buffer's start to its flags
 };
 
+// The receive rows take 8 bytes per entry (the low-latency words; the flag
+// protocol uses the first half of each parity's area as fp32 rows).
 __host__ __device__ inline int64_t peer_flags_offset(int world, int64_t capacity) {
-  return (int64_t)2 * world * capacity * 4;
+  return (int64_t)2 * world * capacity * 8;
 }
 
 __device__ __forceinline__ uint32_t* peer_flags(const PeerArgs& p, int r) {
@@ -730,6 +745,43 @@ __global__ void __launch_bounds__(kSelThreads, 1) select_peer_kernel(
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const int64_t parity = epoch & 1u;
+  if (peers.low_latency) {
+    // Low-latency protocol: each score crosses NVLink once, as a 64-bit word
+    // (call number << 32 | score bits) in row `me` of every rank's receive
+    // area; the reader polls the words themselves until they carry this call's
+    // number.  No fence and no flag round trip, at twice the bytes.
+    for (int i = tid; i < m; i += kSelThreads) {
+      const uint64_t word = (static_cast<uint64_t>(epoch) << 32) | __float_as_uint(__ldcg(partial + lo + i));
+      for (int r = 0; r < world; ++r)
+        store_relaxed_sys(reinterpret_cast<uint64_t*>(peers.base[r]) + (parity * world + me) * peers.capacity + lo + i,
+                          word);
+    }
+    const uint64_t* words = reinterpret_cast<const uint64_t*>(peers.base[me]) + parity * world * peers.capacity + lo;
+    bool gave_up = false;
+    const uint64_t start = async::global_ns();
+    for (int i = tid; i < m; i += kSelThreads) {
+      float v = 0.0f;
+      for (int r = 0; r < world; ++r) {
+        uint64_t w = load_relaxed_sys(words + r * peers.capacity + i);
+        for (uint32_t spin = 1; static_cast<uint32_t>(w >> 32) != epoch && !gave_up; ++spin) {
+          if ((spin & 63u) == 0 && async::global_ns() - start > async::kTimeoutNs) {
+            gave_up = true;  // the rest of this thread's words are taken as they are
+            break;
+          }
+          w = load_relaxed_sys(words + r * peers.capacity + i);
+        }
+        const float x = __uint_as_float(static_cast<uint32_t>(w));
+        v = r == 0 ? x : v + x;  // rank order, as the flag protocol sums
+      }
+      if (summed != nullptr) summed[lo + i] = v;
+      keys[i] = order_key(v);
+      flags_smem[i] = base[lo + i] != 0;
+    }
+    if (gave_up && error != nullptr) atomicCAS(error, 0, kPeerError);
+    if (tid == 0) my_count[crank] = epoch;
+    cluster_select<FullPasses>(cluster, nullptr, base, n, k, out, cap, slice, dyn, 0u, 0u, k, true);
+    return;
+  }
   // this CTA's slice of the partial scores into row `me` of every receive buffer,
   // in 16-byte stores where both sides are aligned (slice and capacity are
   // multiples of 4 and the buffers 256-byte aligned, so that rests on `partial`)
@@ -1167,9 +1219,10 @@ extern "C" int cb_peer_buffer_reset(void* buffer, int world, int64_t max_tokens,
   CB_REQUIRE(buffer != nullptr, "null buffer");
   CB_REQUIRE(world >= 1 && world <= kMaxPeers && max_tokens >= 0, "bad world / max_tokens");
   CB_BIND(stream, buffer);
-  const int64_t off = peer_flags_offset(world, peer_row_capacity(max_tokens));
-  const cudaError_t e = cudaMemsetAsync(static_cast<char*>(buffer) + off, 0,
-                                        (size_t)(kMaxPeers + 1) * kClusterCtas * 4,
+  // the whole buffer: the counters restart at call 1, so no word of an earlier
+  // call 1 or 2 may remain in the receive area
+  const int64_t bytes = peer_buffer_bytes(world, peer_row_capacity(max_tokens));
+  const cudaError_t e = cudaMemsetAsync(buffer, 0, static_cast<size_t>(bytes),
                                         reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     set_error("cb_peer_buffer_reset: %s", cudaGetErrorString(e));
@@ -1181,9 +1234,10 @@ extern "C" int cb_peer_buffer_reset(void* buffer, int world, int64_t max_tokens,
 namespace {
 int launch_select_peer(const float* partial, const uint8_t* base_mask, int64_t n, int64_t k,
                        int64_t* out_index, int64_t out_capacity, const uint64_t* buffers, int rank,
-                       int world, int emulated, int64_t max_tokens, float* summed, int32_t* device_error,
-                       void* stream, const char* name) {
+                       int world, int emulated, int64_t max_tokens, int protocol, float* summed,
+                       int32_t* device_error, void* stream, const char* name) {
   clear_error();
+  CB_REQUIRE(protocol == 0 || protocol == 1, "protocol %d is neither 0 (flags) nor 1 (low latency)", protocol);
   CB_REQUIRE(world >= 1 && world <= kMaxPeers, "world size %d outside [1, %d]", world, kMaxPeers);
   CB_REQUIRE(emulated || (rank >= 0 && rank < world), "rank %d outside [0, %d)", rank, world);
   CB_REQUIRE(buffers != nullptr && buffers[emulated ? 0 : rank] != 0, "null buffer table or own buffer");
@@ -1202,6 +1256,7 @@ int launch_select_peer(const float* partial, const uint8_t* base_mask, int64_t n
   args.rank = emulated ? 0 : rank;
   args.world = world;
   args.emulated = emulated;
+  args.low_latency = protocol;
   args.capacity = peer_row_capacity(max_tokens);
   args.flags_offset = peer_flags_offset(world, args.capacity);
   // every call exchanges, also with n == 0: the ranks' call counts stay in step
@@ -1235,16 +1290,18 @@ int launch_select_peer(const float* partial, const uint8_t* base_mask, int64_t n
 
 extern "C" int cb_select_topk_peer(const float* partial, const uint8_t* base_mask, int64_t n, int64_t k,
                                    int64_t* out_index, int64_t out_capacity, const uint64_t* buffers,
-                                   int rank, int world, int64_t max_tokens, float* summed,
+                                   int rank, int world, int64_t max_tokens, int protocol, float* summed,
                                    int32_t* device_error, void* stream) {
   return launch_select_peer(partial, base_mask, n, k, out_index, out_capacity, buffers, rank, world, 0,
-                            max_tokens, summed, device_error, stream, "cb_select_topk_peer");
+                            max_tokens, protocol, summed, device_error, stream, "cb_select_topk_peer");
 }
 
 extern "C" int cb_select_topk_peer_all_ranks(const float* partial, const uint8_t* base_mask, int64_t n,
                                              int64_t k, int64_t* out_index, int64_t out_capacity,
                                              const uint64_t* buffers, int world, int64_t max_tokens,
-                                             float* summed, int32_t* device_error, void* stream) {
+                                             int protocol, float* summed, int32_t* device_error,
+                                             void* stream) {
   return launch_select_peer(partial, base_mask, n, k, out_index, out_capacity, buffers, 0, world, 1,
-                            max_tokens, summed, device_error, stream, "cb_select_topk_peer_all_ranks");
+                            max_tokens, protocol, summed, device_error, stream,
+                            "cb_select_topk_peer_all_ranks");
 }

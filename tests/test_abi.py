@@ -53,7 +53,8 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
 
 
 def test_peer_exchange_buffer_layout_without_a_gpu():
-    """cb_peer_select_buffer_size: receive rows [2][world][max_tokens rounded up to 4] fp32,
+    """cb_peer_select_buffer_size: receive rows [2][world][max_tokens rounded up to 4] of 8-byte
+    entries (the low-latency words; the flag protocol's fp32 rows use half),
     then flags [8 ranks][8 cluster CTAs] and call counters [8] u32; world 1-8, at most one
     cluster's 344,064 scores.  Pure arithmetic: no CUDA call."""
     lib = _native.load_library()
@@ -61,12 +62,12 @@ def test_peer_exchange_buffer_layout_without_a_gpu():
     for world, tokens in ((1, 0), (2, 1), (2, 32768), (8, 32769), (8, 8 * 42 * 1024)):
         assert lib.cb_peer_select_buffer_size(world, tokens, ctypes.byref(size)) == _native.CB_OK
         capacity = (tokens + 3) // 4 * 4
-        assert size.value == 2 * world * capacity * 4 + 9 * 8 * 4
+        assert size.value == 2 * world * capacity * 8 + 9 * 8 * 4
     for world, tokens in ((0, 10), (9, 10), (2, -1), (2, 8 * 42 * 1024 + 1)):
         assert lib.cb_peer_select_buffer_size(world, tokens, ctypes.byref(size)) == _native.CB_ERR_INVALID
     assert lib.cb_peer_select_buffer_size(2, 10, None) == _native.CB_ERR_INVALID
     # a null buffer table is rejected before any device work
-    assert lib.cb_select_topk_peer(None, None, 0, 0, None, 0, None, 0, 2, 0, None, None, None) == \
+    assert lib.cb_select_topk_peer(None, None, 0, 0, None, 0, None, 0, 2, 0, 0, None, None, None) == \
         _native.CB_ERR_INVALID
-    assert lib.cb_select_topk_peer(None, None, 0, 0, None, 0, None, 2, 2, 0, None, None, None) == \
+    assert lib.cb_select_topk_peer(None, None, 0, 0, None, 0, None, 2, 2, 0, 0, None, None, None) == \
         _native.CB_ERR_INVALID  # rank outside the world

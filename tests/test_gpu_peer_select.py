@@ -57,19 +57,24 @@ def _check(exchange, partials: np.ndarray, gaps: np.ndarray, ratio: float, devic
         assert np.array_equal(got[r], want), r
 
 
+PROTOCOLS = ["flags", "low_latency"]
+
+
+@pytest.mark.parametrize("protocol", PROTOCOLS)
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
-def test_all_ranks_match_oracle_call_after_call(cuda, world):
+def test_all_ranks_match_oracle_call_after_call(cuda, world, protocol):
     n = 32768
-    exchange = AllRanksExchange(world, n, cuda)
+    exchange = AllRanksExchange(world, n, cuda, protocol)
     for call in range(5):  # both receive buffers twice, counters 1..5
         partials = _partials(world, n, 100 * world + call)
         gaps = np.random.default_rng(call).random(n) < 0.1
         _check(exchange, partials, gaps, 0.15, cuda)
 
 
+@pytest.mark.parametrize("protocol", PROTOCOLS)
 @pytest.mark.parametrize("n", [1, 5, 7, 1001, 40_003])
-def test_all_ranks_ragged_sizes(cuda, n):
-    exchange = AllRanksExchange(4, 40_003, cuda)
+def test_all_ranks_ragged_sizes(cuda, n, protocol):
+    exchange = AllRanksExchange(4, 40_003, cuda, protocol)
     for call in range(2):
         partials = _partials(4, n, n + call)
         gaps = np.zeros(n, dtype=bool)
@@ -77,9 +82,10 @@ def test_all_ranks_ragged_sizes(cuda, n):
         _check(exchange, partials, gaps, 0.2, cuda)
 
 
-def test_all_ranks_nan_ties_and_edge_masks(cuda):
+@pytest.mark.parametrize("protocol", PROTOCOLS)
+def test_all_ranks_nan_ties_and_edge_masks(cuda, protocol):
     n, world = 20_000, 4
-    exchange = AllRanksExchange(world, n, cuda)
+    exchange = AllRanksExchange(world, n, cuda, protocol)
     partials = np.ones((world, n), dtype=np.float32)
     partials[:, ::5] = 2.0          # exact ties at the threshold
     partials[1, [7, 300, 19_999]] = np.nan  # out-of-range cached rows on one rank rank first
@@ -110,16 +116,19 @@ def test_abi_rejects_bad_arguments(cuda):
     out = torch.empty(100, dtype=torch.long, device=cuda)
     buffers = (ctypes.c_uint64 * 2)(0, 0)  # null exchange buffers
     rc = lib.cb_select_topk_peer(ctypes.c_void_p(scores.data_ptr()), ctypes.c_void_p(base.data_ptr()), 100, 5,
-                                 ctypes.c_void_p(out.data_ptr()), 100, buffers, 0, 2, 100, None, None, None)
+                                 ctypes.c_void_p(out.data_ptr()), 100, buffers, 0, 2, 100, 0, None, None, None)
     assert rc == _native.CB_ERR_INVALID
     real = [torch.zeros(size.value, dtype=torch.uint8, device=cuda) for _ in range(2)]
     buffers = (ctypes.c_uint64 * 2)(*[b.data_ptr() for b in real])
     rc = lib.cb_select_topk_peer(ctypes.c_void_p(scores.data_ptr()), ctypes.c_void_p(base.data_ptr()), 200, 5,
-                                 ctypes.c_void_p(out.data_ptr()), 100, buffers, 0, 2, 100, None, None, None)
+                                 ctypes.c_void_p(out.data_ptr()), 100, buffers, 0, 2, 100, 0, None, None, None)
     assert rc == _native.CB_ERR_INVALID  # more tokens than the exchange was sized for
     rc = lib.cb_select_topk_peer(ctypes.c_void_p(scores.data_ptr()), ctypes.c_void_p(base.data_ptr()), 100, 5,
-                                 ctypes.c_void_p(out.data_ptr()), 100, buffers, 2, 2, 100, None, None, None)
+                                 ctypes.c_void_p(out.data_ptr()), 100, buffers, 2, 2, 100, 0, None, None, None)
     assert rc == _native.CB_ERR_INVALID  # rank outside the world
+    rc = lib.cb_select_topk_peer(ctypes.c_void_p(scores.data_ptr()), ctypes.c_void_p(base.data_ptr()), 100, 5,
+                                 ctypes.c_void_p(out.data_ptr()), 100, buffers, 0, 2, 100, 2, None, None, None)
+    assert rc == _native.CB_ERR_INVALID  # no such protocol
 
 
 # ---- real ranks: one process per GPU ------------------------------------------
@@ -130,7 +139,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
+def _rank_main(rank: int, world: int, port: int, out_dir: str, protocol: str = "flags") -> None:
     import torch.distributed as dist
 
     from cacheblend_b200.peer_exchange import PeerScoreExchange
@@ -142,7 +151,7 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     device = torch.device("cuda", rank)
     torch.cuda.set_device(device)
     n = 32768
-    exchange = PeerScoreExchange(dist.group.WORLD, n, device)
+    exchange = PeerScoreExchange(dist.group.WORLD, n, device, protocol)
     results = {}
     try:
         gaps = np.random.default_rng(7).random(n) < 0.1
@@ -178,12 +187,13 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two or more GPUs")
-def test_processes_exchange_over_nvlink(tmp_path):
+@pytest.mark.parametrize("protocol", PROTOCOLS)
+def test_processes_exchange_over_nvlink(tmp_path, protocol):
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 8)
     world = 1 << (world.bit_length() - 1)  # 2, 4 or 8
-    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path), protocol), nprocs=world,
                        start_method="spawn")
     got = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     n = 32768
