@@ -275,3 +275,18 @@ def test_executor_peer_exchange_decision(monkeypatch):
     assert two._peer_exchange(1000, cuda) is None and two._peer_unavailable
     monkeypatch.setattr(ex, "PeerScoreExchange", FakeExchange)
     assert two._peer_exchange(1000, cuda) is None  # no second attempt
+
+
+def test_attention_modes_and_no_cpu_fallback():
+    """blend_attention's exact_rounding maps onto the ABI's mode codes (reference order 1,
+    flash order 2, fp32 logits 0), rejects other values, and refuses CPU tensors."""
+    from cacheblend_b200.attention import _MODES, blend_attention
+
+    assert _MODES[True] == _MODES["reference"] == 1
+    assert _MODES["flash"] == 2
+    assert _MODES[False] == _MODES["fused"] == 0
+    q = torch.zeros(4, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        blend_attention(q, q, q, torch.arange(4), 1.0, exact_rounding="exact")
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        blend_attention(q, q, q, torch.arange(4), 1.0)
