@@ -118,8 +118,8 @@ def _peer_rank_main(rank: int, world: int, port: int, out_dir: str, fail_open_ra
             owner = (ctypes.c_uint8 * 64).from_address(args[1])[0] - 1
             ctypes.c_uint64.from_address(args[2]).value = 0x1000000 * (owner + 1) + 0x100 * (rank + 1)
         elif name == "cb_select_topk_peer":
-            _, _, n, k, _, cap, table, r, w, max_tokens = args[:10]
-            seen.update(n=n, k=k, cap=cap, rank=r, world=w, max_tokens=max_tokens,
+            _, _, n, k, _, cap, table, r, w, max_tokens, protocol = args[:11]
+            seen.update(n=n, k=k, cap=cap, rank=r, world=w, max_tokens=max_tokens, protocol=protocol,
                         table=list((ctypes.c_uint64 * w).from_address(table)))
         elif name in ("cb_peer_buffer_close", "cb_peer_buffer_destroy"):
             calls[-1] = f"{name}:{args[1]:#x}"
@@ -156,7 +156,7 @@ def test_peer_exchange_host_protocol(tmp_path):
         table[rank] = 0x10000 * (rank + 1)
         table[other] = mapped
         assert got["seen"] == {"n": 1000, "k": 150, "cap": 170, "rank": rank, "world": world,
-                               "max_tokens": 1000, "table": table}
+                               "max_tokens": 1000, "protocol": 0, "table": table}
         assert got["selected"] == 170
         assert got["calls"] == ["cb_peer_select_buffer_size", "cb_peer_buffer_create", "cb_peer_buffer_open",
                                 "cb_select_topk_peer", f"cb_peer_buffer_close:{mapped:#x}",
